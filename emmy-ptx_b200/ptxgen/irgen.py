@@ -1,0 +1,668 @@
+"""Kernel IR generator: the problem families of the open set at any shape.
+
+Emmy's tracer (``tools/generate.py:57-71``) is not available, so this module
+writes Kernel IR directly, in the repr grammar ``ptxgen.ir`` parses.  For each
+family it follows the schedule of the shipped problem of that family and only
+re-derives the shape-dependent literals:
+
+* ``pointwise``   -- p00..p03 (``Tile[a0]``, ``U`` elements per cell, grouped
+                     vector write);
+* ``reduce_full`` -- r01..r03 (one CTA of ``T`` threads strides the array;
+                     optional mean epilogue);
+* ``reduce_rows`` -- r04 (one row per CTA);
+* ``rmsnorm``, ``softmax``, ``l2norm`` -- f01..f03 (reduce, then a second
+                     strided pass over the row);
+* ``matmul``      -- m01 (32x64x64 tiles, 3-stage ``cp.async`` ring,
+                     512 threads, 2x2 outputs per thread);
+* ``matmul_splitk`` -- m02 (16x32x8 tiles, K split into slices reduced with
+                     atomic writes into a zeroed C);
+* ``attention``   -- a02 (one output element per thread, online softmax)
+                     and its ``[B, H, S, D]`` generalisation with K given
+                     untransposed.
+
+At the shipped shapes the generated bodies equal the shipped ones byte for
+byte (``tests/test_irgen.py``); that pins the generator to the reference's
+schedule.  Every generator returns ``(graph_json, meta_json)``.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+
+from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCopy,
+                 CpAsyncWait, Dim, ElementwiseImpl, Init, Let, Literal, Load, Loop, Smem,
+                 StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var, WarpShuffle, Window,
+                 Write, datatype)
+
+F32 = datatype("f32")
+
+
+def L(v: int) -> Literal:
+    return Literal(value=int(v), dtype="int")
+
+
+def Lf(v: float) -> Literal:
+    return Literal(value=float(v), dtype="float")
+
+
+def V(n: str) -> Var:
+    return Var(name=n)
+
+
+def _b(op):
+    return lambda a, b: BinaryExpr(op=op, left=a, right=b)
+
+
+ADD, SUB, MUL, DIV, MOD, LT, EQ = (_b(o) for o in ("+", "-", "*", "/", "%", "<", "=="))
+
+
+def EW(name: str) -> ElementwiseImpl:
+    return ElementwiseImpl(name)
+
+
+def ax(name: str, extent: int, window=None) -> Axis:
+    return Axis(name=name, extent=Dim(extent), window=window)
+
+
+def win(parent: str, extent: int) -> Window:
+    return Window(parent=ax(parent, extent), base=None, bound=None, partition=False)
+
+
+def tile(axes, body, block_threads=None, raster_axes=None, raster_group=None) -> Tile:
+    return Tile(axes=tuple(axes), body=tuple(body), block_threads=block_threads, aux_threads=0,
+                raster_axes=raster_axes, raster_group=raster_group, raster_orient="m")
+
+
+def load(names, buf, index, dtype=F32) -> Load:
+    if isinstance(names, str):
+        names = (names,)
+    return Load(names=tuple(names), input=buf, index=tuple(index), dtype=dtype)
+
+
+def assign(name, op, *args, dtype=F32) -> Assign:
+    return Assign(name=name, op=EW(op), args=tuple(args), dtype=dtype)
+
+
+def accum(name, value, op, axes, base=None, dtype=F32) -> Accum:
+    return Accum(name=name, value=value, op=EW(op), dtype=dtype, axes=tuple(axes), base=base)
+
+
+def write(out, index, values, atomic=False, dtype=F32) -> Write:
+    if isinstance(values, str):
+        values = (values,)
+    return Write(output=out, index=tuple(index), values=tuple(values), value_dtype=dtype,
+                 atomic=atomic, swizzle="NONE")
+
+
+def strided(axis, extent, start, step, body) -> StridedLoop:
+    return StridedLoop(axis=ax(axis, extent), start=start, step=step, body=tuple(body),
+                       unroll=False, end=None, seed=True)
+
+
+def loop(axis, extent, body, unroll=False, seed=True) -> Loop:
+    return Loop(axis=ax(axis, extent), body=tuple(body), unroll=unroll, seed=seed)
+
+
+# ---------------------------------------------------------------------------
+# graph + meta packaging
+# ---------------------------------------------------------------------------
+
+
+def package(entry: str, node: str, body, inputs: list[tuple], constants: list[tuple],
+            output: tuple, arg_order: list[str], grid, block, smem_bytes=0,
+            zero_outputs=(), rtol=1e-3, atol=1e-4, code="", pid="generated",
+            kernel_inputs: list[str] | None = None, graph_out_shape=None):
+    """Build the graph json and meta json the loader reads.
+
+    ``inputs``: (name, shape, dtype, seed); ``constants``: (name, value);
+    ``output``: (name, shape, dtype)."""
+    nodes: dict = {}
+    for name, value in constants:
+        nodes[name] = {"op": "ConstantOp",
+                       "op_fields": {"name": name, "value": value, "context_value": None,
+                                     "load_ops": [], "source_path": None, "source_parts": [],
+                                     "source_shape": None, "source_dtype": None,
+                                     "source_graph": None},
+                       "inputs": [], "outputs": [{"name": name, "shape": [1], "dtype": "f32"}]}
+    for name, shape, dt, _seed in inputs:
+        nodes[name] = {"op": "InputOp", "op_fields": {}, "inputs": [],
+                       "outputs": [{"name": name, "shape": list(shape), "dtype": dt}]}
+    nodes = dict(sorted(nodes.items()))
+    oname, oshape, odt = output
+    kin = kernel_inputs if kernel_inputs is not None else [n for n in arg_order if n != oname]
+    nodes[node] = {"op": "KernelOp",
+                   "op_fields": {"body": [repr(s) for s in body], "name": entry,
+                                 "zero_delegated": [], "serial": []},
+                   "inputs": list(kin),
+                   "outputs": [{"name": oname,
+                                "shape": list(oshape if graph_out_shape is None else graph_out_shape),
+                                "dtype": odt}]}
+    graph = {"inputs": [i[0] for i in inputs], "outputs": [oname], "nodes": nodes}
+    args = []
+    for name in arg_order:
+        c = next((c for c in constants if c[0] == name), None)
+        i = next((i for i in inputs if i[0] == name), None)
+        if c is not None:
+            args.append({"name": name, "dtype": "f32", "shape": [1], "data": [c[1]]})
+        elif i is not None:
+            args.append({"name": name, "dtype": i[2], "shape": list(i[1]), "seed": i[3]})
+        else:
+            args.append({"name": name, "dtype": odt, "shape": list(oshape), "output": True})
+    meta = {"id": pid, "code": code, "rtol": rtol, "atol": atol,
+            "graph_inputs": [i[0] for i in inputs], "graph_outputs": [oname],
+            "kernels": [{"node": node, "entry": entry, "arg_order": list(arg_order),
+                         "grid": [int(g) for g in grid], "block": [int(b) for b in block],
+                         "smem_bytes": int(smem_bytes), "zero_outputs": list(zero_outputs),
+                         "args": args, "final": True}]}
+    return graph, meta
+
+
+# ---------------------------------------------------------------------------
+# category 1: pointwise
+# ---------------------------------------------------------------------------
+
+# A pointwise program: per-element steps, in emission order.
+#   ("load", base, buffer, "vec"|"const")   ("op", base, opname, argbases...)
+PROGRAMS = {
+    "add": [("load", "in0", "x0", "vec"), ("load", "in1", "x1", "vec"),
+            ("op", "v0", "add", "in0", "in1")],
+    "scale_shift": [("load", "in1", "mul_c1", "const"), ("load", "in2", "x", "vec"),
+                    ("op", "v0", "multiply", "in1", "in2"), ("load", "in0", "add_c1", "const"),
+                    ("op", "v1", "add", "in0", "v0")],
+    "relu_mul": [("load", "in0", "x", "vec"), ("op", "v0", "relu", "in0"),
+                 ("load", "in1", "y", "vec"), ("op", "v1", "multiply", "in1", "v0")],
+}
+
+
+def pointwise(n: int, unroll: int, program: str = "add", block: int = 256,
+              out: str = "add", arg_order=None, constants=(), entry="k_add_pointwise",
+              rtol=0.0, atol=0.0, pid="pointwise"):
+    steps = PROGRAMS[program]
+    if n % unroll:
+        raise ValueError("n must be a multiple of the unroll factor")
+    cells = n // unroll
+    body = []
+    for k in range(unroll):
+        idx = ADD(MUL(V("a0"), L(unroll)), L(k))
+        for st in steps:
+            if st[0] == "load":
+                _, base, buf, kind = st
+                body.append(load(f"{base}__u{k}", buf, (L(0),) if kind == "const" else (idx,)))
+            else:
+                _, base, opname, *args = st
+                body.append(assign(f"{base}__u{k}", opname, *[f"{a}__u{k}" for a in args]))
+    last = [s for s in steps if s[0] == "op"][-1][1]
+    body.append(write(out, (ADD(MUL(V("a0"), L(unroll)), L(0)),),
+                      tuple(f"{last}__u{k}" for k in range(unroll))))
+    t = tile([ax("a0", cells)], body)
+    vec_inputs = []
+    seen = set()
+    for st in steps:
+        if st[0] == "load" and st[3] == "vec" and st[2] not in seen:
+            seen.add(st[2])
+            vec_inputs.append(st[2])
+    if arg_order is None:
+        arg_order = [c[0] for c in constants] + vec_inputs + [out]
+    inputs = [(b, (n,), "f32", i) for i, b in enumerate(sorted(vec_inputs))]
+    grid = (math.ceil(cells / block), 1, 1)
+    return package(entry, out, [t], inputs, list(constants), (out, (n,), "f32"), arg_order,
+                   grid, (block, 1, 1), rtol=rtol, atol=atol, pid=pid)
+
+
+# ---------------------------------------------------------------------------
+# category 2: reductions
+# ---------------------------------------------------------------------------
+
+
+def _combine(state=("acc0",), kind="add"):
+    if kind == "add":
+        return (Assign(name="acc0", op=EW("add"), args=("acc0", "acc0__o"), dtype=None),)
+    if kind == "maximum":
+        return (Assign(name="acc0", op=EW("maximum"), args=("acc0", "acc0__o"), dtype=None),)
+    if kind == "online_softmax":
+        return (
+            Assign(name="acc0__o__gn", op=EW("maximum"), args=("acc0", "acc0__o"), dtype=None),
+            Assign(name="acc0__o__dg", op=EW("subtract"), args=("acc0", "acc0__o__gn"), dtype=None),
+            Assign(name="acc0__o__alpha", op=EW("exp"), args=("acc0__o__dg",), dtype=None),
+            Assign(name="acc0__o__dg_o", op=EW("subtract"), args=("acc0__o", "acc0__o__gn"),
+                   dtype=None),
+            Assign(name="acc0__o__beta", op=EW("exp"), args=("acc0__o__dg_o",), dtype=None),
+            Assign(name="acc0__o__acc1_sa", op=EW("multiply"), args=("acc0__o__alpha", "acc1"),
+                   dtype=None),
+            Assign(name="acc0__o__acc1_sb", op=EW("multiply"), args=("acc0__o__beta", "acc1__o"),
+                   dtype=None),
+            Assign(name="acc1", op=EW("add"), args=("acc0__o__acc1_sa", "acc0__o__acc1_sb"),
+                   dtype=None),
+            Assign(name="acc0", op=EW("copy"), args=("acc0__o__gn",), dtype=None),
+        )
+    raise ValueError(kind)
+
+
+def _block_combine(tid_axis: str, threads: int, states=("acc0",), kind="add"):
+    """WarpShuffle + per-warp smem slots + TreeHalve, as r01..f03 write it."""
+    comb = _combine(states, kind)
+    sb = tuple(f"{s}__o" for s in states)
+    warps = threads // 32
+    out = [WarpShuffle(state=tuple(states), state_b=sb, combine_states=comb, length=32,
+                       dtype=F32)]
+    out += [Smem(name=f"{s}_smem", extents=(warps,), dtype="float", align=0) for s in states]
+    out.append(Cond(cond=EQ(V("lane"), L(0)),
+                    body=tuple(write(f"{s}_smem", (V("warp"),), s) for s in states),
+                    else_body=()))
+    out.append(Sync(barrier_id=0, count=None, warp=False))
+    out.append(TreeHalve(bufs=tuple(f"{s}_smem" for s in states), state=tuple(states),
+                         state_b=sb, combine_states=comb, length=warps, tid_var="warp",
+                         dtype=F32, barrier_id=0, barrier_count=None, inner=None))
+    return out
+
+
+def reduce_full(n: int, threads: int = 128, mean: bool = False, entry=None, pid="reduce_full"):
+    """Full-array sum (r01/r02) or mean (r03) by one CTA of ``threads``."""
+    body = [strided("a0", n, V("a0_co"), L(threads),
+                    [load("in0", "x", (V("a0"),)), accum("acc0", "in0", "add", ("a0",))])]
+    body += _block_combine("a0_co", threads)
+    if mean:
+        tail = [load("in1", "mean_keepdim_count", (L(0),)),
+                assign("v0", "divide", "acc0", "in1"), write("mean", (), "v0")]
+        out, entry = "mean", entry or "k_mean_ffcca3"
+        constants = [("mean_keepdim_count", float(n))]
+        arg_order = ["x", "mean_keepdim_count", "mean"]
+    else:
+        tail = [write("sum_1", (), "acc0")]
+        out, entry = "sum_1", entry or "k_sum_1_reduce"
+        constants = []
+        arg_order = ["x", "sum_1"]
+    body.append(Cond(cond=EQ(V("a0_co"), L(0)), body=tuple(tail), else_body=()))
+    t = tile([ax("a0_co", threads)], body, block_threads=threads)
+    return package(entry, out, [t], [("x", (n,), "f32", 0)], constants, (out, (1,), "f32"),
+                   arg_order, (1, 1, 1), (threads, 1, 1), rtol=1e-4, atol=1e-4, pid=pid,
+                   graph_out_shape=())
+
+
+def reduce_rows(rows: int, cols: int, threads: int = 128, entry="k_sum_1_reduce",
+                pid="reduce_rows"):
+    """Row sum (r04): one row per CTA."""
+    body = [strided("a1", cols, V("a1_co"), L(threads),
+                    [load("in0", "x", (V("a0"), V("a1"))),
+                     accum("acc0", "in0", "add", ("a1",))])]
+    body += _block_combine("a1_co", threads)
+    body.append(Cond(cond=EQ(V("a1_co"), L(0)), body=(write("sum_1", (V("a0"),), "acc0"),),
+                     else_body=()))
+    t = tile([ax("a0", rows), ax("a1_co", threads)], body, block_threads=threads)
+    return package(entry, "sum_1", [t], [("x", (rows, cols), "f32", 0)], [],
+                   ("sum_1", (rows,), "f32"), ["x", "sum_1"], (rows, 1, 1), (threads, 1, 1),
+                   rtol=1e-4, atol=1e-4, pid=pid)
+
+
+# ---------------------------------------------------------------------------
+# category 4: fused rows
+# ---------------------------------------------------------------------------
+
+
+def rmsnorm(rows: int, cols: int, eps: float = 1e-5, threads: int = 128,
+            entry="k_mean_cbd1de", pid="rmsnorm"):
+    body = [strided("a1", cols, V("a1_co"), L(threads),
+                    [load("in2", "x", (V("a0"), V("a1"))), assign("v1", "multiply", "in2", "in2"),
+                     accum("acc0", "v1", "add", ("a1",))])]
+    body += _block_combine("a1_co", threads)
+    body += [load("in1", "mean_count", (L(0),)), assign("v0", "reciprocal", "in1"),
+             assign("v2", "multiply", "acc0", "v0"), load("in0", "add_c1", (L(0),)),
+             assign("v3", "add", "in0", "v2"), assign("v4", "sqrt", "v3"),
+             assign("v5", "reciprocal", "v4"),
+             strided("a2", cols, V("a1_co"), L(threads),
+                     [load("in3", "x", (V("a0"), V("a2"))), assign("v6", "multiply", "in3", "v5"),
+                      load("in4", "w", (V("a2"),)), assign("v7", "multiply", "in4", "v6"),
+                      write("mul_1", (V("a0"), V("a2")), "v7")])]
+    t = tile([ax("a0", rows), ax("a1_co", threads)], body, block_threads=threads)
+    return package(entry, "mul_1", [t], [("w", (cols,), "f32", 1), ("x", (rows, cols), "f32", 0)],
+                   [("add_c1", eps), ("mean_count", float(cols))],
+                   ("mul_1", (rows, cols), "f32"), ["mean_count", "add_c1", "x", "w", "mul_1"],
+                   (rows, 1, 1), (threads, 1, 1), rtol=1e-3, atol=1e-4, pid=pid)
+
+
+def softmax(rows: int, cols: int, threads: int = 128, entry="k_softmax_05263d", pid="softmax"):
+    step = [Let(name="one", value=Lf(1.0), dtype=F32),
+            load("in0", "x", (V("a0"), V("a1"))),
+            assign("in0__gn", "maximum", "acc0", "in0"),
+            assign("in0__dg", "subtract", "acc0", "in0__gn"),
+            assign("in0__alpha", "exp", "in0__dg"),
+            assign("in0__dg_o", "subtract", "in0", "in0__gn"),
+            assign("in0__beta", "exp", "in0__dg_o"),
+            assign("in0__acc1_sa", "multiply", "acc1", "in0__alpha"),
+            assign("in0__acc1_sb", "multiply", "in0__beta", "one"),
+            accum("acc1", "in0__acc1_sb", "add", ("a1",), base="in0__acc1_sa"),
+            accum("acc0", "in0", "maximum", ("a1",))]
+    body = [strided("a1", cols, V("a1_co"), L(threads), step)]
+    body += _block_combine("a1_co", threads, states=("acc0", "acc1"), kind="online_softmax")
+    body += [assign("v2", "reciprocal", "acc1"),
+             strided("a3", cols, V("a1_co"), L(threads),
+                     [load("in2", "x", (V("a0"), V("a3"))), assign("v3", "subtract", "in2", "acc0"),
+                      assign("v4", "exp", "v3"), assign("v5", "multiply", "v2", "v4"),
+                      write("softmax", (V("a0"), V("a3")), "v5")])]
+    t = tile([ax("a0", rows), ax("a1_co", threads)], body, block_threads=threads)
+    return package(entry, "softmax", [t], [("x", (rows, cols), "f32", 0)], [],
+                   ("softmax", (rows, cols), "f32"), ["x", "softmax"], (rows, 1, 1),
+                   (threads, 1, 1), rtol=1e-3, atol=1e-5, pid=pid)
+
+
+def l2norm(rows: int, cols: int, threads: int = 128, entry="k_div_reduce", pid="l2norm"):
+    body = [strided("a1", cols, V("a1_co"), L(threads),
+                    [load("in0", "x", (V("a0"), V("a1"))), assign("v0", "multiply", "in0", "in0"),
+                     accum("acc0", "v0", "add", ("a1",))])]
+    body += _block_combine("a1_co", threads)
+    body += [assign("v1", "sqrt", "acc0"), assign("v2", "reciprocal", "v1"),
+             strided("a2", cols, V("a1_co"), L(threads),
+                     [load("in1", "x", (V("a0"), V("a2"))), assign("v3", "multiply", "in1", "v2"),
+                      write("div", (V("a0"), V("a2")), "v3")])]
+    t = tile([ax("a0", rows), ax("a1_co", threads)], body, block_threads=threads)
+    return package(entry, "div", [t], [("x", (rows, cols), "f32", 0)], [],
+                   ("div", (rows, cols), "f32"), ["x", "div"], (rows, 1, 1), (threads, 1, 1),
+                   rtol=1e-3, atol=1e-4, pid=pid)
+
+
+# ---------------------------------------------------------------------------
+# category 3: matmul
+# ---------------------------------------------------------------------------
+
+
+def _m01_copy(smem, rowbase, src, src_row, src_col, lane_rows, tidl):
+    lr = DIV(MUL(tidl, L(4)), L(64))
+    lc = MOD(MUL(tidl, L(4)), L(64))
+    return CpAsyncCopy(smem=smem, smem_index=(rowbase, L(0)), src=src,
+                       src_index=(src_row(lr), src_col(lc)), nbytes=16, swizzle="NONE",
+                       lane_index=(lr, lc), lane_rows=lane_rows)
+
+
+def matmul(m: int, n: int, k: int, entry="k_matmul_2967be", pid="matmul"):
+    """C = A.B with the m01 schedule: 32x64 C tile per CTA, K in steps of 64
+    through a 3-stage cp.async ring, 16x32 threads with 2x2 outputs each."""
+    BM, BN, BK, ST = 32, 64, 64, 3
+    if m % BM or n % BN or k % BK or k < 2 * BK:
+        raise ValueError("matmul shape must tile by 32x64x64 with K >= 128")
+    tidl = ADD(MUL(V("a0_u"), L(32)), V("a1_u"))
+    body = [Init(name=f"acc0__c{i}_{j}", identity=0.0, dtype=F32) for i in (0, 1) for j in (0, 1)]
+    body += [Smem(name="_a_smem", extents=(BM * ST, BK), dtype="float", align=16),
+             Smem(name="_b_smem", extents=(BK * ST, BN), dtype="float", align=16)]
+
+    def a_row(lr):
+        return ADD(MUL(V("a0_b"), L(BM)), ADD(lr, L(0)))
+
+    def b_col(lc):
+        return ADD(MUL(V("a1_b"), L(BN)), lc)
+
+    for s in range(2):
+        koff = L(s * BK)
+        abase = L(0) if s == 0 else ADD(MUL(L(s), L(BM)), L(0))
+        body.append(_m01_copy("_a_smem", abase, "x0", a_row, lambda lc, ko=koff: ADD(ko, lc),
+                               32, tidl))
+        for half in (0, 32):
+            bbase = L(half) if s == 0 else ADD(MUL(L(s), L(BK)), L(half))
+            body.append(_m01_copy("_b_smem", bbase, "x1",
+                                  lambda lr, ko=koff, h=half: ADD(ko, ADD(lr, L(h))), b_col, 32,
+                                  tidl))
+        body.append(CpAsyncCommit())
+    kn = TernaryExpr(cond=LT(ADD(V("_ks"), L(2 * BK)), L(k)), if_true=ADD(V("_ks"), L(2 * BK)),
+                     if_false=L(k - BK))
+    slot = MOD(ADD(DIV(V("_ks"), L(BK)), L(2)), L(ST))
+    cur = MOD(DIV(V("_ks"), L(BK)), L(ST))
+    inner = [
+        _m01_copy("_a_smem", ADD(MUL(slot, L(BM)), L(0)), "x0", a_row,
+                  lambda lc: ADD(kn, lc), 32, tidl),
+        _m01_copy("_b_smem", ADD(MUL(slot, L(BK)), L(0)), "x1",
+                  lambda lr: ADD(kn, ADD(lr, L(0))), b_col, 32, tidl),
+        _m01_copy("_b_smem", ADD(MUL(slot, L(BK)), L(32)), "x1",
+                  lambda lr: ADD(kn, ADD(lr, L(32))), b_col, 32, tidl),
+        CpAsyncCommit(), CpAsyncWait(group=2), Sync(barrier_id=0, count=None, warp=False),
+    ]
+
+    def bcol(j):
+        return SUB(ADD(ADD(MUL(V("a1_b"), L(BN)), MUL(V("a1_u"), L(2))), L(j)),
+                   MUL(V("a1_b"), L(BN)))
+
+    def arow(i):
+        return SUB(ADD(ADD(MUL(V("a0_b"), L(BM)), MUL(V("a0_u"), L(2))), L(i)),
+                   MUL(V("a0_b"), L(BM)))
+
+    ki = [
+        Load(names=("in1__c0_0",), input="_b_smem",
+             index=(ADD(MUL(cur, L(BK)), V("_ki")), bcol(0)), dtype=None),
+        Load(names=("in0__c0_0",), input="_a_smem",
+             index=(ADD(MUL(cur, L(BM)), arow(0)), V("_ki")), dtype=None),
+        assign("acc0__v__c0_0", "multiply", "in1__c0_0", "in0__c0_0"),
+        accum("acc0__c0_0", "acc0__v__c0_0", "add", ("_ki",)),
+        Load(names=("in1__c0_1",), input="_b_smem",
+             index=(ADD(MUL(cur, L(BK)), V("_ki")), bcol(1)), dtype=None),
+        assign("acc0__v__c0_1", "multiply", "in1__c0_1", "in0__c0_0"),
+        accum("acc0__c0_1", "acc0__v__c0_1", "add", ("_ki",)),
+        Load(names=("in0__c1_0",), input="_a_smem",
+             index=(ADD(MUL(cur, L(BM)), arow(1)), V("_ki")), dtype=None),
+        assign("acc0__v__c1_0", "multiply", "in1__c0_0", "in0__c1_0"),
+        accum("acc0__c1_0", "acc0__v__c1_0", "add", ("_ki",)),
+        assign("acc0__v__c1_1", "multiply", "in1__c0_1", "in0__c1_0"),
+        accum("acc0__c1_1", "acc0__v__c1_1", "add", ("_ki",)),
+    ]
+    inner.append(loop("_ki", BK, ki, unroll=True, seed=False))
+    inner.append(Sync(barrier_id=0, count=None, warp=False))
+    body.append(strided("_ks", k, L(0), L(BK), inner))
+
+    def orow(i):
+        return ADD(ADD(MUL(V("a0_b"), L(BM)), MUL(V("a0_u"), L(2))), L(i))
+
+    def ocol(j):
+        return ADD(ADD(MUL(V("a1_b"), L(BN)), MUL(V("a1_u"), L(2))), L(j))
+
+    body.append(write("matmul", (orow(0), ocol(0)), ("acc0__c0_0", "acc0__c0_1")))
+    body.append(write("matmul", (orow(1), ocol(0)), ("acc0__c1_0", "acc0__c1_1")))
+    t = tile([ax("a0_b", m // BM, win("a0", m)), ax("a1_b", n // BN, win("a1", n)),
+              ax("a0_u", 16), ax("a1_u", 32)], body, block_threads=512,
+             raster_axes=("a0_b", "a1_b"))
+    smem = (BM * ST * BK + BK * ST * BN) * 4
+    return package(entry, "matmul", [t], [("x0", (m, k), "f32", 0), ("x1", (k, n), "f32", 1)],
+                   [], ("matmul", (m, n), "f32"), ["x1", "x0", "matmul"],
+                   ((m // BM) * (n // BN), 1, 1), (512, 1, 1), smem_bytes=smem,
+                   rtol=1e-3, atol=1e-3, pid=pid, kernel_inputs=["x1", "x0"])
+
+
+def matmul_splitk(m: int, n: int, k: int, slice_k: int = 8, entry="k_matmul",
+                  pid="matmul_splitk"):
+    """C += A.B over K slices of ``slice_k`` with atomic writes (m02): 16x32 C
+    tile per CTA, 8x32 threads, 2 rows x 1 column each, K step 8."""
+    BM, BN, BK, TH = 16, 32, 8, 256
+    if m % BM or n % BN or k % slice_k or slice_k % BK:
+        raise ValueError("split-K shape must tile by 16x32 with K slices of multiple of 8")
+    tidl = ADD(MUL(V("a0_u"), L(32)), V("a1_u"))
+    body = [Init(name="acc0__c0_0", identity=0.0, dtype=F32),
+            Init(name="acc0__c1_0", identity=0.0, dtype=F32),
+            Smem(name="_a_smem", extents=(BM, BK), dtype="float", align=16),
+            Smem(name="_b_smem", extents=(BK, BN), dtype="float", align=16)]
+    fa4 = MUL(V("_fa"), L(4))
+    fb4 = MUL(V("_fb"), L(4))
+    ca = CpAsyncCopy(smem="_a_smem", smem_index=(DIV(fa4, L(BK)), MOD(fa4, L(BK))), src="x0",
+                     src_index=(ADD(MUL(V("a0_b"), L(BM)), DIV(fa4, L(BK))),
+                                ADD(MUL(V("_a2_ks"), L(slice_k)), ADD(V("_ks"), MOD(fa4, L(BK))))),
+                     nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0)
+    cb = CpAsyncCopy(smem="_b_smem", smem_index=(DIV(fb4, L(BN)), MOD(fb4, L(BN))), src="x1",
+                     src_index=(ADD(MUL(V("_a2_ks"), L(slice_k)), ADD(V("_ks"), DIV(fb4, L(BN)))),
+                                ADD(MUL(V("a1_b"), L(BN)), MOD(fb4, L(BN)))),
+                     nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0)
+
+    def bcol():
+        return SUB(ADD(ADD(MUL(V("a1_b"), L(BN)), MUL(V("a1_u"), L(1))), L(0)),
+                   MUL(V("a1_b"), L(BN)))
+
+    def arow(i):
+        return SUB(ADD(ADD(MUL(V("a0_b"), L(BM)), MUL(V("a0_u"), L(2))), L(i)),
+                   MUL(V("a0_b"), L(BM)))
+
+    ki = [Load(names=("in1__c0_0",), input="_b_smem", index=(V("_ki"), bcol()), dtype=None),
+          Load(names=("in0__c0_0",), input="_a_smem", index=(arow(0), V("_ki")), dtype=None),
+          assign("acc0__v__c0_0", "multiply", "in1__c0_0", "in0__c0_0"),
+          accum("acc0__c0_0", "acc0__v__c0_0", "add", ("_ki",)),
+          Load(names=("in0__c1_0",), input="_a_smem", index=(arow(1), V("_ki")), dtype=None),
+          assign("acc0__v__c1_0", "multiply", "in1__c0_0", "in0__c1_0"),
+          accum("acc0__c1_0", "acc0__v__c1_0", "add", ("_ki",))]
+    ks = [strided("_fa", BM * BK // 4, tidl, L(TH), [ca]),
+          strided("_fb", BK * BN // 4, tidl, L(TH), [cb]),
+          CpAsyncCommit(), CpAsyncWait(group=0), Sync(barrier_id=0, count=None, warp=False),
+          loop("_ki", BK, ki, unroll=True, seed=False),
+          Sync(barrier_id=0, count=None, warp=False)]
+    body.append(strided("_ks", slice_k, L(0), L(BK), ks))
+
+    def orow(i):
+        return ADD(ADD(MUL(V("a0_b"), L(BM)), MUL(V("a0_u"), L(2))), L(i))
+
+    ocol = ADD(ADD(MUL(V("a1_b"), L(BN)), MUL(V("a1_u"), L(1))), L(0))
+    body.append(write("matmul", (orow(0), ocol), "acc0__c0_0", atomic=True))
+    body.append(write("matmul", (orow(1), ocol), "acc0__c1_0", atomic=True))
+    slices = k // slice_k
+    t = tile([ax("_a2_ks", slices), ax("a0_b", m // BM, win("a0", m)),
+              ax("a1_b", n // BN, win("a1", n)), ax("a0_u", 8), ax("a1_u", 32)], body,
+             block_threads=TH, raster_axes=("a0_b", "a1_b"))
+    return package(entry, "matmul", [t], [("x0", (m, k), "f32", 0), ("x1", (k, n), "f32", 1)],
+                   [], ("matmul", (m, n), "f32"), ["x1", "x0", "matmul"],
+                   (slices * (m // BM) * (n // BN), 1, 1), (TH, 1, 1),
+                   zero_outputs=["matmul"], rtol=1e-3, atol=1e-3, pid=pid,
+                   kernel_inputs=["x1", "x0"])
+
+
+# ---------------------------------------------------------------------------
+# category 5: attention
+# ---------------------------------------------------------------------------
+
+
+def _online_step(score_name: str, vload: Load, key_axis: str):
+    """The per-key online-softmax update of a02, for one output element."""
+    s = "__c0_0"
+    return [
+        assign(f"v4{s}", "multiply", score_name, "v1"),
+        Let(name=f"one{s}", value=Lf(1.0), dtype=F32),
+        assign(f"v4__gn{s}", "maximum", f"acc1{s}", f"v4{s}"),
+        assign(f"v4__dg{s}", "subtract", f"acc1{s}", f"v4__gn{s}"),
+        assign(f"v4__alpha{s}", "exp", f"v4__dg{s}"),
+        assign(f"v4__dg_o{s}", "subtract", f"v4{s}", f"v4__gn{s}"),
+        assign(f"v4__beta{s}", "exp", f"v4__dg_o{s}"),
+        assign(f"v4__acc3_sa{s}", "multiply", f"acc3{s}", f"v4__alpha{s}"),
+        assign(f"v4__acc3_sb{s}", "multiply", f"one{s}", f"v4__beta{s}"),
+        accum(f"acc3{s}", f"v4__acc3_sb{s}", "add", (key_axis,), base=f"v4__acc3_sa{s}"),
+        assign(f"v4__acc5__sum_sa{s}", "multiply", f"acc5__sum{s}", f"v4__alpha{s}"),
+        vload,
+        assign(f"v4__acc5__sum_sb{s}", "multiply", "in7__bc0", f"v4__beta{s}"),
+        accum(f"acc5__sum{s}", f"v4__acc5__sum_sb{s}", "add", (key_axis,),
+              base=f"v4__acc5__sum_sa{s}"),
+        accum(f"acc1{s}", f"v4{s}", "maximum", (key_axis,)),
+    ]
+
+
+def attention(s: int, d: int, scale_div: float | None = None,
+              entry="k_matmul_softmax_reduce_6f0029", pid="attention"):
+    """softmax(q.kt / c) . v for one head, q,v [S,D], kt [D,S] (a02)."""
+    if d % 32:
+        raise ValueError("head dim must be a multiple of 32")
+    c = float(scale_div) if scale_div is not None else math.sqrt(d)
+    row = ADD(ADD(MUL(V("a0_b"), L(1)), MUL(V("a0_u"), L(1))), L(0))
+    col = ADD(ADD(MUL(V("a5_b"), L(32)), MUL(V("a5_u"), L(1))), L(0))
+    dot = loop("a2", d, [load("in2__ar0", "q", (row, V("a2"))),
+                         load("in1__ar0", "kt", (V("a2"), V("a1"))),
+                         assign("v3__ar0", "multiply", "in1__ar0", "in2__ar0"),
+                         accum("acc0__ar0", "v3__ar0", "add", ("a2",))])
+    vload = load("in7__bc0", "v", (V("a1"), col))
+    body = [load("in0", "div_c1", (L(0),)), assign("v1", "reciprocal", "in0"),
+            loop("a1", s, [dot] + _online_step("acc0__ar0", vload, "a1")),
+            assign("v9__c0_0", "reciprocal", "acc3__c0_0"),
+            assign("acc5__c0_0", "multiply", "acc5__sum__c0_0", "v9__c0_0"),
+            write("matmul_1", (row, col), "acc5__c0_0")]
+    t = tile([ax("a0_b", s, win("a0", s)), ax("a5_b", d // 32, win("a5", d)),
+              ax("a0_u", 1), ax("a5_u", 32)], body, block_threads=32,
+             raster_axes=("a0_b", "a5_b"), raster_group=8)
+    return package(entry, "matmul_1", [t],
+                   [("kt", (d, s), "f32", 1), ("q", (s, d), "f32", 0), ("v", (s, d), "f32", 2)],
+                   [("div_c1", c)], ("matmul_1", (s, d), "f32"),
+                   ["div_c1", "q", "kt", "v", "matmul_1"], (s * d // 32, 1, 1), (32, 1, 1),
+                   rtol=1e-3, atol=1e-4, pid=pid)
+
+
+def attention_bhsd(b: int, h: int, s: int, d: int, dtype: str = "f32",
+                   entry="k_attention_bhsd", pid="attention_bhsd"):
+    """softmax(q.k^T / sqrt(d)) . v over ``[B, H, S, D]`` q, k, v (k NOT
+    transposed), one output element per thread; the a02 schedule with batch
+    and head axes added.  ``dtype='bf16'`` stores q, k, v and the output as
+    bf16 while the arithmetic stays f32."""
+    if d % 32:
+        raise ValueError("head dim must be a multiple of 32")
+    dt = datatype(dtype)
+    row = ADD(ADD(MUL(V("a0_b"), L(1)), MUL(V("a0_u"), L(1))), L(0))
+    col = ADD(ADD(MUL(V("a5_b"), L(32)), MUL(V("a5_u"), L(1))), L(0))
+    bh = (V("ab"), V("ah"))
+    dot = loop("a2", d, [load("in2__ar0", "q", bh + (row, V("a2"))),
+                         load("in1__ar0", "k", bh + (V("a1"), V("a2"))),
+                         assign("v3__ar0", "multiply", "in1__ar0", "in2__ar0"),
+                         accum("acc0__ar0", "v3__ar0", "add", ("a2",))])
+    vload = load("in7__bc0", "v", bh + (V("a1"), col))
+    body = [load("in0", "div_c1", (L(0),)), assign("v1", "reciprocal", "in0"),
+            loop("a1", s, [dot] + _online_step("acc0__ar0", vload, "a1")),
+            assign("v9__c0_0", "reciprocal", "acc3__c0_0"),
+            assign("acc5__c0_0", "multiply", "acc5__sum__c0_0", "v9__c0_0"),
+            write("out", bh + (row, col), "acc5__c0_0")]
+    t = tile([ax("ab", b), ax("ah", h), ax("a0_b", s, win("a0", s)),
+              ax("a5_b", d // 32, win("a5", d)), ax("a0_u", 1), ax("a5_u", 32)], body,
+             block_threads=32, raster_axes=("a0_b", "a5_b"), raster_group=8)
+    shp = (b, h, s, d)
+    tol = (2e-2, 2e-2) if dtype == "bf16" else (1e-3, 1e-4)
+    return package(entry, "out", [t],
+                   [("k", shp, dtype, 1), ("q", shp, dtype, 0), ("v", shp, dtype, 2)],
+                   [("div_c1", math.sqrt(d))], ("out", shp, dtype),
+                   ["div_c1", "q", "k", "v", "out"], (b * h * s * d // 32, 1, 1), (32, 1, 1),
+                   rtol=tol[0], atol=tol[1], pid=pid)
+
+
+# ---------------------------------------------------------------------------
+# the benchmark configurations
+# ---------------------------------------------------------------------------
+
+def bench_kernels():
+    """IR + meta for every BASELINE configuration, keyed by a short name."""
+    return {
+        "vector_add": lambda: pointwise(1 << 28, 4, "add", pid="vector_add_2p28"),
+        "sum": lambda: reduce_full(1 << 26, pid="sum_2p26"),
+        "mean": lambda: reduce_full(1 << 26, mean=True, pid="mean_2p26"),
+        "row_sum": lambda: reduce_rows(8192, 8192, pid="row_sum_8192"),
+        "rmsnorm": lambda: rmsnorm(65536, 4096, eps=1e-6, pid="rmsnorm_65536x4096"),
+        "softmax": lambda: softmax(65536, 4096, pid="softmax_65536x4096"),
+        "l2norm": lambda: l2norm(65536, 4096, pid="l2norm_65536x4096"),
+        "matmul_square": lambda: matmul(8192, 8192, 8192, pid="matmul_8192"),
+        "matmul_rect": lambda: matmul(16384, 4096, 1024, pid="matmul_16384x4096x1024"),
+        "matmul_splitk8": lambda: matmul_splitk(16384, 4096, 1024, slice_k=128,
+                                                pid="matmul_splitk8"),
+        "attention_f32": lambda: attention_bhsd(16, 32, 4096, 128, "f32", pid="attn_f32"),
+        "attention_bf16": lambda: attention_bhsd(16, 32, 4096, 128, "bf16", pid="attn_bf16"),
+    }
+
+
+def golden_cases():
+    """Small generated kernels the reference interpreter is run on to make
+    golden vectors: (name, graph, meta, seed_offset, distribution)."""
+    cases = []
+
+    def add(name, gm, off=0, dist="normal"):
+        cases.append((name, gm[0], gm[1], off, dist))
+
+    add("gen_add_u4_4096", pointwise(4096, 4, "add", pid="gen_add"), 0, "uniform")
+    add("gen_relu_mul_u2_1000", pointwise(1000, 2, "relu_mul", out="mul", entry="k_mul_pointwise",
+                                          pid="gen_relu_mul"))
+    add("gen_sum_5000", reduce_full(5000, pid="gen_sum"), 0, "uniform01")
+    add("gen_mean_8192_t256", reduce_full(8192, threads=256, mean=True, pid="gen_mean"), 0,
+        "uniform01")
+    add("gen_rowsum_48x300", reduce_rows(48, 300, pid="gen_rowsum"))
+    add("gen_rmsnorm_32x640", rmsnorm(32, 640, eps=1e-6, pid="gen_rmsnorm"))
+    add("gen_softmax_40x1000", softmax(40, 1000, pid="gen_softmax"))
+    add("gen_l2norm_24x256_t64", l2norm(24, 256, threads=64, pid="gen_l2norm"))
+    add("gen_matmul_64x128x192", matmul(64, 128, 192, pid="gen_matmul"), 0, "uniform")
+    add("gen_splitk_32x64x64_s16", matmul_splitk(32, 64, 64, slice_k=16, pid="gen_splitk"))
+    add("gen_attn_64x32", attention(64, 32, pid="gen_attn"))
+    add("gen_attn_bhsd_2x2x32x32", attention_bhsd(2, 2, 32, 32, pid="gen_attn_bhsd"))
+    return cases
+
+
+def dumps(obj) -> str:
+    return json.dumps(obj, indent=1) + "\n"

@@ -1,0 +1,169 @@
+#!/usr/bin/env python3
+"""Regenerate the golden fixtures under ``tests/golden/`` from the reference.
+
+Run in a container where the reference checkout exists (default
+``/root/reference``, or ``--ref PATH``).  It writes:
+
+* ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
+  ``expected.npz`` -- the reference's own golden vectors (numpy float64
+  results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
+* ``ref_interp/<case>.npz``: outputs of the reference's golden model
+  ``ptxgen/interp.py`` run here on extra inputs (every problem reseeded, plus
+  IR that ``ptxgen.irgen`` generates at other shapes).  The reference
+  interpreter is imported from the checkout and fed IR objects built by this
+  repository's own deserialiser, which stands in for the absent ``emmy-ml``
+  package.  Inputs are not stored: ``cases.json`` records how to rebuild them.
+
+Nothing at test time reads the reference checkout; only these files.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import shutil
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO / "emmy-ptx_b200"))
+sys.path.insert(0, str(REPO))
+
+from ptxgen import ir  # noqa: E402
+from ptxgen.loader import load_kernel, load_kernel_data  # noqa: E402
+
+
+def install_emmy_standin() -> None:
+    """Register ``emmy.compiler.*`` modules whose classes are ours."""
+    names = {
+        "emmy": {},
+        "emmy.compiler": {},
+        "emmy.compiler.graph": {"Graph": ir.Graph},
+        "emmy.compiler.ir": {},
+        "emmy.compiler.ir.expr": {k: getattr(ir, k) for k in (
+            "BinaryExpr", "Builtin", "CastExpr", "FlatIndex", "FuncCallExpr", "Literal",
+            "TernaryExpr", "Var")},
+        "emmy.compiler.ir.kernel": {k: getattr(ir, k) for k in (
+            "Accum", "Assign", "Cond", "Load", "Loop", "Select", "Smem", "StridedLoop",
+            "Sync", "Tile", "TreeHalve", "WarpShuffle", "Write", "KernelOp")},
+        "emmy.compiler.ir.kernel.ir": {k: getattr(ir, k) for k in (
+            "CpAsyncCommit", "CpAsyncCopy", "CpAsyncWait")},
+        "emmy.compiler.ir.stmt": {k: getattr(ir, k) for k in ("Init", "Let", "ZeroPrologue")},
+    }
+    for mod, attrs in names.items():
+        m = types.ModuleType(mod)
+        m.__path__ = []  # mark as package
+        for k, v in attrs.items():
+            setattr(m, k, v)
+        sys.modules[mod] = m
+
+
+def import_reference(ref: Path):
+    """Import the reference ``ptxgen`` package under the name ``refptxgen``."""
+    install_emmy_standin()
+    pkg = ref / "ptxgen"
+    spec = importlib.util.spec_from_file_location(
+        "refptxgen", pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["refptxgen"] = mod
+    spec.loader.exec_module(mod)
+    return importlib.import_module("refptxgen.interp")
+
+
+def rebuild_inputs(spec, seed_offset: int, dist: str) -> dict[str, np.ndarray]:
+    """Deterministic inputs for a case: runner argument forms with each
+    ``seed`` shifted by ``seed_offset``; ``dist`` picks the distribution."""
+    out: dict[str, np.ndarray] = {}
+    for name in spec.arg_order:
+        a = spec.args[name]
+        if a.scalar:
+            continue
+        if a.output:
+            out[name] = np.zeros(a.shape, dtype=np.float32)
+        elif a.data is not None:
+            out[name] = np.asarray(a.data, dtype=np.float64).astype(np.float32).reshape(a.shape)
+        else:
+            rng = np.random.default_rng(int(a.seed or 0) + seed_offset)
+            if dist == "normal":
+                x = rng.standard_normal(a.shape)
+            elif dist == "uniform01":
+                x = rng.random(a.shape)
+            else:
+                x = rng.uniform(-1.0, 1.0, a.shape)
+            out[name] = x.astype(np.float32)
+    for name in spec.zero_outputs:
+        if name in out:
+            out[name][...] = 0
+    return out
+
+
+def generated_cases():
+    """Extra IR at other shapes, produced by ``ptxgen.irgen``."""
+    from ptxgen import irgen
+    return irgen.golden_cases()
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    ref = Path(args.ref)
+    if not (ref / "ptxgen" / "interp.py").exists():
+        print(f"no reference checkout at {ref}", file=sys.stderr)
+        return 2
+
+    # 1. copy the shipped problems
+    pdst = HERE / "problems"
+    if pdst.exists():
+        shutil.rmtree(pdst)
+    for pdir in sorted((ref / "problems").iterdir()):
+        if not (pdir / "meta.json").exists():
+            continue
+        d = pdst / pdir.name
+        d.mkdir(parents=True)
+        for f in sorted(pdir.iterdir()):
+            if f.name == "meta.json" or f.name == "expected.npz" or f.name.endswith(".ir.json"):
+                shutil.copyfile(f, d / f.name)
+
+    # 2. run the reference interpreter on extra inputs
+    ref_interp = import_reference(ref)
+    odst = HERE / "ref_interp"
+    if odst.exists():
+        shutil.rmtree(odst)
+    odst.mkdir()
+    cases = []
+    for pdir in sorted(pdst.iterdir()):
+        meta = json.loads((pdir / "meta.json").read_text())
+        for k in meta["kernels"]:
+            ir_path = pdir / f"{k['entry']}.ir.json"
+            spec = load_kernel(ir_path)
+            for off, dist in ((1000, "normal"), (2000, "uniform")):
+                inputs = rebuild_inputs(spec, off, dist)
+                outs = ref_interp.interpret(spec, inputs)
+                case = f"{pdir.name}__{k['entry']}__{dist}{off}"
+                np.savez_compressed(odst / f"{case}.npz", **{n: np.asarray(v) for n, v in outs.items()})
+                cases.append({"case": case, "ir": f"problems/{pdir.name}/{ir_path.name}",
+                              "seed_offset": off, "dist": dist})
+    for name, data, meta, off, dist in generated_cases():
+        spec = load_kernel_data(data, meta, source=name)
+        gdir = HERE / "generated"
+        gdir.mkdir(exist_ok=True)
+        (gdir / f"{name}.ir.json").write_text(json.dumps(data, indent=1) + "\n")
+        (gdir / f"{name}.meta.json").write_text(json.dumps(meta, indent=1) + "\n")
+        inputs = rebuild_inputs(spec, off, dist)
+        outs = ref_interp.interpret(spec, inputs)
+        np.savez_compressed(odst / f"{name}.npz", **{n: np.asarray(v) for n, v in outs.items()})
+        cases.append({"case": name, "ir": f"generated/{name}.ir.json",
+                      "meta": f"generated/{name}.meta.json", "seed_offset": off, "dist": dist})
+    (HERE / "cases.json").write_text(json.dumps(cases, indent=1) + "\n")
+    print(f"{len(cases)} reference-interpreter cases written")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,54 @@
+"""The CPU oracle against the reference's golden vectors.
+
+* every shipped problem: oracle output vs ``expected.npz`` within the
+  problem's own ``rtol``/``atol`` (``scripts/verify_semantics.py:65-97``);
+* every recorded case: oracle output vs the reference interpreter's output on
+  the same inputs, bit for bit.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.interp import interpret, make_inputs
+from ptxgen.loader import load_kernel, load_kernel_data
+
+GOLDEN = Path(__file__).parent / "golden"
+PROBLEMS = sorted(p for p in (GOLDEN / "problems").iterdir() if (p / "meta.json").exists())
+
+
+@pytest.mark.parametrize("pdir", PROBLEMS, ids=[p.name for p in PROBLEMS])
+def test_oracle_matches_expected(pdir):
+    meta = json.loads((pdir / "meta.json").read_text())
+    expected = dict(np.load(pdir / "expected.npz"))
+    produced = {}
+    for k in meta["kernels"]:
+        spec = load_kernel(pdir / f"{k['entry']}.ir.json")
+        outs = interpret(spec, make_inputs(spec, produced))
+        produced.update(outs)
+    for name, ref in expected.items():
+        got = np.asarray(produced[name], dtype=np.float32).reshape(ref.shape)
+        assert np.allclose(got, ref, rtol=meta["rtol"], atol=meta["atol"], equal_nan=True), name
+
+
+def _rebuild(spec, off, dist):
+    from tests.golden.make_golden import rebuild_inputs  # same recipe as recorded
+    return rebuild_inputs(spec, off, dist)
+
+
+CASES = json.loads((GOLDEN / "cases.json").read_text())
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["case"] for c in CASES])
+def test_oracle_bit_exact_vs_reference_interpreter(case):
+    if "meta" in case:
+        spec = load_kernel_data(json.loads((GOLDEN / case["ir"]).read_text()),
+                                json.loads((GOLDEN / case["meta"]).read_text()), case["case"])
+    else:
+        spec = load_kernel(GOLDEN / case["ir"])
+    outs = interpret(spec, _rebuild(spec, case["seed_offset"], case["dist"]))
+    ref = np.load(GOLDEN / "ref_interp" / f"{case['case']}.npz")
+    for name in ref.files:
+        assert np.array_equal(np.asarray(outs[name]), ref[name], equal_nan=True), name
