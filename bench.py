@@ -1,0 +1,543 @@
+#!/usr/bin/env python3
+"""Benchmark of the Emmy Kernel IR -> B200 hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl ours|reference]
+
+One step = one pass of the compiled IR kernels of a BASELINE configuration
+over one batch of synthetic inputs already resident in HBM.  The default
+workload is BASELINE configs[1], the reductions: full-array sum and mean over
+2**26 f32 ~ U[0,1] and the row sum of an 8192 x 8192 f32 ~ N(0,1) matrix.
+Other workloads: ``pointwise`` (c = a + b, 2**28), ``rows`` (RMSNorm,
+softmax, L2-norm on 65536 x 4096), ``matmul``, ``attention``.
+
+Multi-GPU (launched by torch.distributed.run): one process per GPU, weak
+scaling -- each rank owns a full-size shard; full reductions add an NCCL
+all-reduce of the per-rank results (the mean's divisor is the global count,
+so the reduced value is the global mean).  Time is taken on the device with
+events on the launching stream, and the reported time is the max over ranks.
+
+``--impl reference`` times the reference's own CPU algorithm -- the CPU
+oracle restating ``ptxgen/interp.py`` -- on the same configuration, rank 0
+only, each step a bounded sample of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "emmy-ptx_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "HBM GB/s (% of 8 TB/s) for mem-bound kernels; TFLOP/s for matmul/attn"
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+
+class Job:
+    """One compiled kernel of a workload with its inputs and work figures."""
+
+    def __init__(self, key, spec, inputs, algo_bytes, algo_flops=0.0, allreduce=None,
+                 check=None):
+        self.key = key
+        self.spec = spec
+        self.inputs = inputs          # host arrays (uploaded per step in e2e)
+        self.algo_bytes = algo_bytes  # per launch
+        self.algo_flops = algo_flops  # per launch
+        self.allreduce = allreduce    # output name reduced across ranks, or None
+        self.check = check            # (outputs) -> None, raises on mismatch
+        self.pk = None
+
+
+def _spec(gm, name):
+    from ptxgen.loader import load_kernel_data
+    return load_kernel_data(gm[0], gm[1], name)
+
+
+def workload_reductions(rank: int, world: int):
+    from ptxgen import irgen
+    n = 1 << 26
+    rows = cols = 8192
+    rng = np.random.default_rng(1000 + rank)
+    x = rng.random(n, dtype=np.float32)
+    xr = rng.standard_normal((rows, cols), dtype=np.float32)
+    total = n * world
+    s_spec = _spec(irgen.reduce_full(n, pid="sum_2p26"), "sum")
+    m_spec = _spec(irgen.reduce_full(n, mean=True, pid="mean_2p26"), "mean")
+    m_spec.args["mean_keepdim_count"].data = [float(total)]
+    r_spec = _spec(irgen.reduce_rows(rows, cols, pid="row_sum"), "row_sum")
+    local_sum = float(x.astype(np.float64).sum())
+
+    def chk_sum(out, key="sum_1", div=1.0):
+        got = float(out[key][0])
+        # the all-reduced value is the global figure; compare the local share
+        want = local_sum / div
+        tol = 1e-5 * abs(want) * (world if world > 1 else 1)
+        if world == 1 and abs(got - want) > tol:
+            raise AssertionError(f"{key}: {got} vs {want}")
+
+    def chk_rows(out):
+        ref = xr[:64].astype(np.float64).sum(-1)
+        bound = 1e-5 * np.abs(xr[:64].astype(np.float64)).sum(-1)
+        if np.any(np.abs(out["sum_1"][:64] - ref) > bound):
+            raise AssertionError("row sums")
+
+    return [
+        Job("sum", s_spec, {"x": x}, n * 4 + 4, allreduce="sum_1", check=chk_sum),
+        Job("mean", m_spec, {"x": x}, n * 4 + 4, allreduce="mean",
+            check=lambda o: chk_sum(o, "mean", float(total))),
+        Job("row_sum", r_spec, {"x": xr}, rows * cols * 4 + rows * 4, check=chk_rows),
+    ], {"workload": "configs[1] reductions: sum+mean over 2^26 f32 U[0,1], row sum 8192x8192 "
+                    "f32 N(0,1)", "elements_per_rank": 2 * n + rows * cols}
+
+
+def workload_pointwise(rank: int, world: int):
+    from ptxgen import irgen
+    n = 1 << 28
+    rng = np.random.default_rng(2000 + rank)
+    a = rng.uniform(-1, 1, n).astype(np.float32)
+    b = rng.uniform(-1, 1, n).astype(np.float32)
+    spec = _spec(irgen.pointwise(n, 4, "add", pid="vector_add_2p28"), "add")
+
+    def chk(out):
+        if not np.array_equal(out["add"][: 1 << 20], a[: 1 << 20] + b[: 1 << 20]):
+            raise AssertionError("vector add not bit-exact")
+
+    return [Job("vector_add", spec, {"x0": a, "x1": b}, 12 * n, check=chk)], {
+        "workload": "configs[0] scaled: c=a+b over 2^28 f32 U[-1,1]", "elements_per_rank": n}
+
+
+def workload_rows(rank: int, world: int):
+    from ptxgen import irgen
+    r, c = 65536, 4096
+    rng = np.random.default_rng(3000 + rank)
+    x = rng.standard_normal((r, c), dtype=np.float32)
+    g = (1.0 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    jobs = []
+    for key, gm in (("rmsnorm", irgen.rmsnorm(r, c, eps=1e-6)), ("softmax", irgen.softmax(r, c)),
+                    ("l2norm", irgen.l2norm(r, c))):
+        spec = _spec(gm, key)
+        ins = {"x": x}
+        if key == "rmsnorm":
+            ins["w"] = g
+        jobs.append(Job(key, spec, ins, 8 * r * c + (4 * c if key == "rmsnorm" else 0)))
+    return jobs, {"workload": "configs[2] fused rows: RMSNorm, softmax, L2-norm on 65536x4096 f32",
+                  "elements_per_rank": 3 * r * c}
+
+
+WORKLOADS = {"reductions": workload_reductions, "pointwise": workload_pointwise,
+             "rows": workload_rows}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], 0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": smax or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as td
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.td = td
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.td.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if not self.pg:
+            return b
+        obj = [b]
+        self.td.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.td.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+
+
+def run_ours(args, dist: Dist):
+    import ctypes as C
+    from ptxgen.runtime import Device, PreparedKernel, check
+    jobs, cfg = WORKLOADS[args.workload](dist.rank, dist.world)
+    dev = Device.get(dist.local)
+    comm = None
+    if dist.world > 1 and any(j.allreduce for j in jobs):
+        uid = None
+        if dist.rank == 0:
+            buf = C.create_string_buffer(128)
+            check(dev.L.emmy_nccl_unique_id(buf), "nccl id")
+            uid = buf.raw
+        uid = dist.bcast_bytes(uid)
+        comm = C.c_void_p()
+        ubuf = C.create_string_buffer(uid, 128)
+        check(dev.L.emmy_nccl_init(dev.ctx, dist.world, dist.rank, ubuf, C.byref(comm)), "nccl init")
+    for j in jobs:
+        j.pk = PreparedKernel(j.spec, dev=dev)
+        j.pk.upload(j.inputs)
+    dev.sync()
+
+    def step(events=None):
+        for i, j in enumerate(jobs):
+            if events is not None:
+                dev.record(events[i][0])
+            j.pk.launch()
+            if events is not None:
+                dev.record(events[i][1])
+            if comm is not None and j.allreduce:
+                a = j.spec.args[j.allreduce]
+                check(dev.L.emmy_allreduce_sum_f32(comm, j.pk.bufs[j.allreduce],
+                                                   a.numel, dev.stream), "allreduce")
+
+    for _ in range(args.warmup):
+        step()
+    dev.sync()
+    for j in jobs:
+        j.pk.check_errors()
+        if j.check is not None and dist.world == 1:
+            j.check(j.pk.download())
+    # ---- timed region: device-resident inputs ----
+    evs = [[(dev.event(), dev.event()) for _ in jobs] for _ in range(args.steps)]
+    t0, t1 = dev.event(), dev.event()
+    dist.barrier()
+    dev.sync()
+    with ClockSampler(dist.local) as clk:
+        dev.record(t0)
+        for s in range(args.steps):
+            step(evs[s])
+        dev.record(t1)
+        dev.sync()
+    dist.barrier()
+    total_ms = dev.elapsed_ms(t0, t1)
+    per_kernel = {j.key: [dev.elapsed_ms(*evs[s][i]) for s in range(args.steps)]
+                  for i, j in enumerate(jobs)}
+    for j in jobs:
+        j.pk.check_errors()
+    ms = dist.max(total_ms) / args.steps
+    # ---- e2e: host buffers through the public launch API ----
+    pinned = {}
+    h2d = 0
+    for j in jobs:
+        for name, arr in j.inputs.items():
+            key = (id(arr), name)
+            if key in pinned:
+                continue
+            p = dev.host_alloc(arr.nbytes)
+            view = np.ctypeslib.as_array((C.c_char * arr.nbytes).from_address(p))
+            view[:] = np.frombuffer(np.ascontiguousarray(arr).tobytes(), dtype=np.uint8).view("S1")
+            pinned[key] = (p, arr.nbytes)
+    out_host = {j.key: {o: np.empty(j.spec.args[o].shape, np.float32) for o in j.spec.outputs}
+                for j in jobs}
+
+    def e2e_step():
+        nb_in, nb_out = 0, 0
+        done = set()
+        for j in jobs:
+            for name, arr in j.inputs.items():
+                p, nb = pinned[(id(arr), name)]
+                if (id(arr), j.key, name) in done:
+                    continue
+                check(dev.L.emmy_memcpy_htod(C.c_uint64(j.pk.bufs[name]), C.c_void_p(p), nb,
+                                             dev.stream), "htod")
+                nb_in += nb
+        step()
+        for j in jobs:
+            for o, host in out_host[j.key].items():
+                dev.dtoh(host, j.pk.bufs[o])
+                nb_out += host.nbytes
+        return nb_in, nb_out
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    dev.sync()
+    e0, e1 = dev.event(), dev.event()
+    dist.barrier()
+    dev.sync()
+    dev.record(e0)
+    esteps = max(1, min(args.steps, 5))
+    for _ in range(esteps):
+        h2d, d2h = e2e_step()
+    dev.record(e1)
+    dev.sync()
+    dist.barrier()
+    e2e_ms = dist.max(dev.elapsed_ms(e0, e1)) / esteps
+    for p, _ in pinned.values():
+        dev.host_free(p)
+
+    bytes_step = sum(j.algo_bytes for j in jobs)
+    flops_step = sum(j.algo_flops for j in jobs)
+    pk = peaks()
+    # dominant kernel and its roofline
+    avg = {k: sum(v) / len(v) for k, v in per_kernel.items()}
+    dom = max(jobs, key=lambda j: sum(per_kernel[j.key]))
+    dom_ms = avg[dom.key]
+    traffic = None
+    tpath = ROOT / "profiles" / "traffic.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get(f"{args.workload}:{dom.key}")
+    if dom.algo_flops:
+        achieved = dom.algo_flops / (dom_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2),
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        achieved = dom.algo_bytes / (dom_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s"}
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["peak_source"] = pk["source"]
+    roof["kernel"] = dom.key
+    roof["traffic"] = traffic
+    roof["frac_of_spec_8tbs"] = round(achieved / SPEC_HBM_GBS, 4) if not dom.algo_flops else None
+    if flops_step:
+        value = flops_step * dist.world / (ms * 1e-3) / 1e12
+        unit = "TFLOP/s"
+        e2e_val = flops_step * dist.world / (e2e_ms * 1e-3) / 1e12
+    else:
+        value = bytes_step * dist.world / (ms * 1e-3) / 1e9
+        unit = "GB/s"
+        e2e_val = bytes_step * dist.world / (e2e_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy, BASELINE shapes and distributions)",
+        "config": dict(cfg, l2="every input is larger than the 126 MB L2",
+                       parallelism=f"shards x{dist.world}, NCCL all-reduce for full reductions"),
+        "kernels_ms": {k: round(v, 4) for k, v in avg.items()},
+        "roofline": roof,
+        "e2e": {"value": round(e2e_val, 2), "unit": unit, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": len(jobs) * args.steps,
+        "clocks": clk.summary(),
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_budget)
+    for j in jobs:
+        j.pk.close()
+    if comm is not None:
+        check(dev.L.emmy_nccl_destroy(comm), "nccl destroy")
+    return line
+
+
+# ---------------------------------------------------------------------------
+# the CPU oracle (reference algorithm) on a bounded sample
+# ---------------------------------------------------------------------------
+
+
+def _oracle_sample(workload: str):
+    """(description, [(spec, inputs, algo_bytes)]) of a bounded sample."""
+    from ptxgen import irgen
+    rng = np.random.default_rng(7)
+    out = []
+    if workload == "reductions":
+        n = 1 << 20
+        x = rng.random(n, dtype=np.float32)
+        for gm in (irgen.reduce_full(n), irgen.reduce_full(n, mean=True)):
+            spec = _spec(gm, "s")
+            ins = {"x": x}
+            if "mean_keepdim_count" in spec.args:
+                ins["mean_keepdim_count"] = np.array([float(n)], np.float32)
+            out.append((spec, ins, n * 4))
+        xr = rng.standard_normal((256, 8192), dtype=np.float32)
+        out.append((_spec(irgen.reduce_rows(256, 8192), "r"), {"x": xr}, xr.nbytes))
+        return "sum+mean over 2^20 f32 and row sum of 256x8192 (same IR, interp algorithm)", out
+    if workload == "pointwise":
+        n = 1 << 22
+        a = rng.uniform(-1, 1, n).astype(np.float32)
+        b = rng.uniform(-1, 1, n).astype(np.float32)
+        out.append((_spec(irgen.pointwise(n, 4, "add"), "a"), {"x0": a, "x1": b}, 12 * n))
+        return "c=a+b over 2^22 f32", out
+    if workload == "rows":
+        x = rng.standard_normal((512, 4096), dtype=np.float32)
+        g = np.ones(4096, np.float32)
+        for gm in (irgen.rmsnorm(512, 4096, eps=1e-6), irgen.softmax(512, 4096),
+                   irgen.l2norm(512, 4096)):
+            spec = _spec(gm, "r")
+            ins = {"x": x}
+            if "w" in spec.args:
+                ins["w"] = g
+            out.append((spec, ins, 8 * x.size))
+        return "RMSNorm, softmax, L2-norm on 512x4096 f32", out
+    raise ValueError(workload)
+
+
+def cpu_baseline(workload: str, budget_s: float = 20.0):
+    from oracle.interp import interpret, make_inputs
+    desc, sample = _oracle_sample(workload)
+    t0 = time.perf_counter()
+    nbytes = 0
+    reps = 0
+    while True:
+        for spec, ins, nb in sample:
+            full = make_inputs(spec)
+            full.update(ins)
+            interpret(spec, full)
+            nbytes += nb
+        reps += 1
+        if time.perf_counter() - t0 > budget_s / 4 or reps >= 4:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{desc}; {reps} pass(es) in {dt:.1f} s, single-threaded numpy oracle"}
+
+
+def run_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return None
+    from oracle.interp import interpret, make_inputs
+    desc, sample = _oracle_sample(args.workload)
+    times = []
+    nbytes = sum(nb for _, _, nb in sample)
+    for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        for spec, ins, nb in sample:
+            full = make_inputs(spec)
+            full.update(ins)
+            interpret(spec, full)
+        if s >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = nbytes / (ms * 1e-3) / 1e9
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+        "config": {"workload": args.workload, "sample": desc},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="reductions", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, dist)
+        else:
+            line = run_ours(args, dist)
+        if dist.rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

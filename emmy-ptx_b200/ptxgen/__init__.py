@@ -1,0 +1,19 @@
+"""ptxgen: Emmy Kernel IR -> sm_100a PTX for NVIDIA B200.
+
+Same public names as the reference package (``ptxgen/__init__.py:3-7``)
+except ``interpret``: the CPU golden model is test infrastructure here
+(``oracle/``), and the product's way to *run* a kernel is ``run_kernel``,
+which executes it on the GPU through ``libemmyrt.so``.
+"""
+
+from .loader import load_kernel
+from .emit import compile_file, compile_kernel
+
+
+def run_kernel(spec, inputs, **kw):
+    """Compile ``spec``, run it on the local B200 and return its outputs."""
+    from .runtime import run_kernel as _run
+    return _run(spec, inputs, **kw)
+
+
+__all__ = ["load_kernel", "compile_kernel", "compile_file", "run_kernel"]

@@ -1,0 +1,49 @@
+"""The IR generator reproduces the reference's shipped problems byte for byte
+(graph, kernel body and launch contract), which pins the IR it writes at the
+benchmark shapes to the reference's schedules."""
+
+import json
+from pathlib import Path
+
+import pytest
+
+from ptxgen import irgen
+
+GOLDEN = Path(__file__).parent / "golden" / "problems"
+
+CASES = {
+    "p00_scalar_add": lambda: irgen.pointwise(128, 2, "add"),
+    "p01_vector_add": lambda: irgen.pointwise(1024, 2, "add"),
+    "p02_scale_shift": lambda: irgen.pointwise(4096, 4, "scale_shift",
+                                               constants=[("mul_c1", 2.0), ("add_c1", 1.0)]),
+    "p03_relu_mul": lambda: irgen.pointwise(2048, 4, "relu_mul", out="mul", entry="k_mul_pointwise"),
+    "r01_array_sum": lambda: irgen.reduce_full(1024),
+    "r02_big_sum": lambda: irgen.reduce_full(65536),
+    "r03_mean": lambda: irgen.reduce_full(32768, mean=True),
+    "r04_row_sum": lambda: irgen.reduce_rows(64, 512),
+    "f01_rmsnorm": lambda: irgen.rmsnorm(64, 1024),
+    "f02_row_softmax": lambda: irgen.softmax(64, 256),
+    "f03_l2norm": lambda: irgen.l2norm(64, 512),
+    "m01_matmul_512": lambda: irgen.matmul(512, 512, 512),
+    "m02_matmul_rect": lambda: irgen.matmul_splitk(128, 64, 256, slice_k=8),
+    "a02_attention_128": lambda: irgen.attention(128, 32, 5.656854),
+}
+
+
+@pytest.mark.parametrize("prob", sorted(CASES))
+def test_generated_equals_shipped(prob):
+    g, m = CASES[prob]()
+    ref_graph = json.loads(next((GOLDEN / prob).glob("*.ir.json")).read_text())
+    ref_meta = json.loads((GOLDEN / prob / "meta.json").read_text())
+    assert g == ref_graph
+    k0, k1 = ref_meta["kernels"][0], m["kernels"][0]
+    for key in ("entry", "arg_order", "grid", "block", "smem_bytes", "zero_outputs", "args"):
+        assert k0[key] == k1[key], key
+
+
+def test_bench_kernels_parse():
+    from ptxgen.loader import load_kernel_data
+    for name, fn in irgen.bench_kernels().items():
+        g, m = fn()
+        spec = load_kernel_data(g, m, name)
+        assert spec.entry
