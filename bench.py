@@ -161,55 +161,89 @@ WORKLOADS = {"reductions": workload_reductions, "pointwise": workload_pointwise,
 # ---------------------------------------------------------------------------
 
 
+def _nvml_handle(N, cuda_index: int):
+    """NVML handle of CUDA device ``cuda_index``: NVML ignores
+    CUDA_VISIBLE_DEVICES, so map through it (indices or UUIDs)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        items = [v.strip() for v in vis.split(",") if v.strip()]
+        if cuda_index < len(items):
+            it = items[cuda_index]
+            if it.isdigit():
+                return N.nvmlDeviceGetHandleByIndex(int(it))
+            return N.nvmlDeviceGetHandleByUUID(it)
+    return N.nvmlDeviceGetHandleByIndex(cuda_index)
+
+
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and throttle reasons while the timed region
+    runs: NVML polled every millisecond from a thread (read-only queries);
+    nvidia-smi as a fallback."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
+        self.samples = []
+        self.smax = None
+        self._stop = False
+        self.error = None
+
+    def _poll(self):
+        try:
+            import pynvml as N
+            h = _nvml_handle(N, self.index)
+            self.smax = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(N, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        except Exception as exc:  # noqa: BLE001
+            self.error = f"{type(exc).__name__}: {exc}"
+            return
+        while not self._stop:
+            try:
+                mhz = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                reasons = get_reasons(h)
+                self.samples.append((mhz, reasons, 0))
+            except Exception as exc:  # noqa: BLE001
+                self.error = f"{type(exc).__name__}: {exc}"
+            time.sleep(0.0005)
 
     def __enter__(self):
+        import threading
+        self.thread = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+            import pynvml as N
+            N.nvmlInit()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            t0 = time.perf_counter()
+            while not self.samples and self.error is None and time.perf_counter() - t0 < 5:
+                time.sleep(0.001)
+        except Exception:
+            self.thread = None
+        self.first = 0
         return self
 
+    def mark(self):
+        """Samples from here on belong to the timed region."""
+        self.first = len(self.samples)
+
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        self._stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], 0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = max(smax, float(f[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": smax or None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": [], "samples": 0,
+                    "source": "nvml", "error": self.error}
+        window = self.samples[self.first:] or self.samples[-1:]
+        mhz = [m for m, _, _ in window]
+        reasons = sorted({n for _, r, _ in window for n, bit in self.REASONS.items()
+                          if r & bit})
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.smax, "reasons": reasons,
+                "samples": len(mhz), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -295,6 +329,12 @@ def run_ours(args, dist: Dist):
     for _ in range(args.warmup):
         step()
     dev.sync()
+    # untimed ramp: keep the GPU busy ~0.3 s so it leaves idle clocks
+    t_ramp = time.perf_counter()
+    while time.perf_counter() - t_ramp < 0.3:
+        for _ in range(16):
+            step()
+        dev.sync()
     for j in jobs:
         j.pk.check_errors()
         if j.check is not None and dist.world == 1:
@@ -305,6 +345,9 @@ def run_ours(args, dist: Dist):
     dist.barrier()
     dev.sync()
     with ClockSampler(dist.local) as clk:
+        for _ in range(8):  # re-warm after the idle gap of the set-up above
+            step()
+        clk.mark()
         dev.record(t0)
         for s in range(args.steps):
             step(evs[s])

@@ -334,9 +334,21 @@ class Lowerer:
         k(f"{opc} {r}, {a.reg}, {b.reg}")
         return Val(r, kind)
 
+    exp_mode = "fast"
+
     def exp_f32(self, x: str) -> str:
-        """exp(x) for an f32 register; returns the result register."""
+        """exp(x) for an f32 register; returns the result register.
+
+        ``fast``: ex2.approx(x * log2 e): relative error about 2^-22 from
+        ex2 plus |x| * 2^-24 * ln 2 from rounding the product (6e-7 at
+        |x| = 10).  ``accurate``: the product's rounding error, and the tail
+        of log2 e, are carried as a first-order correction (about 2 ulp)."""
         k = self.k
+        if self.exp_mode == "fast":
+            t, y = k.reg("f32"), k.reg("f32")
+            k(f"mul.rn.f32 {t}, {x}, {f32_hex(L2E_HI)}")
+            k(f"ex2.approx.ftz.f32 {y}, {t}")
+            return y
         t, e, p, q, y = (k.reg("f32") for _ in range(5))
         k(f"mul.rn.f32 {t}, {x}, {f32_hex(L2E_HI)}")
         k(f"neg.f32 {e}, {t}")

@@ -113,6 +113,37 @@ def _vec_ok(spec: KernelSpec, bufs, n_elems: int) -> int:
     return 4 if n_elems % 4 == 0 else 1
 
 
+def grid_stride(k: Kernel, start: str, stride: str, count: int, process, unroll: int = 4):
+    """``for i = start; i < count; i += stride`` with ``unroll`` indices
+    handed to ``process`` at once while all are in range (so their loads are
+    in flight together), then one at a time."""
+    i = k.reg("u32")
+    last = k.reg("u32")
+    p = k.reg("pred")
+    k(f"mov.u32 {i}, {start}")
+    lu, l1, done = k.label("gsu"), k.label("gs1"), k.label("gsdone")
+    if unroll > 1:
+        k.place(lu)
+        k(f"mad.lo.u32 {last}, {stride}, {unroll - 1}, {i}")
+        k(f"setp.ge.u32 {p}, {last}, {count}")
+        k(f"@{p} bra {l1}")
+        idx = [i]
+        for u in range(1, unroll):
+            r = k.reg("u32")
+            k(f"mad.lo.u32 {r}, {stride}, {u}, {i}")
+            idx.append(r)
+        process(idx)
+        k(f"mad.lo.u32 {i}, {stride}, {unroll}, {i}")
+        k(f"bra.uni {lu}")
+    k.place(l1)
+    k(f"setp.ge.u32 {p}, {i}, {count}")
+    k(f"@{p} bra {done}")
+    process([i])
+    k(f"add.u32 {i}, {i}, {stride}")
+    k(f"bra.uni {l1}")
+    k.place(done)
+
+
 # ---------------------------------------------------------------------------
 # pointwise
 # ---------------------------------------------------------------------------
@@ -347,24 +378,7 @@ def emit_pointwise(spec: KernelSpec, plan: PointwisePlan) -> Module:
             else:
                 _store_scalar(lo, a, out_dt, outs[0])
 
-    # two vectors per iteration while both are in range, then one
-    i = k.reg("u32")
-    i2 = k.reg("u32")
-    p = k.reg("pred")
-    k(f"mov.u32 {i}, {gid}")
-    l2, l1, done = k.label("pw2"), k.label("pw1"), k.label("pwtail")
-    k.place(l2)
-    k(f"add.u32 {i2}, {i}, {stride}")
-    k(f"setp.ge.u32 {p}, {i2}, {nvec}")
-    k(f"@{p} bra {l1}")
-    process([i, i2])
-    k(f"add.u32 {i}, {i2}, {stride}")
-    k(f"bra.uni {l2}")
-    k.place(l1)
-    k(f"setp.ge.u32 {p}, {i}, {nvec}")
-    k(f"@{p} bra {done}")
-    process([i])
-    k.place(done)
+    grid_stride(k, gid, stride, nvec, process, unroll=4)
     tail = n - nvec * vec
     if tail:
         raise NoMatch("tail of a vectorised pointwise")  # vec==4 implies n % 4 == 0
@@ -679,23 +693,7 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
                 lo.run(lb.loop.body)
                 lo.load_hook = saved
 
-    i, i2 = k.reg("u32"), k.reg("u32")
-    k(f"mov.u32 {i}, {gid}")
-    l2, l1, done = k.label("r2"), k.label("r1"), k.label("rdone")
-    k.place(l2)
-    k(f"add.u32 {i2}, {i}, {stride}")
-    k(f"setp.ge.u32 {p}, {i2}, {nvec}")
-    k(f"@{p} bra {l1}")
-    run_elements([i, i2])
-    k(f"add.u32 {i}, {i2}, {stride}")
-    k(f"bra.uni {l2}")
-    k.place(l1)
-    k(f"setp.ge.u32 {p}, {i}, {nvec}")
-    k(f"@{p} bra {done}")
-    run_elements([i])
-    k(f"add.u32 {i}, {i}, {stride}")
-    k(f"bra.uni {l1}")
-    k.place(done)
+    grid_stride(k, gid, stride, nvec, run_elements, unroll=4)
 
     _block_combine(lo, k, ws, "red_slots", None, ident)
 
