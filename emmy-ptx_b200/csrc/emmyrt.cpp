@@ -242,6 +242,10 @@ struct emmy_comm {
   ncclComm_t comm;
 };
 
+// Lets other translation units of this library set the message
+// emmy_last_error() returns; hidden, so it is not part of the C ABI.
+__attribute__((visibility("hidden"))) void emmyrt_set_last_error(const char *msg) { g_err = msg; }
+
 extern "C" {
 
 const char *emmy_version(void) { return "emmyrt 1.0 (sm_100a)"; }

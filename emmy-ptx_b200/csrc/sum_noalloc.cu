@@ -1,0 +1,174 @@
+// emmy_sum_f32_noalloc -- a full-array f32 sum that allocates no memory.
+//
+// Why it exists: some callers of this library cannot call cudaMalloc at the
+// point where they need a reduction -- plugin hosts whose enqueue callback
+// must not allocate (the host framework owns all device memory through its
+// own pool), and latency-critical loops where cudaMalloc's implicit
+// device-wide synchronisation would stall every other stream.  The regular
+// path (the compiled IR kernel of the full-reduction family) keeps its
+// per-CTA partials in module scratch that the driver allocates when the PTX
+// module is loaded.  This variant needs no module load and no allocation:
+// its scratch is the file-scope array below, which every GPU that loads
+// libemmyrt.so holds until the process exits.
+//
+// Limits and sharing rules:
+//   - scratch: NOALLOC_SLOTS (1024) per-CTA partial sums plus one ticket
+//     word, 4.25 KiB per device; the grid is clamped to NOALLOC_SLOTS CTAs,
+//     so the scratch can never overflow;
+//   - n: at most NOALLOC_MAX_ELEMS (2^31 - 1) elements (32-bit indexing);
+//     larger n is rejected with EMMY_EINVAL and a message;
+//   - every call on a device shares the one array and it keeps the previous
+//     call's contents, so each call clears the ticket word (stream-ordered
+//     cudaMemsetAsync) before its kernel; calls that overlap on the GPU
+//     (for example on two streams at once) race on the scratch and must be
+//     serialised by the caller;
+//   - the first call on each device performs the set-up: with that device
+//     current it resolves the device address of the array with
+//     cudaGetSymbolAddress (checked) and caches it; make that first call
+//     before any stream capture.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "emmyrt.h"
+
+// Sets the thread-local message emmy_last_error() returns (emmyrt.cpp; not
+// exported from the library).
+void emmyrt_set_last_error(const char *msg);
+
+namespace {
+
+constexpr int NOALLOC_SLOTS = 1024;           // per-CTA partials
+constexpr int NOALLOC_TICKET_WORD = 0;        // word 0: arrival ticket
+constexpr int NOALLOC_PARTIAL_WORD = 64;      // partials start on their own 256-byte line
+constexpr int NOALLOC_WORDS = NOALLOC_PARTIAL_WORD + NOALLOC_SLOTS;
+constexpr size_t NOALLOC_MAX_ELEMS = 0x7fffffffu;
+constexpr int NOALLOC_THREADS = 512;
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+// The only memory this entry point uses beyond the caller's buffers.
+static __device__ __align__(256) unsigned int g_noalloc_scratch[NOALLOC_WORDS];
+
+std::mutex g_setup_mu;
+unsigned int *g_scratch_addr[NOALLOC_MAX_DEVICES] = {};
+
+__device__ __forceinline__ float warp_sum(float v) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Block-wide sum; every thread receives the result.
+__device__ float block_sum(float v, float *slots) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) slots[warp] = v;
+  __syncthreads();
+  const int nwarps = (blockDim.x + 31) >> 5;
+  v = lane < nwarps ? slots[lane] : 0.0f;
+  v = warp_sum(v);
+  __syncthreads();  // slots may be reused by the caller
+  return v;
+}
+
+__global__ void __launch_bounds__(NOALLOC_THREADS)
+sum_noalloc_kernel(const float *__restrict__ x, uint32_t n, float *__restrict__ out,
+                   unsigned int *scratch) {
+  __shared__ float slots[32];
+  __shared__ unsigned int is_last;
+  float acc = 0.0f;
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t nvec = n / 4;
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  uint32_t i = tid;
+  // four 16-byte loads in flight per thread, then the remainder
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    float4 a = __ldcs(x4 + i), b = __ldcs(x4 + i + stride);
+    float4 c = __ldcs(x4 + i + 2 * stride), d = __ldcs(x4 + i + 3 * stride);
+    acc += ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+    acc += ((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w));
+  }
+  for (; i < nvec; i += stride) {
+    float4 a = __ldcs(x4 + i);
+    acc += (a.x + a.y) + (a.z + a.w);
+  }
+  for (uint32_t j = nvec * 4 + tid; j < n; j += stride) acc += x[j];
+  acc = block_sum(acc, slots);
+
+  float *partials = reinterpret_cast<float *>(scratch + NOALLOC_PARTIAL_WORD);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = acc;
+    __threadfence();
+    const unsigned int ticket = atomicAdd(scratch + NOALLOC_TICKET_WORD, 1u);
+    is_last = (ticket == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // The last CTA folds the partials in a fixed order, so the result does not
+  // depend on which CTA finished last.
+  float total = 0.0f;
+  for (uint32_t j = threadIdx.x; j < gridDim.x; j += blockDim.x) total += __ldcg(partials + j);
+  total = block_sum(total, slots);
+  if (threadIdx.x == 0) {
+    *out = total;
+    scratch[NOALLOC_TICKET_WORD] = 0u;  // leave the ticket clear for the next call
+  }
+}
+
+int set_error(int code, const char *msg) {
+  char buf[256];
+  snprintf(buf, sizeof buf, "emmy_sum_f32_noalloc: %s", msg);
+  emmyrt_set_last_error(buf);
+  return code;
+}
+
+// Device address of the scratch array for the current device (set-up on the
+// first call per device).
+int scratch_for_current_device(unsigned int **out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return set_error(EMMY_EINVAL, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+    g_scratch_addr[dev] = static_cast<unsigned int *>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return EMMY_OK;
+}
+
+}  // namespace
+
+extern "C" int emmy_sum_f32_noalloc(emmy_dptr x, size_t n, emmy_dptr out, emmy_stream stream) {
+  if (x == 0 || out == 0) return set_error(EMMY_EINVAL, "null buffer");
+  if (n == 0 || n > NOALLOC_MAX_ELEMS)
+    return set_error(EMMY_EINVAL, "n must be between 1 and 2^31 - 1 elements");
+  if (x % 16 != 0) return set_error(EMMY_EINVAL, "x must be 16-byte aligned");
+  unsigned int *scratch = nullptr;
+  int rc = scratch_for_current_device(&scratch);
+  if (rc != EMMY_OK) return rc;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  const size_t nvec = (n + 3) / 4;
+  size_t grid = (nvec + NOALLOC_THREADS * 8 - 1) / (NOALLOC_THREADS * 8);
+  if (grid > size_t(sms) * 4) grid = size_t(sms) * 4;
+  if (grid > size_t(NOALLOC_SLOTS)) grid = NOALLOC_SLOTS;
+  if (grid < 1) grid = 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the ticket must start at zero; the partials are overwritten before use
+  e = cudaMemsetAsync(scratch + NOALLOC_TICKET_WORD, 0, sizeof(unsigned int), s);
+  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  sum_noalloc_kernel<<<unsigned(grid), NOALLOC_THREADS, 0, s>>>(
+      reinterpret_cast<const float *>(x), uint32_t(n), reinterpret_cast<float *>(out), scratch);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  return EMMY_OK;
+}

@@ -144,6 +144,22 @@ int emmy_nccl_async_error(emmy_comm *comm, int *nccl_result);
 int emmy_nccl_abort(emmy_comm *comm);
 int emmy_nccl_destroy(emmy_comm *comm);
 
+/* ---- full f32 sum without any allocation ----
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc
+ * where they need the reduction: plugin hosts whose enqueue callback must
+ * not allocate because the host framework owns all device memory, and
+ * latency-critical loops where cudaMalloc's implicit device-wide
+ * synchronisation would stall other streams.  *out = sum of the n f32 at x
+ * (x 16-byte aligned, 1 <= n <= 2^31 - 1, else EMMY_EINVAL), on `stream`
+ * (the CUDA runtime's current device).  It allocates nothing: its scratch is
+ * a 4.25 KiB file-scope device array (1024 per-CTA partials + a ticket) held
+ * by every GPU that loads this library until exit.  The first call on a
+ * device resolves that array's address (cudaGetSymbolAddress) -- make it
+ * before any stream capture.  All calls on a device share the array and
+ * each clears the ticket first; calls that overlap on the GPU race and must
+ * be serialised by the caller. */
+int emmy_sum_f32_noalloc(emmy_dptr x, size_t n, emmy_dptr out, emmy_stream stream);
+
 #ifdef __cplusplus
 }
 #endif
