@@ -323,6 +323,8 @@ class PreparedKernel:
             self.grid, self.block, self.smem = meta_geometry(spec)
         else:
             self.grid, self.block, self.smem = plan_geometry(self.plan, self.dev)
+        self.geometry = geometry
+        self.ws = 0
         self.bufs: dict[str, int] = {}
         for name in spec.arg_order:
             a = spec.args[name]
@@ -336,13 +338,26 @@ class PreparedKernel:
             elif a.data is not None:
                 self.dev.htod(self.bufs[name], np.asarray(a.data, np.float64).astype(
                     _np_dtype(a.dtype)).reshape(a.shape))
-        self._fill_tmaps()
+        if geometry != "meta":
+            self._fill_tmaps()
         self.launches = 0
 
     def _fill_tmaps(self) -> None:
+        """Workspace, tensor maps, then the flags that tell the kernel its
+        plan (tensor maps, block size, shared memory) is in place."""
+        w = self.plan.get("workspace")
+        if w:
+            self.ws = self.dev.alloc(int(w["bytes"]))
+            ptr, _ = self.mod.global_ptr(w["sym"])
+            self.dev.htod(ptr, np.array([self.ws], dtype=np.uint64))
         for t in self.plan.get("tmaps", []):
-            self.mod.fill_tmap(t["sym"], self.bufs[t["buf"]] + int(t.get("offset", 0)),
+            base = self.ws if t["buf"] == "@ws" else self.bufs[t["buf"]]
+            self.mod.fill_tmap(t["sym"], base + int(t.get("offset", 0)),
                                t["dtype"], t["dims"], t["strides"], t["box"], t["swizzle"])
+        for f in self.plan.get("flags", []):
+            ptr, size = self.mod.global_ptr(f["sym"])
+            self.dev.htod(ptr, np.array([int(f["value"])], dtype=np.uint32))
+        self.dev.sync()
 
     def upload(self, inputs: dict[str, np.ndarray], stream=None) -> int:
         nbytes = 0
@@ -362,6 +377,11 @@ class PreparedKernel:
             a = self.spec.args[name]
             self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4, stream)
         ptrs = [self.bufs[n] for n in self.spec.arg_order]
+        if self.geometry != "meta":
+            for pre in self.plan.get("pre", []):
+                g, b, sm = plan_geometry(pre, self.dev)
+                self.mod.launch(pre["entry"], g, b, sm, ptrs, stream)
+                self.launches += 1
         self.mod.launch(self.spec.entry, self.grid, self.block, self.smem, ptrs, stream)
         self.launches += 1
 
@@ -385,6 +405,9 @@ class PreparedKernel:
         for p in self.bufs.values():
             self.dev.free(p)
         self.bufs = {}
+        if self.ws:
+            self.dev.free(self.ws)
+            self.ws = 0
 
 
 def _np_dtype(dtype) -> np.dtype:

@@ -1,0 +1,106 @@
+"""GPU parity for the tcgen05 3xTF32 matmul template (m01/m02 family).
+
+* plan launch (tcgen05 + TMA path) against the oracle and ``expected.npz``;
+* meta.json launch (the SIMT path every other launch takes): bit for bit
+  with the oracle for m01, whose IR sums K in order with one rounding per op;
+* generated shapes and the BASELINE shapes against float64 numpy with the
+  condition-aware bound |got - ref| <= 1e-4 * sum_k |a_ik| |b_kj|
+  (fp32 contractions, 1e-4 relative).
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.interp import interpret, make_inputs
+from ptxgen import irgen
+from ptxgen.loader import load_kernel, load_kernel_data
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden" / "problems"
+TOL = 1e-4
+
+
+def _run(spec, inputs, geometry="plan"):
+    from ptxgen.runtime import run_kernel
+    return run_kernel(spec, {k: v.copy() for k, v in inputs.items()}, geometry=geometry)
+
+
+def _bound_ok(got, a, b, rows=None):
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    if rows is not None:
+        a64 = a64[rows]
+        got = got[rows]
+    ref = a64 @ b64
+    scale = np.abs(a64) @ np.abs(b64)
+    err = np.abs(got.astype(np.float64) - ref)
+    return bool(np.all(err <= TOL * scale + 1e-30)), float(np.max(err / (scale + 1e-30)))
+
+
+@pytest.mark.parametrize("prob", ["m01_matmul_512", "m02_matmul_rect"])
+def test_problem_plan(prob):
+    pdir = GOLDEN / prob
+    meta = json.loads((pdir / "meta.json").read_text())
+    spec = load_kernel(next(pdir.glob("*.ir.json")))
+    inputs = make_inputs(spec)
+    got = _run(spec, inputs)["matmul"]
+    ok, rel = _bound_ok(got, inputs["x0"], inputs["x1"])
+    assert ok, rel
+    exp = np.load(pdir / "expected.npz")["matmul"]
+    assert np.allclose(got, exp, rtol=meta["rtol"], atol=meta["atol"])
+
+
+def test_m01_meta_geometry_bitexact():
+    spec = load_kernel(next((GOLDEN / "m01_matmul_512").glob("*.ir.json")))
+    inputs = make_inputs(spec)
+    want = interpret(spec, {k: v.copy() for k, v in inputs.items()})["matmul"]
+    got = _run(spec, inputs, geometry="meta")["matmul"]
+    assert np.array_equal(got, want)
+
+
+def test_m02_meta_geometry():
+    spec = load_kernel(next((GOLDEN / "m02_matmul_rect").glob("*.ir.json")))
+    inputs = make_inputs(spec)
+    want = interpret(spec, {k: v.copy() for k, v in inputs.items()})["matmul"]
+    got = _run(spec, inputs, geometry="meta")["matmul"]
+    assert np.allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 256), (384, 192, 512), (128, 64, 1024)])
+def test_matmul_generated(m, n, k):
+    spec = load_kernel_data(*irgen.matmul(m, n, k), "mm")
+    rng = np.random.default_rng(m + n + k)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    ok, rel = _bound_ok(got, a, b)
+    assert ok, rel
+
+
+def test_splitk_generated():
+    spec = load_kernel_data(*irgen.matmul_splitk(256, 256, 1024, slice_k=128), "sk")
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((256, 1024)).astype(np.float32)
+    b = rng.standard_normal((1024, 256)).astype(np.float32)
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    ok, rel = _bound_ok(got, a, b)
+    assert ok, rel
+
+
+@pytest.mark.parametrize("shape", ["square", "splitk8"])
+def test_baseline_shapes_sampled(shape):
+    if shape == "square":
+        m = n = k = 8192
+        spec = load_kernel_data(*irgen.matmul(m, n, k), "sq")
+    else:
+        m, n, k = 16384, 4096, 1024
+        spec = load_kernel_data(*irgen.matmul_splitk(m, n, k, slice_k=128), "sk8")
+    rng = np.random.default_rng(1)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    rows = np.random.default_rng(2).choice(m, 64, replace=False)
+    ok, rel = _bound_ok(got, a, b, rows)
+    assert ok, rel
