@@ -372,18 +372,31 @@ class PreparedKernel:
             nbytes += host.nbytes
         return nbytes
 
-    def launch(self, stream=None) -> None:
+    @property
+    def has_pre(self) -> bool:
+        return self.geometry != "meta" and bool(self.plan.get("pre"))
+
+    def launch_pre(self, stream=None) -> None:
+        """The plan's preparatory launches (operand splitting), if any."""
+        if self.geometry == "meta":
+            return
+        ptrs = [self.bufs[n] for n in self.spec.arg_order]
+        for pre in self.plan.get("pre", []):
+            g, b, sm = plan_geometry(pre, self.dev)
+            self.mod.launch(pre["entry"], g, b, sm, ptrs, stream)
+            self.launches += 1
+
+    def launch_main(self, stream=None) -> None:
         for name in self.spec.zero_outputs:
             a = self.spec.args[name]
             self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4, stream)
         ptrs = [self.bufs[n] for n in self.spec.arg_order]
-        if self.geometry != "meta":
-            for pre in self.plan.get("pre", []):
-                g, b, sm = plan_geometry(pre, self.dev)
-                self.mod.launch(pre["entry"], g, b, sm, ptrs, stream)
-                self.launches += 1
         self.mod.launch(self.spec.entry, self.grid, self.block, self.smem, ptrs, stream)
         self.launches += 1
+
+    def launch(self, stream=None) -> None:
+        self.launch_pre(stream)
+        self.launch_main(stream)
 
     def download(self, names=None, stream=None) -> dict[str, np.ndarray]:
         out = {}
