@@ -1,0 +1,89 @@
+"""GPU parity for the fused attention template (a01/a02 family, [B,H,S,D]).
+
+* shipped problems against the oracle and ``expected.npz`` under the plan
+  launch (tensor cores where the shape tiles, a02) and meta.json's launch
+  (the SIMT path that follows the IR per key);
+* generated [B, H, S, D] shapes, f32 (3xTF32, |err| <= 1e-4 of the output
+  scale) and bf16 (bf16 output, |err| <= 2e-2 of the scale), against float64
+  numpy;
+* the BASELINE shape [16, 32, 4096, 128] on sampled (batch, head) pairs.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.interp import interpret, make_inputs
+from ptxgen import irgen
+from ptxgen.loader import load_kernel, load_kernel_data
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden" / "problems"
+
+
+def _run(spec, inputs, geometry="plan"):
+    from ptxgen.runtime import run_kernel
+    return run_kernel(spec, {k: v.copy() for k, v in inputs.items()}, geometry=geometry)
+
+
+def _ref(q, k, v):
+    q, k, v = (x.astype(np.float64) for x in (q, k, v))
+    s = q @ np.swapaxes(k, -1, -2) / np.sqrt(q.shape[-1])
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return p @ v
+
+
+@pytest.mark.parametrize("geometry", ["plan", "meta"])
+@pytest.mark.parametrize("prob", ["a01_attention", "a02_attention_128"])
+def test_problem(prob, geometry):
+    pdir = GOLDEN / prob
+    meta = json.loads((pdir / "meta.json").read_text())
+    spec = load_kernel(next(pdir.glob("*.ir.json")))
+    inputs = make_inputs(spec)
+    want = interpret(spec, {k: v.copy() for k, v in inputs.items()})["matmul_1"]
+    got = _run(spec, inputs, geometry)["matmul_1"]
+    assert np.allclose(got, want, rtol=1e-4, atol=1e-5), float(np.abs(got - want).max())
+    exp = np.load(pdir / "expected.npz")["matmul_1"]
+    assert np.allclose(got, exp, rtol=meta["rtol"], atol=meta["atol"])
+
+
+def _bhsd(b, h, s, d, dtype, seed=0):
+    rng = np.random.default_rng(seed)
+    if dtype == "bf16":
+        from ml_dtypes import bfloat16
+        mk = lambda: rng.standard_normal((b, h, s, d)).astype(bfloat16)  # noqa: E731
+    else:
+        mk = lambda: rng.standard_normal((b, h, s, d)).astype(np.float32)  # noqa: E731
+    return mk(), mk(), mk()
+
+
+@pytest.mark.parametrize("dtype,shape", [("f32", (2, 2, 256, 64)), ("f32", (1, 3, 384, 128)),
+                                         ("bf16", (2, 2, 256, 128)), ("bf16", (1, 2, 512, 64))])
+def test_generated(dtype, shape):
+    b, h, s, d = shape
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "att")
+    q, k, v = _bhsd(b, h, s, d, dtype)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
+    ref = _ref(q, k, v)
+    scale = np.abs(ref).max()
+    tol = 1e-4 if dtype == "f32" else 2e-2
+    assert np.abs(out - ref).max() <= tol * scale, float(np.abs(out - ref).max() / scale)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_baseline_shape_sampled(dtype):
+    b, h, s, d = 16, 32, 4096, 128
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "attbig")
+    q, k, v = _bhsd(b, h, s, d, dtype, seed=3)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"]
+    tol = 1e-4 if dtype == "f32" else 2e-2
+    for (bi, hi) in ((0, 0), (7, 19), (15, 31)):
+        rows = np.arange(0, s, 97)
+        qq = q[bi, hi, rows]
+        ref = _ref(qq, k[bi, hi], v[bi, hi])
+        got = out[bi, hi, rows].astype(np.float64)
+        assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
