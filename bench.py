@@ -179,8 +179,41 @@ def workload_matmul(rank: int, world: int):
                   "rows_per_rank": "M rows sharded, B replicated"}
 
 
+def workload_attention(rank: int, world: int):
+    from ptxgen import irgen
+    from ml_dtypes import bfloat16
+    b, h, s, d = 16, 32, 4096, 128
+    rng = np.random.default_rng(5000 + rank)
+    jobs = []
+    for dt in ("f32", "bf16"):
+        spec = _spec(irgen.attention_bhsd(b, h, s, d, dt, pid=f"attn_{dt}"), f"attn_{dt}")
+        npdt = np.float32 if dt == "f32" else bfloat16
+        q, k, v = (rng.standard_normal((b, h, s, d), dtype=np.float32).astype(npdt)
+                   for _ in range(3))
+
+        def chk(out, q=q, k=k, v=v, dt=dt):
+            bi, hi = 3, 17
+            rows = np.arange(0, s, 257)
+            qq, kk, vv = (x[bi, hi].astype(np.float64) for x in (q, k, v))
+            sc = qq[rows] @ kk.T / np.sqrt(d)
+            sc -= sc.max(-1, keepdims=True)
+            pp = np.exp(sc)
+            ref = (pp / pp.sum(-1, keepdims=True)) @ vv
+            got = out["out"][bi, hi, rows].astype(np.float64)
+            tol = 1e-4 if dt == "f32" else 2e-2
+            if np.abs(got - ref).max() > tol * np.abs(ref).max():
+                raise AssertionError(f"attention {dt} outside tolerance")
+
+        e = 4 if dt == "f32" else 2
+        jobs.append(Job(f"attention_{dt}", spec, {"q": q, "k": k, "v": v}, 4 * b * h * s * d * e,
+                        algo_flops=4.0 * b * h * s * s * d, check=chk))
+    return jobs, {"workload": "configs[4] attention softmax(QK^T/sqrt(d))V, [16,32,4096,128] "
+                              "f32 (3xTF32) and bf16, non-causal",
+                  "heads_per_rank": b * h}
+
+
 WORKLOADS = {"reductions": workload_reductions, "pointwise": workload_pointwise,
-             "rows": workload_rows, "matmul": workload_matmul}
+             "rows": workload_rows, "matmul": workload_matmul, "attention": workload_attention}
 
 
 # ---------------------------------------------------------------------------
@@ -407,8 +440,9 @@ def run_ours(args, dist: Dist):
             view = np.ctypeslib.as_array((C.c_char * arr.nbytes).from_address(p))
             view[:] = np.frombuffer(np.ascontiguousarray(arr).tobytes(), dtype=np.uint8).view("S1")
             pinned[key] = (p, arr.nbytes)
-    out_host = {j.key: {o: np.empty(j.spec.args[o].shape, np.float32) for o in j.spec.outputs}
-                for j in jobs}
+    from ptxgen.runtime import _np_dtype
+    out_host = {j.key: {o: np.empty(j.spec.args[o].shape, _np_dtype(j.spec.args[o].dtype))
+                        for o in j.spec.outputs} for j in jobs}
 
     def e2e_step():
         nb_in, nb_out = 0, 0
@@ -460,14 +494,19 @@ def run_ours(args, dist: Dist):
         traffic = json.loads(tpath.read_text()).get(f"{args.workload}:{dom.key}")
     if dom.algo_flops:
         achieved = dom.algo_flops / (dom_ms * 1e-3) / 1e12
-        # 3xTF32: three TF32 products per useful f32 product; TF32 runs at half
-        # the dense bf16 rate, so the useful-flop ceiling is bf16 / 2 / 3
-        peak3 = pk["bf16_tflops"] / 6.0
-        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak3, 1),
-                "unit": "TFLOP/s",
-                "peak_note": f"3xTF32 useful-flop ceiling = measured dense bf16 "
-                             f"{pk['bf16_tflops']} / 2 (tf32) / 3 (passes)",
-                "tensor_pipe_tflops_tf32": round(3 * achieved, 1)}
+        if dom.spec.args[dom.spec.outputs[0]].dtype == "bf16":
+            roof = {"bound": "tensor", "achieved": round(achieved, 2),
+                    "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                    "peak_note": "measured dense bf16 (cuBLAS burst)"}
+        else:
+            # 3xTF32: three TF32 products per useful f32 product; TF32 runs at
+            # half the dense bf16 rate, so the useful-flop ceiling is bf16 / 6
+            peak3 = pk["bf16_tflops"] / 6.0
+            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak3, 1),
+                    "unit": "TFLOP/s",
+                    "peak_note": f"3xTF32 useful-flop ceiling = measured dense bf16 "
+                                 f"{pk['bf16_tflops']} / 2 (tf32) / 3 (passes)",
+                    "tensor_pipe_tflops_tf32": round(3 * achieved, 1)}
     else:
         achieved = dom.algo_bytes / (dom_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
@@ -553,11 +592,17 @@ def _oracle_sample(workload: str):
         b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
         out.append((_spec(irgen.matmul(m, n, k), "m"), {"x0": a, "x1": b}, 2.0 * m * n * k))
         return "m01-schedule IR matmul 256^3 (work = 2MNK flops)", out
+    if workload == "attention":
+        b, h, s, d = 1, 2, 64, 64
+        q, k, v = (rng.standard_normal((b, h, s, d), dtype=np.float32) for _ in range(3))
+        out.append((_spec(irgen.attention_bhsd(b, h, s, d, "f32"), "a"), {"q": q, "k": k, "v": v},
+                    4.0 * b * h * s * s * d))
+        return "a02-schedule IR attention [1,2,64,64] f32 (work = 4BHS^2D flops)", out
     raise ValueError(workload)
 
 
 def _sample_unit(workload: str):
-    return ("TFLOP/s", 1e12) if workload == "matmul" else ("GB/s", 1e9)
+    return ("TFLOP/s", 1e12) if workload in ("matmul", "attention") else ("GB/s", 1e9)
 
 
 def cpu_baseline(workload: str, budget_s: float = 20.0):
