@@ -312,40 +312,22 @@ class ClockSampler:
 
 
 class Dist:
+    """This process's place in the job (torch.distributed.run env) and the
+    host-side rendezvous; see ``ptxgen.dist``."""
+
     def __init__(self, gpus: int):
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = None
-        if self.world > 1:
-            import datetime
-            import torch.distributed as td
-            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-            self.td = td
-            self.pg = True
+        from ptxgen.dist import Rendezvous
+        self.rdv = Rendezvous(timeout_s=300)
+        self.rank, self.world, self.local = self.rdv.rank, self.rdv.world, self.rdv.local
 
     def barrier(self):
-        if self.pg:
-            self.td.barrier()
+        self.rdv.barrier()
 
     def max(self, v: float) -> float:
-        if not self.pg:
-            return v
-        import torch
-        t = torch.tensor([v], dtype=torch.float64)
-        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
-        return float(t.item())
-
-    def bcast_bytes(self, b: bytes | None) -> bytes:
-        if not self.pg:
-            return b
-        obj = [b]
-        self.td.broadcast_object_list(obj, src=0)
-        return obj[0]
+        return self.rdv.max(v)
 
     def close(self):
-        if self.pg:
-            self.td.destroy_process_group()
+        self.rdv.close()
 
 
 # ---------------------------------------------------------------------------
@@ -360,21 +342,19 @@ def run_ours(args, dist: Dist):
     dev = Device.get(dist.local)
     comm = None
     if dist.world > 1 and any(j.allreduce for j in jobs):
-        uid = None
-        if dist.rank == 0:
-            buf = C.create_string_buffer(128)
-            check(dev.L.emmy_nccl_unique_id(buf), "nccl id")
-            uid = buf.raw
-        uid = dist.bcast_bytes(uid)
-        comm = C.c_void_p()
-        ubuf = C.create_string_buffer(uid, 128)
-        check(dev.L.emmy_nccl_init(dev.ctx, dist.world, dist.rank, ubuf, C.byref(comm)), "nccl init")
+        from ptxgen.dist import NcclComm
+        comm = NcclComm(dev, dist.rdv)
+        nccl_stream = dev.new_stream()
+        ev_ready, ev_done = dev.event(), dev.event()
     for j in jobs:
         j.pk = PreparedKernel(j.spec, dev=dev)
         j.pk.upload(j.inputs)
     dev.sync()
 
+    last_ar = max((i for i, j in enumerate(jobs) if j.allreduce), default=-1)
+
     def step(events=None):
+        pending = []
         for i, j in enumerate(jobs):
             if j.pk.has_pre:
                 if events is not None:
@@ -386,9 +366,18 @@ def run_ours(args, dist: Dist):
             if events is not None:
                 dev.record(events[i][1])
             if comm is not None and j.allreduce:
-                a = j.spec.args[j.allreduce]
-                check(dev.L.emmy_allreduce_sum_f32(comm, j.pk.bufs[j.allreduce],
-                                                   a.numel, dev.stream), "allreduce")
+                pending.append(j)
+            if pending and i == last_ar:
+                # all-reduce the per-rank results on a second stream, overlapped
+                # with the kernels still to run on the main stream
+                dev.record(ev_ready)
+                dev.wait_event(nccl_stream, ev_ready)
+                for pj in pending:
+                    a = pj.spec.args[pj.allreduce]
+                    comm.allreduce_sum_f32(pj.pk.bufs[pj.allreduce], a.numel, nccl_stream)
+                dev.record(ev_done, nccl_stream)
+        if pending:
+            dev.wait_event(dev.stream, ev_done)
 
     for _ in range(args.warmup):
         step()
@@ -543,7 +532,8 @@ def run_ours(args, dist: Dist):
     for j in jobs:
         j.pk.close()
     if comm is not None:
-        check(dev.L.emmy_nccl_destroy(comm), "nccl destroy")
+        dev.sync(nccl_stream)
+        comm.close()
     return line
 
 

@@ -71,6 +71,7 @@ struct Driver {
   EMMY_FN(cuEventRecord)
   EMMY_FN(cuEventSynchronize)
   EMMY_FN(cuEventElapsedTime)
+  EMMY_FN(cuStreamWaitEvent)
   EMMY_FN(cuGetErrorString)
   EMMY_FN(cuTensorMapEncodeTiled)
 #undef EMMY_FN
@@ -128,6 +129,7 @@ void load_driver() {
   EMMY_LOAD(cuEventRecord, "cuEventRecord")
   EMMY_LOAD(cuEventSynchronize, "cuEventSynchronize")
   EMMY_LOAD(cuEventElapsedTime, "cuEventElapsedTime")
+  EMMY_LOAD(cuStreamWaitEvent, "cuStreamWaitEvent")
   EMMY_LOAD(cuGetErrorString, "cuGetErrorString")
   EMMY_LOAD(cuTensorMapEncodeTiled, "cuTensorMapEncodeTiled")
 #undef EMMY_LOAD
@@ -598,6 +600,13 @@ int emmy_event_elapsed(emmy_event start, emmy_event end, float *ms) {
   CU_TRY(g_drv.cuEventSynchronize(static_cast<CUevent>(end)), "cuEventSynchronize");
   CU_TRY(g_drv.cuEventElapsedTime(ms, static_cast<CUevent>(start), static_cast<CUevent>(end)),
          "cuEventElapsedTime");
+  return EMMY_OK;
+}
+
+int emmy_stream_wait_event(emmy_stream stream, emmy_event ev) {
+  DRV_OR_FAIL();
+  CU_TRY(g_drv.cuStreamWaitEvent(static_cast<CUstream>(stream), static_cast<CUevent>(ev), 0),
+         "cuStreamWaitEvent");
   return EMMY_OK;
 }
 

@@ -83,6 +83,7 @@ def load_library():
         "emmy_event_destroy": (i32, [vp]),
         "emmy_event_record": (i32, [vp, vp]),
         "emmy_event_elapsed": (i32, [vp, vp, C.POINTER(C.c_float)]),
+        "emmy_stream_wait_event": (i32, [vp, vp]),
         "emmy_error_word": (i32, [vp, C.POINTER(u32), i32, vp]),
         "emmy_nccl_unique_id": (i32, [vp]),
         "emmy_nccl_init": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
@@ -216,6 +217,14 @@ class Device:
 
     def record(self, ev, stream=None) -> None:
         check(self.L.emmy_event_record(ev, stream or self.stream), "event record")
+
+    def new_stream(self):
+        s = C.c_void_p()
+        check(self.L.emmy_stream_create(self.ctx, C.byref(s)), "stream create")
+        return s
+
+    def wait_event(self, stream, ev) -> None:
+        check(self.L.emmy_stream_wait_event(stream, ev), "stream wait event")
 
     def elapsed_ms(self, a, b) -> float:
         ms = C.c_float()

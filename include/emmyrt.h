@@ -127,6 +127,9 @@ int emmy_event_create(emmy_ctx *ctx, emmy_event *out);
 int emmy_event_destroy(emmy_event ev);
 int emmy_event_record(emmy_event ev, emmy_stream stream);
 int emmy_event_elapsed(emmy_event start, emmy_event end, float *ms);
+/* Make `stream` wait for `ev` (overlap of NCCL on a second stream with the
+ * next kernels; no counterpart in the single-stream reference runner). */
+int emmy_stream_wait_event(emmy_stream stream, emmy_event ev);
 
 /* ---- kernel error word ---- */
 /* Kernels that can fail (bounded waits that expire, index checks in the
