@@ -61,8 +61,14 @@ def select_template(spec: KernelSpec):
     return None, reasons, None
 
 
-def compile_module(spec: KernelSpec):
-    """Return the ``ptx.Module`` for ``spec`` (plan header included)."""
+def compile_module(spec: KernelSpec, generic: bool = False):
+    """Return the ``ptx.Module`` for ``spec`` (plan header included);
+    ``generic=True`` (or ``EMMY_TEMPLATE=generic``) skips the templates."""
+    if generic or os.environ.get("EMMY_TEMPLATE") == "generic":
+        from . import generic as g
+        mod = g.emit_generic(spec)
+        mod.plan.setdefault("template", "generic")
+        return mod
     name, plan, emit = select_template(spec)
     if name is not None:
         try:
@@ -74,15 +80,17 @@ def compile_module(spec: KernelSpec):
             plan = [f"{name}: {exc}"]
     from . import generic
     try:
-        return generic.emit_generic(spec)
+        mod = generic.emit_generic(spec)
+        mod.plan.setdefault("template", "generic")
+        return mod
     except (NoMatch, LowerError) as exc:
         why = "; ".join(plan) if isinstance(plan, list) else ""
         raise NotImplementedError(f"no template accepts this IR ({why}); generic lowering: {exc}")
 
 
-def compile_kernel(spec: KernelSpec) -> str:
+def compile_kernel(spec: KernelSpec, generic: bool = False) -> str:
     """``KernelSpec`` -> PTX text (``ptxgen/emit.py:1553``)."""
-    return compile_module(spec).render()
+    return compile_module(spec, generic=generic).render()
 
 
 def compile_file(path: str | Path) -> str:

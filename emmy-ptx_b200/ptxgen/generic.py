@@ -1,7 +1,550 @@
-"""Statement-by-statement sm_100a lowering of any Kernel IR (placeholder)."""
+"""Statement-by-statement sm_100a lowering of any Kernel IR.
 
-from .analysis import NoMatch
+The correctness floor behind the templates: any IR in the vocabulary of
+``TASK.md:89-187`` that no template accepts is lowered statement by statement
+under meta.json's launch, with the semantics of the golden model
+(``ptxgen/interp.py``):
+
+* ``Tile``: one cell per thread, ``gid = ctaid * ntid + tid``; lanes with
+  ``gid >= N`` keep running on a clamped cell with every side effect masked
+  off (``interp.py:634-663``), so block-wide barriers and shuffles always see
+  the whole block;
+* ``Cond`` narrows the mask instead of branching (``interp.py:858-864``);
+  loads of masked-off lanes read element 0, register writes of masked-off
+  lanes do not land (predicated moves), stores are predicated;
+* ``Loop``/``StridedLoop`` seed their accumulators (``interp.py:782-856``);
+  a loop whose trip count depends on the thread exits per thread (such a
+  loop may not contain a barrier);
+* ``WarpShuffle`` is an XOR butterfly over ``activemask`` in which an
+  inactive partner yields the caller's own value (``interp.py:868-888``);
+* ``TreeHalve`` is the shared-memory halving tree with a barrier per level
+  and a broadcast of slot 0 (``interp.py:890-926``);
+* ``cp.async`` copies land at once (``interp.py:930-958``): plain 4/8/16-byte
+  loads and shared stores, the commit/wait statements are no-ops and the
+  IR's own ``Sync`` orders them;
+* shared-memory buffers are static, or one dynamic pool when meta.json
+  gives a dynamic size, with the XOR swizzle of ``interp.py:578-586``.
+"""
+
+from __future__ import annotations
+
+from . import ir
+from .analysis import NoMatch, numel
+from .lower import Lowerer, LowerError, Val, storage_kind, value_kind
+from .model import KernelSpec, dtype_info
+from .ptx import Kernel, Module
+
+_PTX_T = {"f32": "f32", "f64": "f64", "s32": "s32", "s64": "s64", "f16": "b16", "bf16": "b16",
+          "pred": "u8"}
+_SWZ = {"B128": (6, 0x7), "B64": (6, 0x3), "B32": (6, 0x1)}
 
 
-def emit_generic(spec):
-    raise NoMatch("generic lowering not available")
+def _collective(body) -> bool:
+    return any(isinstance(s, (ir.Sync, ir.TreeHalve, ir.WarpShuffle)) for s in ir.walk(body))
+
+
+class Generic:
+    def __init__(self, spec: KernelSpec):
+        self.spec = spec
+        self.mod = Module(comment=f"emmy-b200 generic lowering for {spec.entry}")
+        self.mod.add_global(".visible .global .align 4 .u32 emmy_err;")
+        params = []
+        for n in spec.arg_order:
+            a = spec.args[n]
+            if a.scalar:
+                params.append((f"p_{n}", "." + {"f32": "f32", "f64": "f64", "s32": "s32",
+                                                "s64": "s64"}[value_kind(a.dtype)]))
+            else:
+                params.append((f"p_{n}", ".u64"))
+        self.k = Kernel(spec.entry, params)
+        self.lo = Lowerer(self.k)
+        self.lo.load_hook = self.do_load
+        self.lo.write_hook = self.do_write
+        self.lo.extra = {
+            ir.Tile: self.do_tile, ir.Loop: self.do_loop, ir.StridedLoop: self.do_strided,
+            ir.Cond: self.do_cond, ir.Sync: self.do_sync, ir.Smem: lambda st: None,
+            ir.WarpShuffle: self.do_shuffle, ir.TreeHalve: self.do_tree,
+            ir.CpAsyncCopy: self.do_cp_async, ir.CpAsyncCommit: lambda st: None,
+            ir.CpAsyncWait: lambda st: None, ir.Select: self.do_select,
+            ir.ZeroPrologue: self.do_zero_prologue,
+        }
+        self.smem: dict[str, tuple] = {}     # name -> (shape, dtype, offset)
+        self.base: dict[str, str] = {}
+
+    # -- set-up --------------------------------------------------------------
+
+    def layout_smem(self) -> None:
+        decls = [s for s in ir.walk(self.spec.op.body) if isinstance(s, ir.Smem)]
+        off = 0
+        for d in decls:
+            if d.name in self.smem:
+                continue
+            eb = dtype_info(d.dtype)[2]
+            al = max(int(d.align or 0), eb, 4)
+            off = (off + al - 1) // al * al
+            shape = tuple(int(e) for e in d.extents)
+            self.smem[d.name] = (shape, d.dtype, off)
+            off += numel(shape) * eb
+        self.smem_bytes = off
+        k = self.k
+        if not self.smem:
+            return
+        if self.spec.smem_bytes > 0 or off > 48 * 1024:
+            self.mod.add_global(".extern .shared .align 16 .b8 emmy_dyn_smem[];")
+            self.dyn = True
+            r = k.reg("u32")
+            k(f"mov.u32 {r}, emmy_dyn_smem")
+        else:
+            self.dyn = False
+            k.shared(f"\t.shared .align 16 .b8 emmy_smem[{max(16, off)}];")
+            r = k.reg("u32")
+            k(f"mov.u32 {r}, emmy_smem")
+        self.smem_base = r
+
+    def emit(self) -> Module:
+        k, lo, spec = self.k, self.lo, self.spec
+        for n in spec.arg_order:
+            a = spec.args[n]
+            if a.scalar:
+                kind = value_kind(a.dtype)
+                r = k.reg(kind)
+                k(f"ld.param.{_PTX_T[kind]} {r}, [p_{n}]")
+                lo.bind(n, Val(r, kind))
+            else:
+                self.base[n] = k.param_ptr(f"p_{n}")
+        self.layout_smem()
+        tid = k.sreg("%tid.x")
+        lane, warp = k.reg("s32"), k.reg("s32")
+        k(f"and.b32 {lane}, {tid}, 31")
+        k(f"shr.u32 {warp}, {tid}, 5")
+        lo.bind("lane", Val(lane, "s32"))
+        lo.bind("warp", Val(warp, "s32"))
+        self.tid = tid
+        lo.run(spec.op.body)
+        self.mod.kernels.append(k)
+        self.mod.plan = {"entry": spec.entry, "kind": "generic", "block": int(spec.block[0]),
+                         "grid_max": int(spec.grid[0] * spec.grid[1] * spec.grid[2]),
+                         "grid_per_sm": 0,
+                         "smem": int(spec.smem_bytes if self.smem and self.dyn else 0),
+                         "geometry": "meta"}
+        if tuple(spec.block[1:]) != (1, 1):
+            raise NoMatch("1-D blocks only")
+        return self.mod
+
+    # -- masks -----------------------------------------------------------------
+
+    def and_mask(self, p: str | None) -> str | None:
+        cur = self.lo.mask
+        if p is None:
+            return cur
+        if cur is None:
+            return p
+        r = self.k.reg("pred")
+        self.k(f"and.pred {r}, {cur}, {p}")
+        return r
+
+    def guard(self) -> str:
+        return f"@{self.lo.mask} " if self.lo.mask is not None else ""
+
+    # -- addressing ------------------------------------------------------------
+
+    def shape_of(self, name: str):
+        if name in self.smem:
+            return self.smem[name][0]
+        return self.spec.args[name].shape
+
+    def flat(self, index, shape) -> Val:
+        """Row-major element offset as s32 (``interp.py:559-576``)."""
+        lo, k = self.lo, self.k
+        n = len(index)
+        if n == 0:
+            return lo.const(0, "s32")
+        dims = [1] * max(0, n - len(shape)) + [int(d) for d in shape]
+        dims = dims[len(dims) - n:]
+        total = None
+        stride = 1
+        for e, d in zip(reversed(index), reversed(dims)):
+            v = lo.coerce(lo.ev(e), "s32")
+            if stride != 1:
+                t = k.reg("s32")
+                k(f"mul.lo.s32 {t}, {v.reg}, {stride}")
+                v = Val(t, "s32")
+            if total is None:
+                total = v
+            else:
+                t = k.reg("s32")
+                k(f"add.s32 {t}, {total.reg}, {v.reg}")
+                total = Val(t, "s32")
+            stride *= d
+        return total
+
+    def swizzle(self, idx: Val, mode) -> Val:
+        base, _, sh = str(mode or "NONE").partition("@")
+        if base not in _SWZ:
+            return idx
+        shift, msk = _SWZ[base]
+        if sh:
+            shift = int(sh)
+        k = self.k
+        t, r = k.reg("s32"), k.reg("s32")
+        k(f"shr.s32 {t}, {idx.reg}, {shift}")
+        k(f"and.b32 {t}, {t}, {msk}")
+        k(f"shl.b32 {t}, {t}, 3")
+        k(f"xor.b32 {r}, {idx.reg}, {t}")
+        return Val(r, "s32")
+
+    def clamp_masked(self, idx: Val) -> Val:
+        """Masked-off lanes read element 0 (``interp.py:697-701``)."""
+        if self.lo.mask is None:
+            return idx
+        r = self.k.reg("s32")
+        self.k(f"selp.s32 {r}, {idx.reg}, 0, {self.lo.mask}")
+        return Val(r, "s32")
+
+    def addr(self, name: str, idx: Val, j: int = 0) -> tuple[str, bool, object]:
+        """(address register, shared?, dtype) of element idx+j of ``name``."""
+        k = self.k
+        if name in self.smem:
+            shape, dt, off = self.smem[name]
+            eb = dtype_info(dt)[2]
+            a = k.reg("u32")
+            k(f"mad.lo.u32 {a}, {idx.reg}, {eb}, {self.smem_base}")
+            if off + j * eb:
+                k(f"add.u32 {a}, {a}, {off + j * eb}")
+            return a, True, dt
+        if name not in self.base:
+            raise LowerError(f"unknown buffer {name!r}")
+        dt = self.spec.args[name].dtype
+        eb = dtype_info(dt)[2]
+        a = k.reg("u64")
+        k(f"mad.wide.s32 {a}, {idx.reg}, {eb}, {self.base[name]}")
+        if j:
+            k(f"add.u64 {a}, {a}, {j * eb}")
+        return a, False, dt
+
+    def load_elem(self, a: str, shared: bool, dt, kind: str) -> Val:
+        k, lo = self.k, self.lo
+        sk = storage_kind(dt)
+        sp = "shared" if shared else "global"
+        if sk in ("f16", "bf16"):
+            h, r = k.reg("b16"), k.reg("f32")
+            k(f"ld.{sp}.b16 {h}, [{a}]")
+            k(f"cvt.f32.{sk} {r}, {h}")
+            v = Val(r, "f32")
+        elif sk == "pred":
+            b, pr = k.reg("s32"), k.reg("pred")
+            k(f"ld.{sp}.u8 {b}, [{a}]")
+            k(f"setp.ne.s32 {pr}, {b}, 0")
+            v = Val(pr, "pred")
+        else:
+            r = k.reg(sk)
+            k(f"ld.{sp}.{_PTX_T[sk]} {r}, [{a}]")
+            v = Val(r, sk)
+        return lo.coerce(v, kind)
+
+    def store_elem(self, a: str, shared: bool, dt, v: Val, atomic: bool = False) -> None:
+        k, lo = self.k, self.lo
+        sk = storage_kind(dt)
+        sp = "shared" if shared else "global"
+        g = self.guard()
+        if atomic:
+            if shared or sk not in ("f32", "s32"):
+                raise LowerError("atomic add supports f32/s32 global buffers")
+            s = lo.coerce(v, sk)
+            k(f"{g}red.global.add.{sk} [{a}], {s.reg}")
+            return
+        if sk in ("f16", "bf16"):
+            f = lo.coerce(v, "f32")
+            h = k.reg("b16")
+            k(f"cvt.rn.{sk}.f32 {h}, {f.reg}")
+            k(f"{g}st.{sp}.b16 [{a}], {h}")
+        elif sk == "pred":
+            s = lo.coerce(v, "s32")
+            k(f"{g}st.{sp}.u8 [{a}], {s.reg}")
+        else:
+            s = lo.coerce(v, sk)
+            k(f"{g}st.{sp}.{_PTX_T[sk]} [{a}], {s.reg}")
+
+    # -- statements ------------------------------------------------------------
+
+    def do_tile(self, st: ir.Tile) -> None:
+        k, lo = self.k, self.lo
+        ext = [int(a.extent.as_static()) for a in st.axes]
+        n = 1
+        for e in ext:
+            n *= e
+        cta, ntid = k.sreg("%ctaid.x"), k.sreg("%ntid.x")
+        gid, safe = k.reg("u32"), k.reg("u32")
+        k(f"mad.lo.u32 {gid}, {cta}, {ntid}, {self.tid}")
+        act = k.reg("pred")
+        k(f"setp.lt.u32 {act}, {gid}, {n}")
+        k(f"min.u32 {safe}, {gid}, {max(0, n - 1)}")
+        stride = 1
+        for axis, e in reversed(list(zip(st.axes, ext))):
+            r = k.reg("s32")
+            if e == 1:
+                k(f"mov.u32 {r}, 0")
+            elif stride == 1:
+                k(f"rem.u32 {r}, {safe}, {e}")
+            else:
+                k(f"div.u32 {r}, {safe}, {stride}")
+                k(f"rem.u32 {r}, {r}, {e}")
+            lo.env[axis.name] = Val(r, "s32")
+            stride *= e
+        saved = lo.mask
+        lo.mask = self.and_mask(act)
+        lo.run(st.body)
+        lo.mask = saved
+
+    def do_load(self, st: ir.Load) -> None:
+        lo = self.lo
+        if st.dtype is not None:
+            kind = value_kind(st.dtype)
+        elif st.input in self.smem:
+            kind = value_kind(self.smem[st.input][1])
+        else:
+            kind = value_kind(self.spec.args[st.input].dtype)
+        idx = self.clamp_masked(self.flat(st.index, self.shape_of(st.input)))
+        for j, name in enumerate(st.names):
+            e = idx
+            if j:
+                t = self.k.reg("s32")
+                self.k(f"add.s32 {t}, {idx.reg}, {j}")
+                e = Val(t, "s32")
+            if st.input in self.smem:
+                e = self.swizzle(e, getattr(st, "swizzle", "NONE"))
+            a, sh, dt = self.addr(st.input, e)
+            lo.bind(name, self.load_elem(a, sh, dt, kind))
+
+    def do_write(self, st: ir.Write) -> None:
+        idx = self.flat(st.index, self.shape_of(st.output))
+        shared = st.output in self.smem
+        for j, name in enumerate(st.values):
+            e = idx
+            if j:
+                t = self.k.reg("s32")
+                self.k(f"add.s32 {t}, {idx.reg}, {j}")
+                e = Val(t, "s32")
+            if shared:
+                e = self.swizzle(e, getattr(st, "swizzle", "NONE"))
+            a, sh, dt = self.addr(st.output, e)
+            self.store_elem(a, sh, dt, self.lo.env[name], atomic=bool(st.atomic) and not sh)
+
+    def _loop(self, axis: str, start: Val, bound: Val, step: Val, body, seed: bool,
+              uniform: bool) -> None:
+        k, lo = self.k, self.lo
+        lo.seed_accums(body, seed)
+        var = k.reg("s32")
+        k(f"mov.b32 {var}, {start.reg}")
+        saved_env = lo.env.get(axis)
+        head, done = k.label("lp"), k.label("lpend")
+        k.place(head)
+        p = k.reg("pred")
+        k(f"setp.ge.s32 {p}, {var}, {bound.reg}")
+        if uniform:
+            k(f"@{p} bra.uni {done}")
+        else:
+            k(f"@{p} bra {done}")
+            if lo.mask is not None:
+                k(f"@!{lo.mask} bra {done}")
+        lo.env[axis] = Val(var, "s32")
+        lo.run(body)
+        k(f"add.s32 {var}, {var}, {step.reg}")
+        k(f"bra {head}")
+        k.place(done)
+        if saved_env is None:
+            lo.env.pop(axis, None)
+        else:
+            lo.env[axis] = saved_env
+
+    def _thread_free(self, e) -> bool:
+        """Expression independent of the thread (literals only)."""
+        return isinstance(e, ir.Literal) or (hasattr(e, "free_vars") and not e.free_vars)
+
+    def do_loop(self, st: ir.Loop) -> None:
+        lo = self.lo
+        ext = int(st.axis.extent.as_static())
+        self._loop(st.axis.name, lo.const(0, "s32"), lo.const(ext, "s32"), lo.const(1, "s32"),
+                   st.body, bool(st.seed), uniform=True)
+
+    def do_strided(self, st: ir.StridedLoop) -> None:
+        lo = self.lo
+        ext = int(st.axis.extent.as_static())
+        start = lo.coerce(lo.ev(st.start), "s32")
+        step = lo.coerce(lo.ev(st.step) if hasattr(st.step, "free_vars") else
+                         lo.const(int(st.step), "s32"), "s32")
+        bound = lo.coerce(lo.ev(st.end), "s32") if st.end is not None else lo.const(ext, "s32")
+        uniform = self._thread_free(st.start) and self._thread_free(st.step) and (
+            st.end is None or self._thread_free(st.end))
+        if not uniform and _collective(st.body):
+            raise LowerError("barrier inside a loop whose trip count depends on the thread")
+        self._loop(st.axis.name, start, bound, step, st.body, bool(st.seed), uniform)
+
+    def do_cond(self, st: ir.Cond) -> None:
+        lo, k = self.lo, self.k
+        c = lo.truthy(lo.ev(st.cond))
+        saved = lo.mask
+        lo.mask = self.and_mask(c.reg)
+        lo.run(st.body)
+        lo.mask = saved
+        if st.else_body:
+            n = k.reg("pred")
+            k(f"not.pred {n}, {c.reg}")
+            lo.mask = self.and_mask(n)
+            lo.run(st.else_body)
+            lo.mask = saved
+
+    def do_sync(self, st: ir.Sync) -> None:
+        if st.warp:
+            self.k("bar.warp.sync -1")
+        elif st.count is not None:
+            self.k(f"barrier.sync {int(st.barrier_id or 0)}, {int(st.count)}")
+        else:
+            self.k(f"barrier.sync {int(st.barrier_id or 0)}")
+
+    def do_shuffle(self, st: ir.WarpShuffle) -> None:
+        k, lo = self.k, self.lo
+        am = k.reg("u32")
+        k(f"activemask.b32 {am}")
+        lane = k.sreg("%laneid")
+        off = int(st.length) // 2
+        while off > 0:
+            src, bit = k.reg("u32"), k.reg("u32")
+            k(f"xor.b32 {src}, {lane}, {off}")
+            k(f"shr.u32 {bit}, {am}, {src}")
+            k(f"and.b32 {bit}, {bit}, 1")
+            ok = k.reg("pred")
+            k(f"setp.ne.u32 {ok}, {bit}, 0")
+            for s, sb in zip(st.state, st.state_b):
+                cur = lo.env[s]
+                if cur.kind not in ("f32", "s32"):
+                    raise LowerError("shuffle of a non-32-bit state")
+                r, out = k.reg(cur.kind), k.reg(cur.kind)
+                k(f"shfl.sync.bfly.b32 {r}, {cur.reg}, {off}, 31, {am}")
+                k(f"selp.{'f32' if cur.kind == 'f32' else 'b32'} {out}, {r}, {cur.reg}, {ok}")
+                lo.bind(sb, Val(out, cur.kind))
+            lo.run(st.combine_states)
+            off //= 2
+
+    def do_tree(self, st: ir.TreeHalve) -> None:
+        k, lo = self.k, self.lo
+        if st.inner is not None:
+            raise LowerError("TreeHalve(inner=...)")
+        t = lo.coerce(lo.env[st.tid_var], "s32")
+        kinds = {s: lo.env[s].kind for s in st.state}
+        length = int(st.length)
+        half = length // 2
+        bar = f"barrier.sync {int(st.barrier_id or 0)}"
+        if st.barrier_count is not None:
+            bar += f", {int(st.barrier_count)}"
+        while half > 0:
+            k(bar)
+            inner = k.reg("pred")
+            k(f"setp.lt.s32 {inner}, {t.reg}, {half}")
+            for b, s, sb in zip(st.bufs, st.state, st.state_b):
+                size = numel(self.smem[b][0])
+                i0, i1 = k.reg("s32"), k.reg("s32")
+                k(f"min.s32 {i0}, {t.reg}, {size - 1}")
+                k(f"max.s32 {i0}, {i0}, 0")
+                k(f"add.s32 {i1}, {t.reg}, {half}")
+                k(f"min.s32 {i1}, {i1}, {size - 1}")
+                k(f"max.s32 {i1}, {i1}, 0")
+                bk = value_kind(self.smem[b][1])
+                a0, sh, dt = self.addr(b, Val(i0, "s32"))
+                a1, _, _ = self.addr(b, Val(i1, "s32"))
+                lo.bind(s, self.load_elem(a0, True, dt, bk))
+                lo.bind(sb, self.load_elem(a1, True, dt, bk))
+            k(bar)
+            saved = lo.mask
+            lo.mask = self.and_mask(inner)
+            lo.run(st.combine_states)
+            for b, s in zip(st.bufs, st.state):
+                size = numel(self.smem[b][0])
+                i0 = k.reg("s32")
+                k(f"min.s32 {i0}, {t.reg}, {size - 1}")
+                k(f"max.s32 {i0}, {i0}, 0")
+                a0, _, dt = self.addr(b, Val(i0, "s32"))
+                self.store_elem(a0, True, dt, lo.env[s])
+            lo.mask = saved
+            half //= 2
+        k(bar)
+        for b, s in zip(st.bufs, st.state):
+            z = lo.const(0, "s32")
+            a0, _, dt = self.addr(b, z)
+            lo.bind(s, lo.coerce(self.load_elem(a0, True, dt, value_kind(dt)), kinds[s]))
+
+    def do_cp_async(self, st: ir.CpAsyncCopy) -> None:
+        k, lo = self.k, self.lo
+        if st.smem not in self.smem:
+            raise LowerError(f"cp.async into non-Smem {st.smem!r}")
+        shape = self.smem[st.smem][0]
+        dst = self.flat(st.smem_index, shape)
+        if st.lane_index is not None:
+            cols = int(shape[-1]) if shape else 1
+            ln = lo.coerce(lo.ev(st.lane_index[0]), "s32")
+            cl = lo.coerce(lo.ev(st.lane_index[1]), "s32")
+            t = k.reg("s32")
+            k(f"mad.lo.s32 {t}, {ln.reg}, {cols}, {dst.reg}")
+            k(f"add.s32 {t}, {t}, {cl.reg}")
+            dst = Val(t, "s32")
+        dst = self.swizzle(dst, st.swizzle)
+        src = self.clamp_masked(self.flat(st.src_index, self.shape_of(st.src)))
+        nb = int(st.nbytes)
+        eb = dtype_info(self.spec.args[st.src].dtype)[2]
+        sa, _, _ = self.addr(st.src, src)
+        da, _, _ = self.addr(st.smem, dst)
+        g = self.guard()
+        words = nb // 4
+        regs = k.regs("b32", words)
+        if words == 4:
+            k(f"ld.global.v4.b32 {{{', '.join(regs)}}}, [{sa}]")
+            k(f"{g}st.shared.v4.b32 [{da}], {{{', '.join(regs)}}}")
+        elif words == 2:
+            k(f"ld.global.v2.b32 {{{', '.join(regs)}}}, [{sa}]")
+            k(f"{g}st.shared.v2.b32 [{da}], {{{', '.join(regs)}}}")
+        elif words == 1:
+            k(f"ld.global.b32 {regs[0]}, [{sa}]")
+            k(f"{g}st.shared.b32 [{da}], {regs[0]}")
+        else:
+            raise LowerError(f"cp.async of {nb} bytes")
+        del eb
+
+    def do_select(self, st: ir.Select) -> None:
+        lo = self.lo
+        br = list(st.branches)
+        kind = lo.env[br[-1].value].kind
+        for b in br[:-1]:
+            kk = lo.env[b.value].kind
+            kind = ("f64" if "f64" in (kk, kind) else "f32") if ("f32" in (kk, kind) or
+                                                                  "f64" in (kk, kind)) else "s32"
+        res = lo.coerce(lo.env[br[-1].value], kind)
+        for b in reversed(br[:-1]):
+            c = lo.truthy(lo.ev(b.select))
+            res = lo.select(c, lo.coerce(lo.env[b.value], kind), res)
+        lo.bind(st.name, res)
+
+    def do_zero_prologue(self, st: ir.ZeroPrologue) -> None:
+        k = self.k
+        a = self.spec.args[st.dst]
+        words = min(int(st.words), (a.nbytes + 3) // 4)
+        cta, ntid = k.sreg("%ctaid.x"), k.sreg("%ntid.x")
+        p = k.reg("pred")
+        skip = k.label("nozp")
+        k(f"setp.ne.u32 {p}, {cta}, 0")
+        k(f"@{p} bra {skip}")
+        i = k.reg("u32")
+        k(f"mov.u32 {i}, {self.tid}")
+        lp = k.label("zp")
+        k.place(lp)
+        k(f"setp.ge.u32 {p}, {i}, {words}")
+        k(f"@{p} bra {skip}")
+        ad = k.addr(self.base[st.dst], i, 4)
+        k(f"st.global.u32 [{ad}], 0")
+        k(f"add.u32 {i}, {i}, {ntid}")
+        k(f"bra {lp}")
+        k.place(skip)
+        k("barrier.sync 0")
+
+
+def emit_generic(spec: KernelSpec) -> Module:
+    return Generic(spec).emit()

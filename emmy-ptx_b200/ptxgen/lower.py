@@ -80,6 +80,7 @@ class Lowerer:
         self.load_hook = None     # (stmt) -> None, binds names
         self.write_hook = None    # (stmt) -> None
         self.extra = {}           # stmt type -> handler
+        self.mask = None          # predicate register: lanes whose register writes land
 
     # -- registers ---------------------------------------------------------
 
@@ -92,10 +93,17 @@ class Lowerer:
         return r
 
     def bind(self, name: str, v: Val) -> Val:
-        """Write ``v`` into ``name``'s register (one register per name+kind)."""
+        """Write ``v`` into ``name``'s register (one register per name+kind).
+        Under a mask only the active lanes take the value; a name first
+        bound under a mask starts at 0 in the other lanes (interp.py:458-468)."""
+        fresh = (name, v.kind) not in self.home
         r = self.home_reg(name, v.kind)
+        if fresh and self.mask is not None and v.kind != "pred":
+            zero = {"f32": "0f00000000", "f64": "0d0000000000000000"}.get(v.kind, "0")
+            self.k(f"mov.{self._mov_t(v.kind)} {r}, {zero}")
         if r != v.reg:
-            self.k(f"mov.{self._mov_t(v.kind)} {r}, {v.reg}")
+            guard = f"@{self.mask} " if self.mask is not None else ""
+            self.k(f"{guard}mov.{self._mov_t(v.kind)} {r}, {v.reg}")
         out = Val(r, v.kind)
         self.env[name] = out
         return out
