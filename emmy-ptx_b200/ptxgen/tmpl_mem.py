@@ -384,8 +384,11 @@ def emit_pointwise(spec: KernelSpec, plan: PointwisePlan) -> Module:
         raise NoMatch("tail of a vectorised pointwise")  # vec==4 implies n % 4 == 0
     m = Module(comment=f"emmy-b200 pointwise template for {spec.entry}")
     m.kernels.append(k)
-    m.plan = {"entry": spec.entry, "kind": "pointwise", "block": 256, "grid_per_sm": 8,
-              "grid_max": max(1, math.ceil(nvec / 256)), "smem": 0}
+    # one-shot grid: every thread takes exactly one batch of 4 vectors (the
+    # unrolled body), no grid-stride tail -- measured faster on B200 than a
+    # persistent grid (6.8 vs 6.1 TB/s for c=a+b over 2^28)
+    m.plan = {"entry": spec.entry, "kind": "pointwise", "block": 256, "grid_per_sm": 0,
+              "grid_max": max(1, math.ceil(nvec / (256 * 4))), "smem": 0}
     return m
 
 
@@ -839,10 +842,11 @@ def match_rows(spec: KernelSpec) -> RowsPlan:
 
 
 def rows_block(n_cols: int, vec: int) -> int:
+    """256 threads per row once a row has 512+ chunks (8 CTAs of 256 per SM
+    measured faster than 4 of 512 for 4096-wide rows), fewer for short rows."""
     chunks = max(1, n_cols // vec)
-    for b in (512, 256, 128):
-        if chunks >= 2 * b:
-            return b
+    if chunks >= 512:
+        return 256
     return 128 if chunks >= 128 else max(32, 32 * math.ceil(chunks / 32))
 
 
