@@ -182,7 +182,7 @@ def workload_matmul(rank: int, world: int):
 def workload_attention(rank: int, world: int):
     from ptxgen import irgen
     from ml_dtypes import bfloat16
-    b, h, s, d = 16, 32, 4096, 128
+    b, h, s, d = (1 if _SMALL else 16), 32, 4096, 128
     rng = np.random.default_rng(5000 + rank)
     jobs = []
     for dt in ("f32", "bf16"):
@@ -192,7 +192,7 @@ def workload_attention(rank: int, world: int):
                    for _ in range(3))
 
         def chk(out, q=q, k=k, v=v, dt=dt):
-            bi, hi = 3, 17
+            bi, hi = 3 % b, 17
             rows = np.arange(0, s, 257)
             qq, kk, vv = (x[bi, hi].astype(np.float64) for x in (q, k, v))
             sc = qq[rows] @ kk.T / np.sqrt(d)
@@ -211,6 +211,8 @@ def workload_attention(rank: int, world: int):
                               "f32 (3xTF32) and bf16, non-causal",
                   "heads_per_rank": b * h}
 
+
+_SMALL = False
 
 WORKLOADS = {"reductions": workload_reductions, "pointwise": workload_pointwise,
              "rows": workload_rows, "matmul": workload_matmul, "attention": workload_attention}
@@ -339,6 +341,14 @@ def run_ours(args, dist: Dist):
     import ctypes as C
     from ptxgen.runtime import Device, PreparedKernel, check
     jobs, cfg = WORKLOADS[args.workload](dist.rank, dist.world)
+    if args.jobs:
+        keep = set(args.jobs.split(","))
+        jobs = [j for j in jobs if j.key in keep]
+        if not jobs:
+            raise SystemExit(f"--jobs {args.jobs}: no such job in {args.workload}")
+        cfg["jobs"] = sorted(keep)
+    if _SMALL:
+        cfg["small"] = "reduced shapes for profiler captures; not a bench configuration"
     dev = Device.get(dist.local)
     comm = None
     if dist.world > 1 and any(j.allreduce for j in jobs):
@@ -663,7 +673,13 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--jobs", default="",
+                    help="comma-separated job keys of the workload to run (default: all)")
+    ap.add_argument("--small", action="store_true",
+                    help="reduced shapes (attention: B=1) for profiler captures only")
     args = ap.parse_args(argv)
+    global _SMALL
+    _SMALL = args.small
     if args.warmup < 3:
         args.warmup = 3
     dist = Dist(args.gpus)

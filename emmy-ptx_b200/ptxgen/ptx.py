@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import struct
 
-PTX_VERSION = "8.7"
+PTX_VERSION = "8.8"
 PTX_TARGET = "sm_100a"
 
 # register class per value kind

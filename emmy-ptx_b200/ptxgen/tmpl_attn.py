@@ -10,10 +10,14 @@ B200 kernel (one persistent CTA per SM, 192 threads; a unit is one
 batch*head and 128 query rows):
 
 * warp 0 -- TMA: the unit's Q tile once, then per key block the K block and
-  the V^T block (all K-major, 128-byte swizzle);
-* warp 1 -- allocates TMEM (S block + O, f32) and issues
+  the V^T block (all K-major, 128-byte swizzle), into two stages each when
+  shared memory holds them (bf16 up to D=128), else one, with separate
+  full/empty barriers for K and V so K_{g+1} streams in once S_g is done;
+* warp 1 -- allocates TMEM (two S blocks + O, f32) and issues
   ``S = Q . K^T`` then ``O += P . V^T`` with ``tcgen05.mma`` (kind::tf32 in
-  three hi/lo passes for f32 data; kind::f16 on bf16 data);
+  three hi/lo passes for f32 data; kind::f16 on bf16 data).  With two K/V
+  stages it issues ``S_{g+1}`` ahead of ``O += P_g V_g``, so the tensor pipe
+  works on the next scores while the softmax warps exponentiate these;
 * warps 2-5 -- one thread per query row: ``tcgen05.ld`` of its S row, row max,
   ``p = exp(s/c0 - m)``, running sum, P written to shared memory as the A
   operand of the next MMA (hi/lo TF32 or bf16), rescale of its O row in TMEM
@@ -33,6 +37,7 @@ each output element with the IR's own per-key statements.
 from __future__ import annotations
 
 import math
+import os
 
 from . import ir
 from .analysis import NoMatch, flat_affine, numel
@@ -42,7 +47,8 @@ from .ptx import Kernel, Module, f32_hex
 from .tmpl_mma import ERR_WAIT_TIMEOUT, PLAN_MAGIC, _Ctx, _desc_const
 
 LOG2E = 1.4426950408889634
-THREADS = 192
+SMEM_MAX = 232448            # shared memory per CTA, static + dynamic
+XCH_STATIC = 4096            # static shared memory of the two-threads-per-row form
 W_PROD, W_MMA = 0, 1
 BQ = 128
 RESCALE_T = 8.0
@@ -140,28 +146,48 @@ def _idesc(kind: str, m: int, n: int) -> int:
 
 
 def _layout(plan):
-    """Shared-memory regions (bytes) of one unit: Q (resident), K block, V^T
-    block and P, each ``passes`` deep (hi, lo) for f32."""
+    """Shared-memory regions (bytes) of one unit: Q (resident), ``kvst``
+    stages of the K block and the V^T block, and P; each ``halves`` deep
+    (hi, lo) for f32."""
     e, atom, bkv, d = plan.e, plan.atom, plan.bkv, plan.d
     halves = 2 if plan.dtype == "f32" else 1
     q_chunk = BQ * 128                 # one 128-byte-wide column chunk of 128 rows
     q_bytes = (d // atom) * q_chunk
     k_chunk = bkv * 128
     k_bytes = (d // atom) * k_chunk
-    v_chunk = d * 128                  # V^T: d rows, bkv keys wide
+    v_chunk = d * 128                  # V^T: d rows, one atom of keys wide
     v_bytes = max(1, bkv // atom) * v_chunk
     p_chunk = BQ * 128
-    p_bytes = max(1, bkv // atom) * p_chunk
+    # bf16 P lives in TMEM (over its own S columns) and feeds the P . V MMA
+    # from there; f32 (hi/lo TF32) P is staged in shared memory
+    p_tmem = plan.dtype != "f32"
+    p_bytes = 0 if p_tmem else max(1, bkv // atom) * p_chunk
+    base = halves * (q_bytes + p_bytes)
+    per_stage = halves * (k_bytes + v_bytes)
+    kvst = 2 if base + 2 * per_stage + 1024 <= 232448 - 2048 else 1
     lay = {}
     off = 0
-    for name, size in (("q", q_bytes), ("k", k_bytes), ("v", v_bytes), ("p", p_bytes)):
-        for h in range(halves):
-            lay[(name, h)] = off
-            off += size
+    for h in range(halves):
+        lay[("q", h)] = off
+        off += q_bytes
+    for st in range(kvst):
+        for name, size in (("k", k_bytes), ("v", v_bytes)):
+            for h in range(halves):
+                lay[(name, st, h)] = off
+                off += size
+    for h in range(halves):
+        lay[("p", h)] = off
+        off += p_bytes
     lay["total"] = off
+    # two softmax threads per query row (warps 2-9) when the exchange slots
+    # fit beside the dynamic layout, else one (warps 2-5)
+    split = 2 if off + 1024 + XCH_STATIC <= SMEM_MAX else 1
+    lay["split"] = split
+    lay["p_tmem"] = p_tmem
+    lay["threads"] = 64 + 128 * split
     lay.update(q_bytes=q_bytes, k_bytes=k_bytes, v_bytes=v_bytes, p_bytes=p_bytes,
                q_chunk=q_chunk, k_chunk=k_chunk, v_chunk=v_chunk, p_chunk=p_chunk,
-               halves=halves)
+               halves=halves, kvst=kvst)
     return lay
 
 
@@ -188,7 +214,7 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
         k(f"ld.global.u32 {flag}, [emmy_plan]")
         k(f"setp.ne.u32 {p}, {flag}, {PLAN_MAGIC}")
         k(f"@{p} bra {simt}")
-        k(f"setp.ne.u32 {p}, {ntid}, {THREADS}")
+        k(f"setp.ne.u32 {p}, {ntid}, {lay['threads']}")
         k(f"@{p} bra {simt}")
         k(f"mov.u32 {dsz}, %dynamic_smem_size")
         k(f"setp.lt.u32 {p}, {dsz}, {dyn}")
@@ -209,7 +235,7 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     if tc_ok:
         pre, ws_bytes, tm = _emit_pre(mod, spec, plan)
         plan_d.update({
-            "block": THREADS, "grid_per_sm": 1, "grid_max": BH * (S // BQ), "smem": dyn,
+            "block": lay["threads"], "grid_per_sm": 1, "grid_max": BH * (S // BQ), "smem": dyn,
             "workspace": {"sym": "emmy_ws", "bytes": ws_bytes}, "pre": pre, "tmaps": tm,
             "flags": [{"sym": "emmy_plan", "value": PLAN_MAGIC}],
             "tile": [BQ, plan.bkv, D], "passes": plan.passes,
@@ -525,6 +551,63 @@ def _emit_simt(k: Kernel, spec, plan, base, tid, ntid, cta, ncta):
 # tensor-core path
 # ---------------------------------------------------------------------------
 
+# 2^f on [-1/2, 1/2]: degree-3 minimax polynomial (relative error), fitted by
+# a Remez exchange in f64 and rounded to f32; evaluated by Horner in f32 its
+# maximum relative error is 7.5e-5, below half an ulp of bf16 (2^-9).
+EXP2_POLY = (0.9999280571937561, 0.6932609677314758, 0.2426111251115799,
+             0.0551716685295105)
+EXP_POLY_DEFAULT = 0
+
+
+def _exp_poly_share() -> int:
+    """Element pairs out of every four whose exp2 runs on the FMA pipe
+    (polynomial) instead of the MUFU (``ex2.approx``); bf16 P only."""
+    v = os.environ.get("EMMY_ATTN_EXP_POLY")
+    return max(0, min(4, int(v))) if v else EXP_POLY_DEFAULT
+
+
+def _pair_const(v: float) -> str:
+    b = int(f32_hex(v)[2:], 16)
+    return f"0x{(b << 32) | b:016X}"
+
+
+def _exp2_poly_consts(k: Kernel):
+    """Packed (x2) registers: the 1.5 * 2^23 shift and the coefficients."""
+    regs = []
+    for v in (12582912.0,) + EXP2_POLY:
+        r = k.reg("b64")
+        k(f"mov.b64 {r}, {_pair_const(v)}")
+        regs.append(r)
+    return regs
+
+
+def _exp2_poly_pair(k: Kernel, pr, consts):
+    """exp2 of the two f32 lanes of ``pr`` (each <= 8) on the FMA pipe:
+    x = max(x, -125); x = j + f with j = rint(x) from the 1.5 * 2^23 shift
+    (the low bits of the shifted value hold j), 2^f by the polynomial, and
+    j added to the exponent field with one integer multiply-add
+    (``j << 23`` == ``bits(x + 1.5 * 2^23) * 2^23`` modulo 2^32)."""
+    a, b = k.reg("b32"), k.reg("b32")
+    k(f"mov.b64 {{{a}, {b}}}, {pr}")
+    k(f"max.f32 {a}, {a}, {f32_hex(-125.0)}")
+    k(f"max.f32 {b}, {b}, {f32_hex(-125.0)}")
+    x, tt, jf, f, q = (k.reg("b64") for _ in range(5))
+    k(f"mov.b64 {x}, {{{a}, {b}}}")
+    magic, c0, c1, c2, c3 = consts
+    k(f"add.rn.f32x2 {tt}, {x}, {magic}")
+    k(f"sub.rn.f32x2 {jf}, {tt}, {magic}")
+    k(f"sub.rn.f32x2 {f}, {x}, {jf}")
+    k(f"fma.rn.f32x2 {q}, {f}, {c3}, {c2}")
+    k(f"fma.rn.f32x2 {q}, {q}, {f}, {c1}")
+    k(f"fma.rn.f32x2 {q}, {q}, {f}, {c0}")
+    t0, t1, q0, q1, r0, r1 = k.regs("b32", 6)
+    k(f"mov.b64 {{{t0}, {t1}}}, {tt}")
+    k(f"mov.b64 {{{q0}, {q1}}}, {q}")
+    k(f"mad.lo.s32 {r0}, {t0}, 8388608, {q0}")
+    k(f"mad.lo.s32 {r1}, {t1}, 8388608, {q1}")
+    return r0, r1
+
+
 
 def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     S, D, BH, BKV = plan.s, plan.d, plan.bh, plan.bkv
@@ -535,14 +618,20 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     nkv = S // BKV
     qblocks = S // BQ
     units = BH * qblocks
+    kvst = lay["kvst"]
+    stage_k = lay[("k", 1, 0)] - lay[("k", 0, 0)] if kvst > 1 else 0
     cx = _Ctx(k)
-    for nm in ("q_full", "q_empty", "kv_full", "kv_empty", "s_full", "p_full", "pv_done",
-               "drain"):
+    for nm in ("q_full", "q_empty", "p_full", "pv_done", "drain"):
         k.shared(f"\t.shared .align 8 .b64 bar_{nm};")
+    for nm, cnt in (("k_full", kvst), ("k_empty", kvst), ("v_full", kvst), ("v_empty", kvst),
+                    ("s_full", 2), ("s_free", 2)):
+        k.shared(f"\t.shared .align 8 .b64 bar_{nm}[{cnt}];")
     k.shared("\t.shared .align 4 .u32 tmem_slot;")
     k.shared("\t.shared .align 4 .u32 abort_flag;")
+    # TMEM: two S buffers (the MMA warp fills one while the softmax warps
+    # read the other), then O
     s_cols = max(32, BKV)
-    tcols = 1 << (s_cols + D - 1).bit_length()
+    tcols = 1 << (2 * s_cols + D - 1).bit_length()
     warp, lane = k.reg("u32"), k.reg("u32")
     k(f"shr.u32 {warp}, {tid}, 5")
     k(f"and.b32 {lane}, {tid}, 31")
@@ -562,9 +651,15 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     skip = k.label("noinit")
     k(f"setp.ne.u32 {p}, {tid}, 0")
     k(f"@{p} bra {skip}")
-    for nm, cnt in (("q_full", 1), ("q_empty", 1), ("kv_full", 1), ("kv_empty", 1),
-                    ("s_full", 1), ("p_full", 128), ("pv_done", 1), ("drain", 1)):
+    split = lay["split"]
+    p_tmem = lay["p_tmem"]
+    for nm, cnt in (("q_full", 1), ("q_empty", 1), ("p_full", 128 * split), ("pv_done", 1),
+                    ("drain", 1)):
         k(f"mbarrier.init.shared::cta.b64 [bar_{nm}], {cnt}")
+    for nm, n, cnt in (("k_full", kvst, 1), ("k_empty", kvst, 1), ("v_full", kvst, 1),
+                       ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1 if p_tmem else 4 * split)):
+        for i in range(n):
+            k(f"mbarrier.init.shared::cta.b64 [bar_{nm}+{8 * i}], {cnt}")
     k("st.shared.u32 [abort_flag], 0")
     for r in tm.values():
         k(f"prefetch.tensormap [{r}]")
@@ -586,25 +681,45 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     teardown, abort_l = k.label("teardown"), k.label("abort")
     role_mma, role_sm = k.label("rmma"), k.label("rsm")
 
-    def smem(name, h, extra=0):
-        r = k.reg("u32")
-        k(f"add.u32 {r}, {ring}, {lay[(name, h)] + extra}")
-        return r
-
     def unit_coords(u):
         bh, qb = k.reg("u32"), k.reg("u32")
         k(f"div.u32 {bh}, {u}, {qblocks}")
         k(f"rem.u32 {qb}, {u}, {qblocks}")
         return bh, qb
 
+    def stage_of(g):
+        """(stage index, parity of its full phase) of global key block ``g``."""
+        st, ph = k.reg("u32"), k.reg("u32")
+        if kvst == 1:
+            k(f"mov.u32 {st}, 0")
+            k(f"and.b32 {ph}, {g}, 1")
+        else:
+            k(f"and.b32 {st}, {g}, 1")
+            k(f"shr.u32 {ph}, {g}, 1")
+            k(f"and.b32 {ph}, {ph}, 1")
+        return st, ph
+
+    def bar_at(name, idx):
+        r = k.reg("u32")
+        k(f"mov.u32 {r}, bar_{name}")
+        k(f"mad.lo.u32 {r}, {idx}, 8, {r}")
+        return r
+
+    def flip(ph):
+        r = k.reg("u32")
+        k(f"xor.b32 {r}, {ph}, 1")
+        return r
+
     # ================= producer =================
     k(f"setp.ne.u32 {p}, {warp}, {W_PROD}")
     k(f"@{p} bra {role_mma}")
-    k(f"setp.ne.u32 {p}, {lane}, 0")
-    k(f"@{p} bra {teardown}")
-    uit, kvit, u = k.reg("u32"), k.reg("u32"), k.reg("u32")
+    # the whole warp runs the loop (converged, so its addresses stay
+    # warp-uniform); one elected lane issues the copies
+    pe = k.reg("pred")
+    k(f"elect.sync _|{pe}, -1")
+    uit, g, u = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {uit}, 0")
-    k(f"mov.u32 {kvit}, 0")
+    k(f"mov.u32 {g}, 0")
     k(f"mov.u32 {u}, {cta}")
     ul, ue = k.label("p_unit"), k.label("p_unitend")
     k.place(ul)
@@ -618,39 +733,46 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"xor.b32 {ph}, {ph}, 1")
     cx.wait("bar_q_empty", ph, abort_l)
     qbytes = lay["q_bytes"] * halves
-    k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [bar_q_full], {qbytes}")
+    k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [bar_q_full], {qbytes}")
     for h in range(halves):
         for c in range(D // atom):
-            dst, cc = smem("q", h, c * lay["q_chunk"]), k.reg("u32")
+            dst, cc = k.reg("u32"), k.reg("u32")
+            k(f"add.u32 {dst}, {ring}, {lay[('q', h)] + c * lay['q_chunk']}")
             k(f"mov.u32 {cc}, {c * atom}")
-            k(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+            k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
               f"[{dst}], [{tm['qh' if h == 0 else 'ql']}, {{{cc}, {qrow}, {bh}}}], [bar_q_full]")
     j = k.reg("u32")
     k(f"mov.u32 {j}, 0")
     jl = k.label("p_kv")
     k.place(jl)
-    ph2 = k.reg("u32")
-    k(f"and.b32 {ph2}, {kvit}, 1")
-    k(f"xor.b32 {ph2}, {ph2}, 1")
-    cx.wait("bar_kv_empty", ph2, abort_l)
-    kvbytes = (lay["k_bytes"] + lay["v_bytes"]) * halves
-    k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [bar_kv_full], {kvbytes}")
+    st, phf = stage_of(g)
+    phe = flip(phf)
+    soff = k.reg("u32")
+    k(f"mad.lo.u32 {soff}, {st}, {stage_k}, {ring}")
     krow = k.reg("u32")
     k(f"mul.lo.u32 {krow}, {j}, {BKV}")
+    kb, vb = bar_at("k_empty", st), bar_at("v_empty", st)
+    kf, vf = bar_at("k_full", st), bar_at("v_full", st)
+    cx.wait(kb, phe, abort_l)
+    k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{kf}], {lay['k_bytes'] * halves}")
     for h in range(halves):
         for c in range(D // atom):
-            dst, cc = smem("k", h, c * lay["k_chunk"]), k.reg("u32")
+            dst, cc = k.reg("u32"), k.reg("u32")
+            k(f"add.u32 {dst}, {soff}, {lay[('k', 0, h)] + c * lay['k_chunk']}")
             k(f"mov.u32 {cc}, {c * atom}")
-            k(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-              f"[{dst}], [{tm['kh' if h == 0 else 'kl']}, {{{cc}, {krow}, {bh}}}], [bar_kv_full]")
+            k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+              f"[{dst}], [{tm['kh' if h == 0 else 'kl']}, {{{cc}, {krow}, {bh}}}], [{kf}]")
+    cx.wait(vb, phe, abort_l)
+    k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{vf}], {lay['v_bytes'] * halves}")
+    for h in range(halves):
         for c in range(max(1, BKV // atom)):
-            dst, cc = smem("v", h, c * lay["v_chunk"]), k.reg("u32")
+            dst, cc, z = k.reg("u32"), k.reg("u32"), k.reg("u32")
+            k(f"add.u32 {dst}, {soff}, {lay[('v', 0, h)] + c * lay['v_chunk']}")
             k(f"add.u32 {cc}, {krow}, {c * atom}")
-            z = k.reg("u32")
             k(f"mov.u32 {z}, 0")
-            k(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-              f"[{dst}], [{tm['vh' if h == 0 else 'vl']}, {{{cc}, {z}, {bh}}}], [bar_kv_full]")
-    k(f"add.u32 {kvit}, {kvit}, 1")
+            k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+              f"[{dst}], [{tm['vh' if h == 0 else 'vl']}, {{{cc}, {z}, {bh}}}], [{vf}]")
+    k(f"add.u32 {g}, {g}, 1")
     k(f"add.u32 {j}, {j}, 1")
     k(f"setp.lt.u32 {p}, {j}, {nkv}")
     k(f"@{p} bra {jl}")
@@ -661,24 +783,128 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"bra.uni {teardown}")
 
     # ================= MMA issuer =================
+    # Key block g: S[g%2] = Q . K_g^T, then (once the softmax warps have
+    # written P_g) O (+)= P_g . V_g^T.  With two K/V stages the issue order is
+    # S_{g+1} before O += P_g V_g, so the tensor pipe computes the next scores
+    # while the softmax warps work on this block's.
     k.place(role_mma)
     k(f"setp.ne.u32 {p}, {warp}, {W_MMA}")
     k(f"@{p} bra {role_sm}")
-    k(f"setp.ne.u32 {p}, {lane}, 0")
-    k(f"@{p} bra {teardown}")
+    # converged warp, one elected lane issues (descriptors stay warp-uniform)
+    pm = k.reg("pred")
+    k(f"elect.sync _|{pm}, -1")
     kmaj = _desc_const(16, 1024, 2)      # K-major, 128-byte swizzle, 8-row groups 1 KB apart
     id_s, id_o = k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {id_s}, {_idesc(kind, BQ, BKV)}")
     k(f"mov.u32 {id_o}, {_idesc(kind, BQ, D)}")
     yes = k.reg("pred")
     k(f"setp.eq.u32 {yes}, 0, 0")
-    s_t, o_t = k.reg("u32"), k.reg("u32")
-    k(f"mov.u32 {s_t}, {tmem}")
-    k(f"add.u32 {o_t}, {tmem}, {s_cols}")
-    uit2, kvit2, u2 = k.reg("u32"), k.reg("u32"), k.reg("u32")
+    o_t = k.reg("u32")
+    k(f"add.u32 {o_t}, {tmem}, {2 * s_cols}")
+    uit2, g2, u2 = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {uit2}, 0")
-    k(f"mov.u32 {kvit2}, 0")
+    k(f"mov.u32 {g2}, 0")
     k(f"mov.u32 {u2}, {cta}")
+    pairs = [(0, 0), (0, 1), (1, 0)] if f32 else [(0, 0)]
+
+    # Shared-memory descriptors: one base per K/V stage, built once; an
+    # operand's descriptor is its stage base plus (byte offset >> 4) in the
+    # 14-bit start-address field (shared addresses stay below 2^18, so the
+    # field never carries).
+    def mkdesc(addr_reg):
+        ad, r = k.reg("u32"), k.reg("u64")
+        k(f"shr.u32 {ad}, {addr_reg}, 4")
+        k(f"and.b32 {ad}, {ad}, 16383")
+        k(f"cvt.u64.u32 {r}, {ad}")
+        k(f"or.b64 {r}, {r}, 0x{kmaj:016X}")
+        return r
+
+    d_base = mkdesc(ring)
+    d_stage1 = k.reg("u64")
+    k(f"add.s64 {d_stage1}, {d_base}, {stage_k >> 4}")
+
+    def stage_desc(st_):
+        ps, r = k.reg("pred"), k.reg("u64")
+        if kvst == 1:
+            return d_base
+        k(f"setp.ne.u32 {ps}, {st_}, 0")
+        k(f"selp.b64 {r}, {d_stage1}, {d_base}, {ps}")
+        return r
+
+    def dsc(base_d, off):
+        assert off % 16 == 0
+        r = k.reg("u64")
+        k(f"add.s64 {r}, {base_d}, {off >> 4}")
+        return r
+
+    def issue_qk(gr):
+        st_, phf_ = stage_of(gr)
+        b, phs = k.reg("u32"), k.reg("u32")
+        k(f"and.b32 {b}, {gr}, 1")
+        k(f"shr.u32 {phs}, {gr}, 1")
+        k(f"and.b32 {phs}, {phs}, 1")
+        k(f"xor.b32 {phs}, {phs}, 1")
+        ds = stage_desc(st_)
+        s_t = k.reg("u32")
+        k(f"mad.lo.u32 {s_t}, {b}, {s_cols}, {tmem}")
+        cx.wait(bar_at("k_full", st_), phf_, abort_l)
+        cx.wait(bar_at("s_free", b), phs, abort_l)
+        k("tcgen05.fence::after_thread_sync")
+        first = True
+        for c in range(D // atom):
+            for kk in range(4):
+                for (ha, hb) in pairs:
+                    a_ = dsc(d_base, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
+                    b_ = dsc(ds, lay[("k", 0, hb)] + c * lay["k_chunk"] + kk * 32)
+                    acc = yes
+                    if first:
+                        acc = k.reg("pred")
+                        k(f"setp.ne.u32 {acc}, 0, 0")
+                        first = False
+                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a_}, {b_}, {id_s}, {acc}")
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+          f"[{bar_at('s_full', b)}]")
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+          f"[{bar_at('k_empty', st_)}]")
+
+    def issue_pv(gr, jr):
+        st_, phf_ = stage_of(gr)
+        php_ = k.reg("u32")
+        k(f"and.b32 {php_}, {gr}, 1")
+        ds = stage_desc(st_)
+        firstb = k.reg("pred")
+        k(f"setp.ne.u32 {firstb}, {jr}, 0")
+        cx.wait("bar_p_full", php_, abort_l)
+        cx.wait(bar_at("v_full", st_), phf_, abort_l)
+        k("tcgen05.fence::after_thread_sync")
+        if p_tmem:
+            pb = k.reg("u32")                 # P_g: packed bf16 over S buffer g % 2
+            k(f"and.b32 {pb}, {gr}, 1")
+            k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
+        first = True
+        for c in range(max(1, BKV // atom)):
+            for kk in range(min(4, BKV * e // 32)):
+                for (ha, hb) in pairs:
+                    if p_tmem:
+                        a_ = k.reg("u32")     # 16 keys per K-step = 8 packed columns
+                        k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8}")
+                        a_ = f"[{a_}]"
+                    else:
+                        a_ = dsc(d_base, lay[("p", ha)] + c * lay["p_chunk"] + kk * 32)
+                    b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
+                    acc = firstb if first else yes
+                    first = False
+                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{o_t}], {a_}, {b_}, {id_o}, {acc}")
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+          f"[{bar_at('v_empty', st_)}]")
+        if p_tmem:
+            # P_g was read from S buffer g % 2: the buffer is free once this is done
+            b2 = k.reg("u32")
+            k(f"and.b32 {b2}, {gr}, 1")
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar_at('s_free', b2)}]")
+
     ml, me = k.label("m_unit"), k.label("m_unitend")
     k.place(ml)
     k(f"setp.ge.u32 {p}, {u2}, {units}")
@@ -686,76 +912,72 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     ph3 = k.reg("u32")
     k(f"and.b32 {ph3}, {uit2}, 1")
     cx.wait("bar_q_full", ph3, abort_l)
+    issue_qk(g2)
     j2 = k.reg("u32")
     k(f"mov.u32 {j2}, 0")
     mj = k.label("m_kv")
     k.place(mj)
-    ph4 = k.reg("u32")
-    k(f"and.b32 {ph4}, {kvit2}, 1")
-    cx.wait("bar_kv_full", ph4, abort_l)
-    k("tcgen05.fence::after_thread_sync")
-
-    def desc(addr_reg, off):
-        ad, r = k.reg("u32"), k.reg("u64")
-        k(f"add.u32 {ad}, {addr_reg}, {off}")
-        k(f"shr.u32 {ad}, {ad}, 4")
-        k(f"and.b32 {ad}, {ad}, 16383")
-        k(f"cvt.u64.u32 {r}, {ad}")
-        k(f"or.b64 {r}, {r}, 0x{kmaj:016X}")
-        return r
-
-    pairs = [(0, 0), (0, 1), (1, 0)] if f32 else [(0, 0)]
-    # S = Q . K^T over D, in atom-wide chunks of 4 MMA K-steps
-    first = True
-    for c in range(D // atom):
-        for kk in range(4):
-            for (ha, hb) in pairs:
-                a = desc(ring, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
-                b = desc(ring, lay[("k", hb)] + c * lay["k_chunk"] + kk * 32)
-                acc = yes
-                if first:
-                    acc = k.reg("pred")
-                    k(f"setp.ne.u32 {acc}, 0, 0")
-                    first = False
-                k(f"tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a}, {b}, {id_s}, {acc}")
-    k("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_s_full]")
-    # O (+)= P . V^T over the key block
-    cx.wait("bar_p_full", ph4, abort_l)
-    k("tcgen05.fence::after_thread_sync")
-    firstb = k.reg("pred")
-    k(f"setp.ne.u32 {firstb}, {j2}, 0")
-    first = True
-    for c in range(max(1, BKV // atom)):
-        for kk in range(min(4, BKV * e // 32)):
-            for (ha, hb) in pairs:
-                a = desc(ring, lay[("p", ha)] + c * lay["p_chunk"] + kk * 32)
-                b = desc(ring, lay[("v", hb)] + c * lay["v_chunk"] + kk * 32)
-                acc = firstb if first else yes
-                first = False
-                k(f"tcgen05.mma.cta_group::1.kind::{kind} [{o_t}], {a}, {b}, {id_o}, {acc}")
-    k("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
-    k("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_kv_empty]")
-    k(f"add.u32 {kvit2}, {kvit2}, 1")
-    k(f"add.u32 {j2}, {j2}, 1")
-    k(f"setp.lt.u32 {p}, {j2}, {nkv}")
-    k(f"@{p} bra {mj}")
-    k("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_q_empty]")
+    gn, jn = k.reg("u32"), k.reg("u32")
+    k(f"add.u32 {gn}, {g2}, 1")
+    k(f"add.u32 {jn}, {j2}, 1")
+    last = k.reg("pred")
+    k(f"setp.ge.u32 {last}, {jn}, {nkv}")
+    nxt = k.label("m_noqk")
+    if kvst > 1:
+        k(f"@{last} bra {nxt}")
+        issue_qk(gn)
+        k.place(nxt)
+        issue_pv(g2, j2)
+    else:
+        issue_pv(g2, j2)
+        k(f"@{last} bra {nxt}")
+        issue_qk(gn)
+        k.place(nxt)
+    k(f"mov.u32 {g2}, {gn}")
+    k(f"mov.u32 {j2}, {jn}")
+    k(f"@!{last} bra {mj}")
+    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_q_empty]")
     k(f"add.u32 {uit2}, {uit2}, 1")
     k(f"add.u32 {u2}, {u2}, {ncta}")
     k(f"bra.uni {ml}")
     k.place(me)
     k(f"bra.uni {teardown}")
 
-    # ================= softmax / correction / epilogue: warps 2-5 =================
+    # ================= softmax / correction / epilogue: warps 2-9 =================
+    # Two threads per query row: warps 2-5 take the first half of the key
+    # block's columns (and of O's), warps 6-9 the second half.  A warp may only
+    # touch TMEM lanes 32 * (warp % 4) .. +31, so both warps of a row pair sit
+    # on the same lane quarter; they swap partial row maxima through shared
+    # memory under a 64-thread named barrier (id 1 + quarter), the running
+    # sums stay per thread and are added once, in the epilogue.
     k.place(role_sm)
-    quad, row = k.reg("u32"), k.reg("u32")
+    if split == 2:
+        k.shared("\t.shared .align 16 .f32 xch_max[512];")    # [parity][half][row]
+        k.shared("\t.shared .align 16 .f32 xch_sum[256];")    # [half][row]
+    quad, row, half = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"and.b32 {quad}, {warp}, 3")
     k(f"mad.lo.u32 {row}, {quad}, 32, {lane}")
+    k(f"sub.u32 {half}, {warp}, 2")
+    k(f"shr.u32 {half}, {half}, 2")
+    bar_id = k.reg("u32")
+    k(f"add.u32 {bar_id}, {quad}, 1")
+    hs, ho = BKV // split, D // split       # columns of S and of O per thread
     lane_off = k.reg("u32")
     k(f"mul.lo.u32 {lane_off}, {quad}, {32 << 16}")
     s_row, o_row = k.reg("u32"), k.reg("u32")
     k(f"add.u32 {s_row}, {tmem}, {lane_off}")
-    k(f"add.u32 {o_row}, {s_row}, {s_cols}")
+    k(f"mad.lo.u32 {s_row}, {half}, {hs}, {s_row}")
+    k(f"add.u32 {o_row}, {tmem}, {lane_off}")
+    k(f"add.u32 {o_row}, {o_row}, {2 * s_cols}")
+    k(f"mad.lo.u32 {o_row}, {half}, {ho}, {o_row}")
+    if split == 2:
+        # exchange slots: mine and my partner's (same row, other half)
+        x_me, x_pa = k.reg("u32"), k.reg("u32")
+        k(f"mov.u32 {x_me}, xch_max")
+        k(f"mad.lo.u32 {x_me}, {row}, 4, {x_me}")
+        k(f"xor.b32 {x_pa}, {half}, 1")
+        k(f"mad.lo.u32 {x_pa}, {x_pa}, 512, {x_me}")
+        k(f"mad.lo.u32 {x_me}, {half}, 512, {x_me}")
     cr = k.reg("f32")
     k(f"ld.global.nc.f32 {cr}, [{base[plan.scale]}]")
     v1, sc2 = k.reg("f32"), k.reg("f32")
@@ -767,9 +989,23 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"and.b32 {rlo}, {row}, 7")
     k(f"mad.lo.u32 {prow}, {r8}, 1024, {ring}")
     k(f"mad.lo.u32 {prow}, {rlo}, 128, {prow}")
-    uit3, kvit3, u3 = k.reg("u32"), k.reg("u32"), k.reg("u32")
+    # this thread's 16-byte units of the P row: (column chunk, unit) pairs,
+    # the second half's offset folded into a register once
+    per16 = 16 // e
+    my_units = []
+    for U in range(hs // per16):
+        col = U * per16
+        my_units.append((col // atom, (col % atom) // per16, col))
+    u_first = k.reg("u32")            # global unit index of this half's first unit
+    k(f"mul.lo.u32 {u_first}, {half}, {hs // per16}")
+    p_half = k.reg("u32")             # byte offset of this half's first column chunk
+    k(f"mul.lo.u32 {p_half}, {half}, {(hs // atom) * lay['p_chunk'] if hs >= atom else 0}")
+    k(f"add.u32 {prow}, {prow}, {p_half}")
+    lane0 = k.reg("pred")
+    k(f"setp.eq.u32 {lane0}, {lane}, 0")
+    uit3, g3, u3 = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {uit3}, 0")
-    k(f"mov.u32 {kvit3}, 0")
+    k(f"mov.u32 {g3}, 0")
     k(f"mov.u32 {u3}, {cta}")
     sl, se = k.label("s_unit"), k.label("s_unitend")
     k.place(sl)
@@ -782,131 +1018,253 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"mov.u32 {j3}, 0")
     sj = k.label("s_kv")
     k.place(sj)
-    ph5 = k.reg("u32")
-    k(f"and.b32 {ph5}, {kvit3}, 1")
-    cx.wait("bar_s_full", ph5, abort_l)
+    sb, ph5 = k.reg("u32"), k.reg("u32")
+    k(f"and.b32 {sb}, {g3}, 1")
+    k(f"shr.u32 {ph5}, {g3}, 1")
+    k(f"and.b32 {ph5}, {ph5}, 1")
+    cx.wait(bar_at("s_full", sb), ph5, abort_l)
     k("bar.warp.sync -1")
     k("tcgen05.fence::after_thread_sync")
-    # S row -> registers (log2-scaled), row max
-    nreg = BKV
+    # my half of the S row -> registers
+    nreg = hs
     sv = k.regs("f32", nreg)
-    for c0 in range(0, BKV, 32):
-        cnt = min(32, BKV - c0)
+    s_cur = k.reg("u32")
+    k(f"mad.lo.u32 {s_cur}, {sb}, {s_cols}, {s_row}")
+    for c0 in range(0, nreg, 32):
+        cnt = min(32, nreg - c0)
         tad = k.reg("u32")
-        k(f"add.u32 {tad}, {s_row}, {c0}")
-        shape = f"32x32b.x{cnt}"
-        k(f"tcgen05.ld.sync.aligned.{shape}.b32 {{{', '.join(sv[c0:c0 + cnt])}}}, [{tad}]")
+        k(f"add.u32 {tad}, {s_cur}, {c0}")
+        k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(sv[c0:c0 + cnt])}}}, [{tad}]")
     k("tcgen05.wait::ld.sync.aligned")
+    if not p_tmem:
+        # this warp's share of S[g%2] is in registers: hand the buffer back
+        k("tcgen05.fence::before_thread_sync")
+        k("bar.warp.sync -1")
+        k(f"@{lane0} mbarrier.arrive.shared::cta.b64 _, [{bar_at('s_free', sb)}]")
+    # raw partial max in independent three-input chains; scaling by sc2 > 0
+    # is monotone, so max(s) * sc2 == max(s * sc2) exactly
+    nch = min(4, nreg)
+    mx = k.regs("f32", nch)
+    for i in range(nch):
+        k(f"mov.f32 {mx[i]}, {sv[i]}")
+    rest = sv[nch:]
+    for i in range(0, len(rest) - 1, 2):
+        c = mx[(i // 2) % nch]
+        k(f"max.f32 {c}, {c}, {rest[i]}, {rest[i + 1]}")
+    if len(rest) % 2:
+        k(f"max.f32 {mx[0]}, {mx[0]}, {rest[-1]}")
     mb = k.reg("f32")
-    k(f"mul.rn.f32 {sv[0]}, {sv[0]}, {sc2}")
-    k(f"mov.f32 {mb}, {sv[0]}")
-    for t in range(1, nreg):
-        k(f"mul.rn.f32 {sv[t]}, {sv[t]}, {sc2}")
-        k(f"max.f32 {mb}, {mb}, {sv[t]}")
-    # previous P . V done before P is overwritten or O rescaled
+    k(f"mov.f32 {mb}, {mx[0]}")
+    for i in range(1, nch):
+        k(f"max.f32 {mb}, {mb}, {mx[i]}")
+    # swap partial maxima with the partner thread (slots double-buffered by
+    # block parity, so a slot is rewritten only after the partner read it)
+    if split == 2:
+        xo = k.reg("u32")
+        k(f"mul.lo.u32 {xo}, {sb}, 1024")
+        xa, xb = k.reg("u32"), k.reg("u32")
+        k(f"add.u32 {xa}, {x_me}, {xo}")
+        k(f"add.u32 {xb}, {x_pa}, {xo}")
+        k(f"st.shared.f32 [{xa}], {mb}")
+        k(f"barrier.sync {bar_id}, 64")
+        mo = k.reg("f32")
+        k(f"ld.shared.f32 {mo}, [{xb}]")
+        k(f"max.f32 {mb}, {mb}, {mo}")
+    k(f"mul.rn.f32 {mb}, {mb}, {sc2}")
     pnot0 = k.reg("pred")
     k(f"setp.ne.u32 {pnot0}, {j3}, 0")
-    wprev = k.label("nowaitpv")
-    k(f"@!{pnot0} bra {wprev}")
-    php = k.reg("u32")
-    k(f"sub.u32 {php}, {kvit3}, 1")
-    k(f"and.b32 {php}, {php}, 1")
-    cx.wait("bar_pv_done", php, abort_l)
-    k.place(wprev)
-    # conditional rescale, warp-uniform
+    # conditional rescale of the running max and sum (registers only; the O
+    # columns in TMEM are rescaled below, once the previous P . V is done)
     need = k.reg("pred")
     thr = k.reg("f32")
     k(f"add.rn.f32 {thr}, {m_run}, {f32_hex(RESCALE_T)}")
     k(f"setp.gt.f32 {need}, {mb}, {thr}")
     anyn = k.reg("pred")
     k(f"vote.sync.any.pred {anyn}, {need}, -1")
+    alpha = k.reg("f32")
+    k(f"mov.f32 {alpha}, 0f3F800000")
     norsc = k.label("norescale")
     k(f"@!{anyn} bra {norsc}")
-    m_new, alpha, dlt = k.reg("f32"), k.reg("f32"), k.reg("f32")
+    m_new, dlt = k.reg("f32"), k.reg("f32")
     k(f"max.f32 {m_new}, {m_run}, {mb}")
     k(f"sub.rn.f32 {dlt}, {m_run}, {m_new}")
     k(f"ex2.approx.ftz.f32 {alpha}, {dlt}")
     k(f"mul.rn.f32 {l_run}, {l_run}, {alpha}")
     k(f"mov.f32 {m_run}, {m_new}")
-    # O row *= alpha (only after the first block has written O)
-    k(f"@!{pnot0} bra {norsc}")
-    k("tcgen05.fence::after_thread_sync")
-    for c0 in range(0, D, 32):
-        ov = k.regs("f32", 32)
-        tad = k.reg("u32")
-        k(f"add.u32 {tad}, {o_row}, {c0}")
-        k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{tad}]")
-        k("tcgen05.wait::ld.sync.aligned")
-        for t in range(32):
-            k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {alpha}")
-        k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{tad}], {{{', '.join(ov)}}}")
-    k("tcgen05.wait::st.sync.aligned")
     k.place(norsc)
-    # P = exp2(s - m), row sum, P -> smem (K-major, 128-byte swizzle)
-    for t in range(nreg):
-        k(f"sub.rn.f32 {sv[t]}, {sv[t]}, {m_run}")
-        k(f"ex2.approx.ftz.f32 {sv[t]}, {sv[t]}")
-        k(f"add.rn.f32 {l_run}, {l_run}, {sv[t]}")
-    per16 = 16 // e                       # elements per 16-byte unit
-    for c in range(max(1, BKV // atom)):
-        for uidx in range(min(8, BKV * e // 16)):
-            vals = sv[c * atom + uidx * per16: c * atom + (uidx + 1) * per16]
+    # p = exp2(s * sc2 - m) with packed f32x2 FMAs, sums in eight partials
+    sc2x2, negm2 = k.reg("b64"), k.reg("b64")
+    negm = k.reg("f32")
+    k(f"neg.f32 {negm}, {m_run}")
+    k(f"mov.b64 {sc2x2}, {{{sc2}, {sc2}}}")
+    k(f"mov.b64 {negm2}, {{{negm}, {negm}}}")
+    nacc = min(4, nreg // 2)
+    acc2 = k.regs("b64", nacc)
+    zf = k.reg("f32")
+    k(f"mov.f32 {zf}, {f32_hex(0.0)}")
+    for i in range(nacc):
+        k(f"mov.b64 {acc2[i]}, {{{zf}, {zf}}}")
+    poly = 0 if f32 else _exp_poly_share()
+    pconsts = _exp2_poly_consts(k) if poly else None
+    for t in range(0, nreg, 2):
+        pr = k.reg("b64")
+        k(f"mov.b64 {pr}, {{{sv[t]}, {sv[t + 1]}}}")
+        k(f"fma.rn.f32x2 {pr}, {pr}, {sc2x2}, {negm2}")
+        if (t // 2) % 4 < poly:
+            sv[t], sv[t + 1] = _exp2_poly_pair(k, pr, pconsts)
+            k(f"mov.b64 {pr}, {{{sv[t]}, {sv[t + 1]}}}")
+        else:
+            k(f"mov.b64 {{{sv[t]}, {sv[t + 1]}}}, {pr}")
+            k(f"ex2.approx.ftz.f32 {sv[t]}, {sv[t]}")
+            k(f"ex2.approx.ftz.f32 {sv[t + 1]}, {sv[t + 1]}")
+            k(f"mov.b64 {pr}, {{{sv[t]}, {sv[t + 1]}}}")
+        acc = acc2[(t // 2) % nacc]
+        k(f"add.rn.f32x2 {acc}, {acc}, {pr}")
+    for i in range(1, nacc):
+        k(f"add.rn.f32x2 {acc2[0]}, {acc2[0]}, {acc2[i]}")
+    sa, sb_ = k.reg("f32"), k.reg("f32")
+    k(f"mov.b64 {{{sa}, {sb_}}}, {acc2[0]}")
+    k(f"add.rn.f32 {sa}, {sa}, {sb_}")
+    k(f"add.rn.f32 {l_run}, {l_run}, {sa}")
+    # P in the MMA operand format, still in registers
+    units16 = []
+    for (c, uidx, col) in my_units:
+        vals = sv[col: col + per16]
+        if f32:
+            hi, lo_ = k.regs("b32", 4), k.regs("f32", 4)
+            for t in range(4):
+                k(f"and.b32 {hi[t]}, {vals[t]}, -8192")
+                k(f"sub.rn.f32 {lo_[t]}, {vals[t]}, {hi[t]}")
+            units16.append((c, uidx, hi, lo_))
+        else:
+            pk = k.regs("b32", 4)
+            for t in range(4):
+                k(f"cvt.rn.bf16x2.f32 {pk[t]}, {vals[2 * t + 1]}, {vals[2 * t]}")
+            units16.append((c, uidx, pk, None))
+    def rescale_o():
+        """my O columns *= alpha (after the previous P . V is done)"""
+        k("tcgen05.fence::after_thread_sync")
+        for c0 in range(0, ho, 32):
+            cnt = min(32, ho - c0)
+            ov = k.regs("f32", cnt)
+            tad = k.reg("u32")
+            k(f"add.u32 {tad}, {o_row}, {c0}")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
+            k("tcgen05.wait::ld.sync.aligned")
+            for t in range(cnt):
+                k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {alpha}")
+            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], {{{', '.join(ov)}}}")
+        k("tcgen05.wait::st.sync.aligned")
+
+    def wait_prev_pv():
+        php = k.reg("u32")
+        k(f"sub.u32 {php}, {g3}, 1")
+        k(f"and.b32 {php}, {php}, 1")
+        cx.wait("bar_pv_done", php, abort_l)
+
+    if p_tmem:
+        # P (packed bf16) over the first half of this row's S columns; the
+        # partner thread's S columns it overwrites were loaded before the
+        # max exchange above
+        packed = [r for (_c, _u, regs, _lo) in units16 for r in regs]
+        p_cur = k.reg("u32")
+        k(f"mad.lo.u32 {p_cur}, {sb}, {s_cols}, {tmem}")
+        k(f"add.u32 {p_cur}, {p_cur}, {lane_off}")
+        k(f"mad.lo.u32 {p_cur}, {half}, {hs // 2}, {p_cur}")
+        for c0 in range(0, len(packed), 32):
+            cnt = min(32, len(packed) - c0)
+            tad = k.reg("u32")
+            k(f"add.u32 {tad}, {p_cur}, {c0}")
+            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], {{{', '.join(packed[c0:c0 + cnt])}}}")
+        k("tcgen05.wait::st.sync.aligned")
+        # O is only touched when some row of this warp moved its max: then the
+        # previous P . V must be done first
+        nor2 = k.label("noorescale")
+        k(f"@!{anyn} bra {nor2}")
+        k(f"@!{pnot0} bra {nor2}")
+        wait_prev_pv()
+        rescale_o()
+        k.place(nor2)
+    else:
+        # the previous P . V must be done before P is overwritten or O rescaled
+        wprev = k.label("nowaitpv")
+        k(f"@!{pnot0} bra {wprev}")
+        wait_prev_pv()
+        nor2 = k.label("noorescale")
+        k(f"@!{anyn} bra {nor2}")
+        rescale_o()
+        k.place(nor2)
+        k.place(wprev)
+        # P -> smem (K-major, 128-byte swizzle: 16-byte unit u of row r at u ^ (r % 8));
+        # the second half's units start ``hs`` columns in, which is whole chunks
+        # when hs >= atom and otherwise half a chunk (units 8 * hs / atom on)
+        for (c, uidx, r0, r1) in units16:
             sw, ad = k.reg("u32"), k.reg("u32")
-            k(f"xor.b32 {sw}, {rlo}, {uidx}")
-            k(f"mad.lo.u32 {ad}, {sw}, 16, {prow}")
-            if f32:
-                hi, lo_ = k.regs("b32", 4), k.regs("f32", 4)
-                for t in range(4):
-                    k(f"and.b32 {hi[t]}, {vals[t]}, -8192")
-                    k(f"sub.rn.f32 {lo_[t]}, {vals[t]}, {hi[t]}")
-                k(f"st.shared.v4.b32 [{ad}+{lay[('p', 0)] + c * lay['p_chunk']}], "
-                  f"{{{', '.join(hi)}}}")
-                k(f"st.shared.v4.f32 [{ad}+{lay[('p', 1)] + c * lay['p_chunk']}], "
-                  f"{{{', '.join(lo_)}}}")
+            if hs >= atom:
+                k(f"xor.b32 {sw}, {rlo}, {uidx}")
             else:
-                pk = k.regs("b32", 4)
-                for t in range(4):
-                    k(f"cvt.rn.bf16x2.f32 {pk[t]}, {vals[2 * t + 1]}, {vals[2 * t]}")
-                k(f"st.shared.v4.b32 [{ad}+{lay[('p', 0)] + c * lay['p_chunk']}], "
-                  f"{{{', '.join(pk)}}}")
-    k("fence.proxy.async.shared::cta")
+                k(f"add.u32 {sw}, {u_first}, {uidx}")
+                k(f"xor.b32 {sw}, {sw}, {rlo}")
+            k(f"mad.lo.u32 {ad}, {sw}, 16, {prow}")
+            k(f"st.shared.v4.b32 [{ad}+{lay[('p', 0)] + c * lay['p_chunk']}], {{{', '.join(r0)}}}")
+            if r1 is not None:
+                k(f"st.shared.v4.f32 [{ad}+{lay[('p', 1)] + c * lay['p_chunk']}], "
+                  f"{{{', '.join(r1)}}}")
+        k("fence.proxy.async.shared::cta")
     k("tcgen05.fence::before_thread_sync")
     k("mbarrier.arrive.shared::cta.b64 _, [bar_p_full]")
-    k(f"add.u32 {kvit3}, {kvit3}, 1")
+    k(f"add.u32 {g3}, {g3}, 1")
     k(f"add.u32 {j3}, {j3}, 1")
     k(f"setp.lt.u32 {p}, {j3}, {nkv}")
     k(f"@{p} bra {sj}")
-    # epilogue: last P . V done, out = O * (1/l)
+    # epilogue: the two partial sums, last P . V done, out = O * (1/l)
+    lo_sum = k.reg("f32")
+    if split == 2:
+        xs, xp = k.reg("u32"), k.reg("u32")
+        k(f"mov.u32 {xs}, xch_sum")
+        k(f"mad.lo.u32 {xs}, {row}, 4, {xs}")
+        k(f"xor.b32 {xp}, {half}, 1")
+        k(f"mad.lo.u32 {xp}, {xp}, 512, {xs}")
+        k(f"mad.lo.u32 {xs}, {half}, 512, {xs}")
+        k(f"st.shared.f32 [{xs}], {l_run}")
+        k(f"barrier.sync {bar_id}, 64")
+        k(f"ld.shared.f32 {lo_sum}, [{xp}]")
+        # both threads add the same two numbers (commutative), so agree on l
+        k(f"add.rn.f32 {lo_sum}, {l_run}, {lo_sum}")
+    else:
+        k(f"mov.f32 {lo_sum}, {l_run}")
     phl = k.reg("u32")
-    k(f"sub.u32 {phl}, {kvit3}, 1")
+    k(f"sub.u32 {phl}, {g3}, 1")
     k(f"and.b32 {phl}, {phl}, 1")
     cx.wait("bar_pv_done", phl, abort_l)
     k("bar.warp.sync -1")
     k("tcgen05.fence::after_thread_sync")
     rl = k.reg("f32")
-    k(f"rcp.rn.f32 {rl}, {l_run}")
+    k(f"rcp.rn.f32 {rl}, {lo_sum}")
     bh3, qb3 = unit_coords(u3)
     grow = k.reg("u32")
     k(f"mad.lo.u32 {grow}, {bh3}, {S}, {row}")
     k(f"mad.lo.u32 {grow}, {qb3}, {BQ}, {grow}")
     k(f"mul.lo.u32 {grow}, {grow}, {D}")
+    k(f"mad.lo.u32 {grow}, {half}, {ho}, {grow}")
     optr = k.addr(base[plan.out], grow, e)
-    for c0 in range(0, D, 32):
-        ov = k.regs("f32", 32)
+    for c0 in range(0, ho, 32):
+        cnt = min(32, ho - c0)
+        ov = k.regs("f32", cnt)
         tad = k.reg("u32")
         k(f"add.u32 {tad}, {o_row}, {c0}")
-        k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{tad}]")
+        k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
         k("tcgen05.wait::ld.sync.aligned")
-        for t in range(32):
+        for t in range(cnt):
             k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {rl}")
         if f32:
-            for v in range(8):
+            for v in range(cnt // 4):
                 k(f"st.global.v4.f32 [{optr}+{(c0 + 4 * v) * 4}], {{{', '.join(ov[4 * v:4 * v + 4])}}}")
         else:
-            pk = k.regs("b32", 16)
-            for t in range(16):
+            pk = k.regs("b32", cnt // 2)
+            for t in range(cnt // 2):
                 k(f"cvt.rn.bf16x2.f32 {pk[t]}, {ov[2 * t + 1]}, {ov[2 * t]}")
-            for v in range(4):
+            for v in range(cnt // 8):
                 k(f"st.global.v4.b32 [{optr}+{(c0 + 8 * v) * 2}], {{{', '.join(pk[4 * v:4 * v + 4])}}}")
     k("tcgen05.fence::before_thread_sync")
     k(f"add.u32 {uit3}, {uit3}, 1")

@@ -171,9 +171,14 @@ class _Ctx:
         t0, t1 = k.reg("u64"), k.reg("u64")
         ab = k.reg("u32")
         loop, done, to = k.label("wt"), k.label("wtok"), k.label("wtto")
+        # fast path: a phase that is already complete costs one try_wait
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar_addr}], {parity}")
+        k(f"@{p} bra {done}")
         k(f"mov.u64 {t0}, %globaltimer")
         k.place(loop)
-        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar_addr}], {parity}")
+        # the hint lets the warp sleep (up to SUSPEND_HINT_NS) until the phase
+        # completes instead of spinning on issue slots its neighbours need
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar_addr}], {parity}, {SUSPEND_HINT_NS}")
         k(f"@{p} bra {done}")
         k(f"ld.volatile.shared.u32 {ab}, [abort_flag]")
         k(f"setp.ne.u32 {p}, {ab}, 0")
@@ -186,6 +191,9 @@ class _Ctx:
         k(f"st.global.u32 [emmy_err], {code}")
         k(f"bra.uni {abort_label}")
         k.place(done)
+
+
+SUSPEND_HINT_NS = 100000
 
 
 def _desc_const(lbo: int, sbo: int, layout: int) -> int:

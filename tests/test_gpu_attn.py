@@ -62,7 +62,9 @@ def _bhsd(b, h, s, d, dtype, seed=0):
 
 
 @pytest.mark.parametrize("dtype,shape", [("f32", (2, 2, 256, 64)), ("f32", (1, 3, 384, 128)),
-                                         ("bf16", (2, 2, 256, 128)), ("bf16", (1, 2, 512, 64))])
+                                         ("f32", (1, 2, 256, 32)),
+                                         ("bf16", (2, 2, 256, 128)), ("bf16", (1, 2, 512, 64)),
+                                         ("bf16", (1, 2, 256, 256))])
 def test_generated(dtype, shape):
     b, h, s, d = shape
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "att")
@@ -72,6 +74,18 @@ def test_generated(dtype, shape):
     scale = np.abs(ref).max()
     tol = 1e-4 if dtype == "f32" else 2e-2
     assert np.abs(out - ref).max() <= tol * scale, float(np.abs(out - ref).max() / scale)
+
+
+@pytest.mark.parametrize("share", [2, 4])
+def test_bf16_polynomial_exp2(share, monkeypatch):
+    """bf16 P with part (or all) of exp2 evaluated by the FMA-pipe polynomial."""
+    monkeypatch.setenv("EMMY_ATTN_EXP_POLY", str(share))
+    b, h, s, d = 2, 2, 512, 128
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "attp")
+    q, k, v = _bhsd(b, h, s, d, "bf16", seed=11)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
+    ref = _ref(q, k, v)
+    assert np.abs(out - ref).max() <= 2e-2 * np.abs(ref).max()
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
