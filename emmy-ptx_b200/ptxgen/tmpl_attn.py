@@ -157,12 +157,8 @@ def _layout(plan):
     k_bytes = (d // atom) * k_chunk
     v_chunk = d * 128                  # V^T: d rows, one atom of keys wide
     v_bytes = max(1, bkv // atom) * v_chunk
-    p_chunk = BQ * 128
-    # bf16 P lives in TMEM (over its own S columns) and feeds the P . V MMA
-    # from there; f32 (hi/lo TF32) P is staged in shared memory
-    p_tmem = plan.dtype != "f32"
-    p_bytes = 0 if p_tmem else max(1, bkv // atom) * p_chunk
-    base = halves * (q_bytes + p_bytes)
+    # (P is not staged here: it lives in TMEM over its own S columns)
+    base = halves * q_bytes
     per_stage = halves * (k_bytes + v_bytes)
     kvst = 2 if base + 2 * per_stage + 1024 <= 232448 - 2048 else 1
     lay = {}
@@ -175,18 +171,14 @@ def _layout(plan):
             for h in range(halves):
                 lay[(name, st, h)] = off
                 off += size
-    for h in range(halves):
-        lay[("p", h)] = off
-        off += p_bytes
     lay["total"] = off
     # two softmax threads per query row (warps 2-9) when the exchange slots
     # fit beside the dynamic layout, else one (warps 2-5)
     split = 2 if off + 1024 + XCH_STATIC <= SMEM_MAX else 1
     lay["split"] = split
-    lay["p_tmem"] = p_tmem
     lay["threads"] = 64 + 128 * split
-    lay.update(q_bytes=q_bytes, k_bytes=k_bytes, v_bytes=v_bytes, p_bytes=p_bytes,
-               q_chunk=q_chunk, k_chunk=k_chunk, v_chunk=v_chunk, p_chunk=p_chunk,
+    lay.update(q_bytes=q_bytes, k_bytes=k_bytes, v_bytes=v_bytes,
+               q_chunk=q_chunk, k_chunk=k_chunk, v_chunk=v_chunk,
                halves=halves, kvst=kvst)
     return lay
 
@@ -630,7 +622,9 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k.shared("\t.shared .align 4 .u32 abort_flag;")
     # TMEM: two S buffers (the MMA warp fills one while the softmax warps
     # read the other), then O
-    s_cols = max(32, BKV)
+    # an S buffer: BKV f32 score columns; for f32 data also the TF32 lo half
+    # of P beside them (hi overwrites the scores)
+    s_cols = max(32, BKV * (2 if f32 else 1))
     tcols = 1 << (2 * s_cols + D - 1).bit_length()
     warp, lane = k.reg("u32"), k.reg("u32")
     k(f"shr.u32 {warp}, {tid}, 5")
@@ -652,12 +646,11 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"setp.ne.u32 {p}, {tid}, 0")
     k(f"@{p} bra {skip}")
     split = lay["split"]
-    p_tmem = lay["p_tmem"]
     for nm, cnt in (("q_full", 1), ("q_empty", 1), ("p_full", 128 * split), ("pv_done", 1),
                     ("drain", 1)):
         k(f"mbarrier.init.shared::cta.b64 [bar_{nm}], {cnt}")
     for nm, n, cnt in (("k_full", kvst, 1), ("k_empty", kvst, 1), ("v_full", kvst, 1),
-                       ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1 if p_tmem else 4 * split)):
+                       ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1)):
         for i in range(n):
             k(f"mbarrier.init.shared::cta.b64 [bar_{nm}+{8 * i}], {cnt}")
     k("st.shared.u32 [abort_flag], 0")
@@ -877,20 +870,19 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         cx.wait("bar_p_full", php_, abort_l)
         cx.wait(bar_at("v_full", st_), phf_, abort_l)
         k("tcgen05.fence::after_thread_sync")
-        if p_tmem:
-            pb = k.reg("u32")                 # P_g: packed bf16 over S buffer g % 2
-            k(f"and.b32 {pb}, {gr}, 1")
-            k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
+        pb, b2 = k.reg("u32"), k.reg("u32")   # P_g lives in S buffer g % 2
+        k(f"and.b32 {b2}, {gr}, 1")
+        k(f"mov.u32 {pb}, {b2}")
+        k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
         first = True
         for c in range(max(1, BKV // atom)):
             for kk in range(min(4, BKV * e // 32)):
                 for (ha, hb) in pairs:
-                    if p_tmem:
-                        a_ = k.reg("u32")     # 16 keys per K-step = 8 packed columns
-                        k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8}")
-                        a_ = f"[{a_}]"
-                    else:
-                        a_ = dsc(d_base, lay[("p", ha)] + c * lay["p_chunk"] + kk * 32)
+                    # A (P) from TMEM: a 32-byte K-step is 8 columns (16 packed
+                    # bf16 or 8 f32); the f32 lo half sits BKV columns on
+                    a_ = k.reg("u32")
+                    k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8 + ha * BKV}")
+                    a_ = f"[{a_}]"
                     b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
                     acc = firstb if first else yes
                     first = False
@@ -898,12 +890,9 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
         k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
           f"[{bar_at('v_empty', st_)}]")
-        if p_tmem:
-            # P_g was read from S buffer g % 2: the buffer is free once this is done
-            b2 = k.reg("u32")
-            k(f"and.b32 {b2}, {gr}, 1")
-            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar_at('s_free', b2)}]")
+        # P_g was read from S buffer g % 2: the buffer is free once this is done
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+          f"[{bar_at('s_free', b2)}]")
 
     ml, me = k.label("m_unit"), k.label("m_unitend")
     k.place(ml)
@@ -983,26 +972,6 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     v1, sc2 = k.reg("f32"), k.reg("f32")
     k(f"rcp.rn.f32 {v1}, {cr}")
     k(f"mul.rn.f32 {sc2}, {v1}, {f32_hex(LOG2E)}")   # scores to log2 units
-    # smem P row address pieces: chunk base + (row/8)*1024 + (row%8)*128; swizzle by row%8
-    r8, rlo, prow = k.reg("u32"), k.reg("u32"), k.reg("u32")
-    k(f"shr.u32 {r8}, {row}, 3")
-    k(f"and.b32 {rlo}, {row}, 7")
-    k(f"mad.lo.u32 {prow}, {r8}, 1024, {ring}")
-    k(f"mad.lo.u32 {prow}, {rlo}, 128, {prow}")
-    # this thread's 16-byte units of the P row: (column chunk, unit) pairs,
-    # the second half's offset folded into a register once
-    per16 = 16 // e
-    my_units = []
-    for U in range(hs // per16):
-        col = U * per16
-        my_units.append((col // atom, (col % atom) // per16, col))
-    u_first = k.reg("u32")            # global unit index of this half's first unit
-    k(f"mul.lo.u32 {u_first}, {half}, {hs // per16}")
-    p_half = k.reg("u32")             # byte offset of this half's first column chunk
-    k(f"mul.lo.u32 {p_half}, {half}, {(hs // atom) * lay['p_chunk'] if hs >= atom else 0}")
-    k(f"add.u32 {prow}, {prow}, {p_half}")
-    lane0 = k.reg("pred")
-    k(f"setp.eq.u32 {lane0}, {lane}, 0")
     uit3, g3, u3 = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {uit3}, 0")
     k(f"mov.u32 {g3}, 0")
@@ -1036,11 +1005,6 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         k(f"add.u32 {tad}, {s_cur}, {c0}")
         k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(sv[c0:c0 + cnt])}}}, [{tad}]")
     k("tcgen05.wait::ld.sync.aligned")
-    if not p_tmem:
-        # this warp's share of S[g%2] is in registers: hand the buffer back
-        k("tcgen05.fence::before_thread_sync")
-        k("bar.warp.sync -1")
-        k(f"@{lane0} mbarrier.arrive.shared::cta.b64 _, [{bar_at('s_free', sb)}]")
     # raw partial max in independent three-input chains; scaling by sc2 > 0
     # is monotone, so max(s) * sc2 == max(s * sc2) exactly
     nch = min(4, nreg)
@@ -1126,91 +1090,56 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"mov.b64 {{{sa}, {sb_}}}, {acc2[0]}")
     k(f"add.rn.f32 {sa}, {sa}, {sb_}")
     k(f"add.rn.f32 {l_run}, {l_run}, {sa}")
-    # P in the MMA operand format, still in registers
-    units16 = []
-    for (c, uidx, col) in my_units:
-        vals = sv[col: col + per16]
-        if f32:
-            hi, lo_ = k.regs("b32", 4), k.regs("f32", 4)
-            for t in range(4):
-                k(f"and.b32 {hi[t]}, {vals[t]}, -8192")
-                k(f"sub.rn.f32 {lo_[t]}, {vals[t]}, {hi[t]}")
-            units16.append((c, uidx, hi, lo_))
-        else:
-            pk = k.regs("b32", 4)
-            for t in range(4):
-                k(f"cvt.rn.bf16x2.f32 {pk[t]}, {vals[2 * t + 1]}, {vals[2 * t]}")
-            units16.append((c, uidx, pk, None))
-    def rescale_o():
-        """my O columns *= alpha (after the previous P . V is done)"""
-        k("tcgen05.fence::after_thread_sync")
-        for c0 in range(0, ho, 32):
-            cnt = min(32, ho - c0)
-            ov = k.regs("f32", cnt)
-            tad = k.reg("u32")
-            k(f"add.u32 {tad}, {o_row}, {c0}")
-            k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
-            k("tcgen05.wait::ld.sync.aligned")
-            for t in range(cnt):
-                k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {alpha}")
-            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], {{{', '.join(ov)}}}")
-        k("tcgen05.wait::st.sync.aligned")
-
-    def wait_prev_pv():
-        php = k.reg("u32")
-        k(f"sub.u32 {php}, {g3}, 1")
-        k(f"and.b32 {php}, {php}, 1")
-        cx.wait("bar_pv_done", php, abort_l)
-
-    if p_tmem:
-        # P (packed bf16) over the first half of this row's S columns; the
-        # partner thread's S columns it overwrites were loaded before the
-        # max exchange above
-        packed = [r for (_c, _u, regs, _lo) in units16 for r in regs]
-        p_cur = k.reg("u32")
-        k(f"mad.lo.u32 {p_cur}, {sb}, {s_cols}, {tmem}")
-        k(f"add.u32 {p_cur}, {p_cur}, {lane_off}")
-        k(f"mad.lo.u32 {p_cur}, {half}, {hs // 2}, {p_cur}")
-        for c0 in range(0, len(packed), 32):
-            cnt = min(32, len(packed) - c0)
-            tad = k.reg("u32")
-            k(f"add.u32 {tad}, {p_cur}, {c0}")
-            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], {{{', '.join(packed[c0:c0 + cnt])}}}")
-        k("tcgen05.wait::st.sync.aligned")
-        # O is only touched when some row of this warp moved its max: then the
-        # previous P . V must be done first
-        nor2 = k.label("noorescale")
-        k(f"@!{anyn} bra {nor2}")
-        k(f"@!{pnot0} bra {nor2}")
-        wait_prev_pv()
-        rescale_o()
-        k.place(nor2)
+    # P in the MMA operand format: TF32 hi/lo (f32) or packed bf16 pairs
+    if f32:
+        p_hi, p_lo = k.regs("b32", nreg), k.regs("f32", nreg)
+        for t in range(nreg):
+            k(f"and.b32 {p_hi[t]}, {sv[t]}, -8192")
+            k(f"sub.rn.f32 {p_lo[t]}, {sv[t]}, {p_hi[t]}")
+        pieces = [(p_hi, 0), (p_lo, BKV)]
     else:
-        # the previous P . V must be done before P is overwritten or O rescaled
-        wprev = k.label("nowaitpv")
-        k(f"@!{pnot0} bra {wprev}")
-        wait_prev_pv()
-        nor2 = k.label("noorescale")
-        k(f"@!{anyn} bra {nor2}")
-        rescale_o()
-        k.place(nor2)
-        k.place(wprev)
-        # P -> smem (K-major, 128-byte swizzle: 16-byte unit u of row r at u ^ (r % 8));
-        # the second half's units start ``hs`` columns in, which is whole chunks
-        # when hs >= atom and otherwise half a chunk (units 8 * hs / atom on)
-        for (c, uidx, r0, r1) in units16:
-            sw, ad = k.reg("u32"), k.reg("u32")
-            if hs >= atom:
-                k(f"xor.b32 {sw}, {rlo}, {uidx}")
-            else:
-                k(f"add.u32 {sw}, {u_first}, {uidx}")
-                k(f"xor.b32 {sw}, {sw}, {rlo}")
-            k(f"mad.lo.u32 {ad}, {sw}, 16, {prow}")
-            k(f"st.shared.v4.b32 [{ad}+{lay[('p', 0)] + c * lay['p_chunk']}], {{{', '.join(r0)}}}")
-            if r1 is not None:
-                k(f"st.shared.v4.f32 [{ad}+{lay[('p', 1)] + c * lay['p_chunk']}], "
-                  f"{{{', '.join(r1)}}}")
-        k("fence.proxy.async.shared::cta")
+        pk = k.regs("b32", nreg // 2)
+        for t in range(nreg // 2):
+            k(f"cvt.rn.bf16x2.f32 {pk[t]}, {sv[2 * t + 1]}, {sv[2 * t]}")
+        pieces = [(pk, 0)]
+    # P over this row's S columns in S buffer g % 2: f32 hi over the thread's
+    # own score columns and lo BKV columns on; bf16 packed into the first half
+    # of the row, whose partner-owned scores were loaded before the max
+    # exchange above
+    p_cur = k.reg("u32")
+    k(f"mad.lo.u32 {p_cur}, {sb}, {s_cols}, {tmem}")
+    k(f"add.u32 {p_cur}, {p_cur}, {lane_off}")
+    k(f"mad.lo.u32 {p_cur}, {half}, {hs if f32 else hs // 2}, {p_cur}")
+    for regs, off in pieces:
+        for c0 in range(0, len(regs), 32):
+            cnt = min(32, len(regs) - c0)
+            tad = k.reg("u32")
+            k(f"add.u32 {tad}, {p_cur}, {off + c0}")
+            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], "
+              f"{{{', '.join(regs[c0:c0 + cnt])}}}")
+    k("tcgen05.wait::st.sync.aligned")
+    # O is only touched when some row of this warp moved its max; then the
+    # previous P . V must be done first
+    nor2 = k.label("noorescale")
+    k(f"@!{anyn} bra {nor2}")
+    k(f"@!{pnot0} bra {nor2}")
+    php = k.reg("u32")
+    k(f"sub.u32 {php}, {g3}, 1")
+    k(f"and.b32 {php}, {php}, 1")
+    cx.wait("bar_pv_done", php, abort_l)
+    k("tcgen05.fence::after_thread_sync")
+    for c0 in range(0, ho, 32):
+        cnt = min(32, ho - c0)
+        ov = k.regs("f32", cnt)
+        tad = k.reg("u32")
+        k(f"add.u32 {tad}, {o_row}, {c0}")
+        k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
+        k("tcgen05.wait::ld.sync.aligned")
+        for t in range(cnt):
+            k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {alpha}")
+        k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tad}], {{{', '.join(ov)}}}")
+    k("tcgen05.wait::st.sync.aligned")
+    k.place(nor2)
     k("tcgen05.fence::before_thread_sync")
     k("mbarrier.arrive.shared::cta.b64 _, [bar_p_full]")
     k(f"add.u32 {g3}, {g3}, 1")
