@@ -16,4 +16,11 @@ def run_kernel(spec, inputs, **kw):
     return _run(spec, inputs, **kw)
 
 
-__all__ = ["load_kernel", "compile_kernel", "compile_file", "run_kernel"]
+def run_problem(pdir, **kw):
+    """Run every kernel of a problem directory in meta.json order on the
+    local B200, intermediates chained on the device (``submit.py:80-159``)."""
+    from .problem import run_problem as _run
+    return _run(pdir, **kw)
+
+
+__all__ = ["load_kernel", "compile_kernel", "compile_file", "run_kernel", "run_problem"]

@@ -61,12 +61,17 @@ def select_template(spec: KernelSpec):
     return None, reasons, None
 
 
-def compile_module(spec: KernelSpec, generic: bool = False):
+def compile_module(spec: KernelSpec, generic: bool = False, checked: bool = False):
     """Return the ``ptx.Module`` for ``spec`` (plan header included);
-    ``generic=True`` (or ``EMMY_TEMPLATE=generic``) skips the templates."""
-    if generic or os.environ.get("EMMY_TEMPLATE") == "generic":
+    ``generic=True`` (or ``EMMY_TEMPLATE=generic``) skips the templates.
+    ``checked=True`` (or ``EMMY_CHECKED=1``) is the range-checked variant:
+    the generic lowering with every global and shared index checked against
+    its buffer; a violation skips the access and is reported through
+    ``emmy_err`` (0x301) with the first offending buffer and index."""
+    checked = checked or os.environ.get("EMMY_CHECKED", "") not in ("", "0")
+    if checked or generic or os.environ.get("EMMY_TEMPLATE") == "generic":
         from . import generic as g
-        mod = g.emit_generic(spec)
+        mod = g.emit_generic(spec, checked=checked)
         mod.plan.setdefault("template", "generic")
         return mod
     name, plan, emit = select_template(spec)
@@ -88,9 +93,9 @@ def compile_module(spec: KernelSpec, generic: bool = False):
         raise NotImplementedError(f"no template accepts this IR ({why}); generic lowering: {exc}")
 
 
-def compile_kernel(spec: KernelSpec, generic: bool = False) -> str:
+def compile_kernel(spec: KernelSpec, generic: bool = False, checked: bool = False) -> str:
     """``KernelSpec`` -> PTX text (``ptxgen/emit.py:1553``)."""
-    return compile_module(spec, generic=generic).render()
+    return compile_module(spec, generic=generic, checked=checked).render()
 
 
 def compile_file(path: str | Path) -> str:

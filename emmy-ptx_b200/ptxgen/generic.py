@@ -43,11 +43,21 @@ def _collective(body) -> bool:
     return any(isinstance(s, (ir.Sync, ir.TreeHalve, ir.WarpShuffle)) for s in ir.walk(body))
 
 
+ERR_OOB = 0x301          # checked mode: an index outside its buffer (access skipped)
+
+
 class Generic:
-    def __init__(self, spec: KernelSpec):
+    def __init__(self, spec: KernelSpec, checked: bool = False):
         self.spec = spec
-        self.mod = Module(comment=f"emmy-b200 generic lowering for {spec.entry}")
+        self.checked = checked
+        self.last_ok = None
+        self.mod = Module(comment=f"emmy-b200 generic lowering for {spec.entry}"
+                                  + (" (checked)" if checked else ""))
         self.mod.add_global(".visible .global .align 4 .u32 emmy_err;")
+        if checked:
+            # first violation: buffer id + 1 (see plan "oob_names") and its index
+            self.mod.add_global(".visible .global .align 4 .u32 emmy_oob_buf;")
+            self.mod.add_global(".visible .global .align 4 .s32 emmy_oob_index;")
         params = []
         for n in spec.arg_order:
             a = spec.args[n]
@@ -127,6 +137,9 @@ class Generic:
                          "grid_per_sm": 0,
                          "smem": int(spec.smem_bytes if self.smem and self.dyn else 0),
                          "geometry": "meta"}
+        if self.checked:
+            self.mod.plan["checked"] = True
+            self.mod.plan["oob_names"] = self.buf_names()
         if tuple(spec.block[1:]) != (1, 1):
             raise NoMatch("1-D blocks only")
         return self.mod
@@ -201,9 +214,46 @@ class Generic:
         self.k(f"selp.s32 {r}, {idx.reg}, 0, {self.lo.mask}")
         return Val(r, "s32")
 
-    def addr(self, name: str, idx: Val, j: int = 0) -> tuple[str, bool, object]:
-        """(address register, shared?, dtype) of element idx+j of ``name``."""
+    def buf_names(self) -> list[str]:
+        """Buffer ids of checked mode: arguments in arg_order, then Smem."""
+        return list(self.spec.arg_order) + list(self.smem)
+
+    def bounds(self, name: str, idx: Val, j: int, count: int) -> tuple[Val, str]:
+        """Checked mode: (index clamped to 0 when elements idx+j .. idx+j+count-1
+        leave ``name``, in-range predicate).  An active lane out of range
+        records the first violation and raises ``emmy_err`` to ERR_OOB; the
+        access itself is then skipped by the caller."""
         k = self.k
+        n = numel(self.shape_of(name))
+        lim = n - j - count + 1
+        if lim <= 0:
+            raise LowerError(f"{name}: access of {count} element(s) at +{j} can never be "
+                             f"inside its {n} elements")
+        ok, viol = k.reg("pred"), k.reg("pred")
+        k(f"setp.lt.u32 {ok}, {idx.reg}, {lim}")
+        k(f"not.pred {viol}, {ok}")
+        if self.lo.mask is not None:
+            k(f"and.pred {viol}, {viol}, {self.lo.mask}")
+        skip = k.label("inb")
+        old, won = k.reg("u32"), k.reg("pred")
+        k(f"@!{viol} bra {skip}")
+        k(f"atom.global.cas.b32 {old}, [emmy_oob_buf], 0, {self.buf_names().index(name) + 1}")
+        k(f"setp.eq.u32 {won}, {old}, 0")
+        k(f"@{won} st.global.s32 [emmy_oob_index], {idx.reg}")
+        k(f"atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_OOB}")
+        k.place(skip)
+        safe = k.reg("s32")
+        k(f"selp.s32 {safe}, {idx.reg}, 0, {ok}")
+        return Val(safe, "s32"), ok
+
+    def addr(self, name: str, idx: Val, j: int = 0, count: int = 1) -> tuple[str, bool, object]:
+        """(address register, shared?, dtype) of element idx+j of ``name``; in
+        checked mode ``self.last_ok`` is the in-range predicate of elements
+        idx+j .. idx+j+count-1 (else None)."""
+        k = self.k
+        self.last_ok = None
+        if self.checked:
+            idx, self.last_ok = self.bounds(name, idx, j, count)
         if name in self.smem:
             shape, dt, off = self.smem[name]
             eb = dtype_info(dt)[2]
@@ -242,11 +292,13 @@ class Generic:
             v = Val(r, sk)
         return lo.coerce(v, kind)
 
-    def store_elem(self, a: str, shared: bool, dt, v: Val, atomic: bool = False) -> None:
+    def store_elem(self, a: str, shared: bool, dt, v: Val, atomic: bool = False,
+                   ok: str | None = None) -> None:
         k, lo = self.k, self.lo
         sk = storage_kind(dt)
         sp = "shared" if shared else "global"
-        g = self.guard()
+        p = self.and_mask(ok)
+        g = f"@{p} " if p is not None else ""
         if atomic:
             if shared or sk not in ("f32", "s32"):
                 raise LowerError("atomic add supports f32/s32 global buffers")
@@ -314,7 +366,11 @@ class Generic:
             if st.input in self.smem:
                 e = self.swizzle(e, getattr(st, "swizzle", "NONE"))
             a, sh, dt = self.addr(st.input, e)
-            lo.bind(name, self.load_elem(a, sh, dt, kind))
+            ok = self.last_ok
+            v = self.load_elem(a, sh, dt, kind)
+            if ok is not None:                 # checked: out of range reads 0
+                v = lo.select(Val(ok, "pred"), v, lo.const(0, v.kind))
+            lo.bind(name, v)
 
     def do_write(self, st: ir.Write) -> None:
         idx = self.flat(st.index, self.shape_of(st.output))
@@ -328,7 +384,8 @@ class Generic:
             if shared:
                 e = self.swizzle(e, getattr(st, "swizzle", "NONE"))
             a, sh, dt = self.addr(st.output, e)
-            self.store_elem(a, sh, dt, self.lo.env[name], atomic=bool(st.atomic) and not sh)
+            self.store_elem(a, sh, dt, self.lo.env[name], atomic=bool(st.atomic) and not sh,
+                            ok=self.last_ok)
 
     def _loop(self, axis: str, start: Val, bound: Val, step: Val, body, seed: bool,
               uniform: bool) -> None:
@@ -491,9 +548,19 @@ class Generic:
         src = self.clamp_masked(self.flat(st.src_index, self.shape_of(st.src)))
         nb = int(st.nbytes)
         eb = dtype_info(self.spec.args[st.src].dtype)[2]
-        sa, _, _ = self.addr(st.src, src)
-        da, _, _ = self.addr(st.smem, dst)
-        g = self.guard()
+        src_elems = max(1, nb // eb)
+        dst_elems = max(1, nb // dtype_info(self.smem[st.smem][1])[2])
+        sa, _, _ = self.addr(st.src, src, count=src_elems)
+        ok_s = self.last_ok
+        da, _, _ = self.addr(st.smem, dst, count=dst_elems)
+        ok_d = self.last_ok
+        p = self.lo.mask
+        for extra in (ok_s, ok_d):
+            if extra is not None:
+                q = k.reg("pred")
+                k(f"and.pred {q}, {p}, {extra}") if p is not None else k(f"mov.pred {q}, {extra}")
+                p = q
+        g = f"@{p} " if p is not None else ""
         words = nb // 4
         regs = k.regs("b32", words)
         if words == 4:
@@ -507,7 +574,6 @@ class Generic:
             k(f"{g}st.shared.b32 [{da}], {regs[0]}")
         else:
             raise LowerError(f"cp.async of {nb} bytes")
-        del eb
 
     def do_select(self, st: ir.Select) -> None:
         lo = self.lo
@@ -546,5 +612,5 @@ class Generic:
         k("barrier.sync 0")
 
 
-def emit_generic(spec: KernelSpec) -> Module:
-    return Generic(spec).emit()
+def emit_generic(spec: KernelSpec, checked: bool = False) -> Module:
+    return Generic(spec, checked=checked).emit()

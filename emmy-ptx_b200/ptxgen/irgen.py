@@ -172,13 +172,17 @@ PROGRAMS = {
                     ("op", "v1", "add", "in0", "v0")],
     "relu_mul": [("load", "in0", "x", "vec"), ("op", "v0", "relu", "in0"),
                  ("load", "in1", "y", "vec"), ("op", "v1", "multiply", "in1", "v0")],
+    # "scalar": element 0 of a one-element input (an earlier kernel's result)
+    "center": [("load", "in0", "x", "vec"), ("load", "in1", "mean", "scalar"),
+               ("op", "v0", "subtract", "in0", "in1")],
 }
 
 
-def pointwise(n: int, unroll: int, program: str = "add", block: int = 256,
+def pointwise(n: int, unroll: int, program="add", block: int = 256,
               out: str = "add", arg_order=None, constants=(), entry="k_add_pointwise",
               rtol=0.0, atol=0.0, pid="pointwise"):
-    steps = PROGRAMS[program]
+    """``program``: a name in PROGRAMS or a list of steps in that format."""
+    steps = PROGRAMS[program] if isinstance(program, str) else list(program)
     if n % unroll:
         raise ValueError("n must be a multiple of the unroll factor")
     cells = n // unroll
@@ -188,7 +192,7 @@ def pointwise(n: int, unroll: int, program: str = "add", block: int = 256,
         for st in steps:
             if st[0] == "load":
                 _, base, buf, kind = st
-                body.append(load(f"{base}__u{k}", buf, (L(0),) if kind == "const" else (idx,)))
+                body.append(load(f"{base}__u{k}", buf, (idx,) if kind == "vec" else (L(0),)))
             else:
                 _, base, opname, *args = st
                 body.append(assign(f"{base}__u{k}", opname, *[f"{a}__u{k}" for a in args]))
@@ -202,9 +206,11 @@ def pointwise(n: int, unroll: int, program: str = "add", block: int = 256,
         if st[0] == "load" and st[3] == "vec" and st[2] not in seen:
             seen.add(st[2])
             vec_inputs.append(st[2])
+    scalar_inputs = sorted({st[2] for st in steps if st[0] == "load" and st[3] == "scalar"})
     if arg_order is None:
-        arg_order = [c[0] for c in constants] + vec_inputs + [out]
+        arg_order = [c[0] for c in constants] + vec_inputs + scalar_inputs + [out]
     inputs = [(b, (n,), "f32", i) for i, b in enumerate(sorted(vec_inputs))]
+    inputs += [(b, (1,), "f32", len(inputs) + i) for i, b in enumerate(scalar_inputs)]
     grid = (math.ceil(cells / block), 1, 1)
     return package(entry, out, [t], inputs, list(constants), (out, (n,), "f32"), arg_order,
                    grid, (block, 1, 1), rtol=rtol, atol=atol, pid=pid)
@@ -278,6 +284,34 @@ def reduce_full(n: int, threads: int = 128, mean: bool = False, entry=None, pid=
     return package(entry, out, [t], [("x", (n,), "f32", 0)], constants, (out, (1,), "f32"),
                    arg_order, (1, 1, 1), (threads, 1, 1), rtol=1e-4, atol=1e-4, pid=pid,
                    graph_out_shape=())
+
+
+def center(n: int, threads: int = 128, unroll: int = 4, pid="center"):
+    """A two-kernel problem: ``mean = sum(x) / n`` (r03 schedule), then
+    ``y = x - mean`` (pointwise) with ``mean`` an intermediate the runner
+    chains from the first kernel (``submit.py:112-122``).  Returns
+    ``({entry: graph}, meta)``; both kernels read ``x`` from seed 0."""
+    g1, m1 = reduce_full(n, threads=threads, mean=True, pid=pid)
+    g2, m2 = pointwise(n, unroll, program="center", out="y", entry="k_sub_pointwise",
+                       rtol=1e-5, atol=1e-5, pid=pid)
+    k1, k2 = dict(m1["kernels"][0]), dict(m2["kernels"][0])
+    k1["final"] = False
+    k2["args"] = [({"name": a["name"], "dtype": a["dtype"], "shape": a["shape"],
+                    "intermediate": True} if a["name"] == "mean" else a) for a in k2["args"]]
+    meta = {"id": pid, "code": "", "rtol": 1e-4, "atol": 1e-4, "graph_inputs": ["x"],
+            "graph_outputs": ["y"], "kernels": [k1, k2]}
+    return {k1["entry"]: g1, k2["entry"]: g2}, meta
+
+
+def write_problem(pdir, graphs: dict, meta: dict) -> None:
+    """Write ``<entry>.ir.json`` per kernel and ``meta.json`` into ``pdir``."""
+    import json
+    from pathlib import Path
+    pdir = Path(pdir)
+    pdir.mkdir(parents=True, exist_ok=True)
+    for entry, g in graphs.items():
+        (pdir / f"{entry}.ir.json").write_text(json.dumps(g, indent=1))
+    (pdir / "meta.json").write_text(json.dumps(meta, indent=1))
 
 
 def reduce_rows(rows: int, cols: int, threads: int = 128, entry="k_sum_1_reduce",

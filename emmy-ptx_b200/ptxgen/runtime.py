@@ -176,6 +176,10 @@ class Device:
     def host_free(self, ptr: int) -> None:
         check(self.L.emmy_host_free(self.ctx, C.c_void_p(ptr)), "emmy_host_free")
 
+    def dtod(self, dst: int, src: int, nbytes: int, stream=None) -> None:
+        check(self.L.emmy_memcpy_dtod(C.c_uint64(dst), C.c_uint64(src), nbytes,
+                                      stream or self.stream), "dtod")
+
     def htod(self, dst: int, arr: np.ndarray, stream=None) -> None:
         arr = np.ascontiguousarray(arr)
         check(self.L.emmy_memcpy_htod(C.c_uint64(dst), arr.ctypes.data_as(C.c_void_p),
@@ -420,8 +424,23 @@ class PreparedKernel:
     def check_errors(self) -> None:
         self.dev.sync()
         code = self.mod.error_word(clear=True)
-        if code:
-            raise EmmyError(f"kernel {self.spec.entry} reported error 0x{code:x}")
+        if not code:
+            return
+        msg = f"kernel {self.spec.entry} reported error 0x{code:x}"
+        names = self.plan.get("oob_names")
+        if names and self.mod.has_global("emmy_oob_buf"):
+            info = np.zeros(2, dtype=np.uint32)
+            pb, _ = self.mod.global_ptr("emmy_oob_buf")
+            pi, _ = self.mod.global_ptr("emmy_oob_index")
+            self.dev.dtoh(info[:1], pb)
+            self.dev.dtoh(info[1:], pi)
+            self.dev.sync()
+            if 0 < info[0] <= len(names):
+                msg += (f": out-of-bounds access to {names[info[0] - 1]}"
+                        f"[{int(info[1].astype(np.int32))}] (first violation; access skipped)")
+            for ptr in (pb, pi):
+                self.dev.memset32(ptr, 0, 1)
+        raise EmmyError(msg)
 
     def close(self) -> None:
         for p in self.bufs.values():
