@@ -158,12 +158,20 @@ def _layout(plan):
     v_chunk = d * 128                  # V^T: d rows, one atom of keys wide
     v_bytes = max(1, bkv // atom) * v_chunk
     # (P is not staged here: it lives in TMEM over its own S columns)
-    base = halves * q_bytes
+    # f32 Q (TF32 hi/lo) lives in TMEM too when the columns allow, as the A
+    # operand of S = Q . K^T: then shared memory holds only K/V stages
+    s_cols = max(32, bkv * (2 if plan.dtype == "f32" else 1))
+    q_tmem = plan.dtype == "f32" and 2 * s_cols + 3 * d <= 512
+    base = 0 if q_tmem else halves * q_bytes
     per_stage = halves * (k_bytes + v_bytes)
-    kvst = 2 if base + 2 * per_stage + 1024 <= 232448 - 2048 else 1
-    lay = {}
+    kvst = 1
+    for cand in (3, 2):
+        if base + cand * per_stage + 1024 + XCH_STATIC <= SMEM_MAX:
+            kvst = cand
+            break
+    lay = {"q_tmem": q_tmem, "s_cols": s_cols}
     off = 0
-    for h in range(halves):
+    for h in range(0 if q_tmem else halves):
         lay[("q", h)] = off
         off += q_bytes
     for st in range(kvst):
@@ -183,6 +191,13 @@ def _layout(plan):
     return lay
 
 
+def _tmap_names(plan, lay):
+    names = ["kh", "kl", "vh", "vl"] if plan.dtype == "f32" else ["kh", "vh"]
+    if not lay["q_tmem"]:
+        names = (["qh", "ql"] if plan.dtype == "f32" else ["qh"]) + names
+    return names
+
+
 def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     params = [(f"p_{n}", ".u64") for n in spec.arg_order]
     k = Kernel(spec.entry, params)
@@ -190,7 +205,8 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     mod.add_global(".visible .global .align 4 .u32 emmy_err;")
     mod.add_global(".visible .global .align 4 .u32 emmy_plan;")
     mod.add_global(".visible .global .align 8 .u64 emmy_ws;")
-    tnames = ["qh", "ql", "kh", "kl", "vh", "vl"] if plan.dtype == "f32" else ["qh", "kh", "vh"]
+    lay = _layout(plan)
+    tnames = _tmap_names(plan, lay)
     for t in tnames:
         mod.add_global(f".visible .global .align 64 .b8 tmap_{t}[128];")
     base = {n: k.param_ptr(f"p_{n}") for n in spec.arg_order}
@@ -198,7 +214,6 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     cta, ncta = k.sreg("%ctaid.x"), k.sreg("%nctaid.x")
     p = k.reg("pred")
     simt = k.label("simt")
-    lay = _layout(plan)
     dyn = lay["total"] + 1024
     if plan.tc and dyn <= 232448 - 1024:
         mod.add_global(".extern .shared .align 1024 .b8 dsmem[];")
@@ -225,7 +240,7 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
               "grid_per_sm": 16, "grid_max": max(1, math.ceil(total / 128)),
               "flops": 4 * BH * S * S * D}
     if tc_ok:
-        pre, ws_bytes, tm = _emit_pre(mod, spec, plan)
+        pre, ws_bytes, tm = _emit_pre(mod, spec, plan, lay)
         plan_d.update({
             "block": lay["threads"], "grid_per_sm": 1, "grid_max": BH * (S // BQ), "smem": dyn,
             "workspace": {"sym": "emmy_ws", "bytes": ws_bytes}, "pre": pre, "tmaps": tm,
@@ -241,28 +256,34 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
 # ---------------------------------------------------------------------------
 
 
-def _ws_layout(plan):
-    """Workspace regions (bytes): hi/lo of Q, K ([BH, S, D]) and V^T ([BH, D, S])
-    for f32; K (only when given transposed) and V^T for bf16."""
+def _ws_layout(plan, lay):
+    """Workspace regions (bytes): hi/lo of K ([BH, S, D]) and V^T ([BH, D, S])
+    for f32 (and of Q when Q is not in TMEM); K (only when given transposed)
+    and V^T for bf16."""
     n = plan.bh * plan.s * plan.d * plan.e
     off = {}
     cur = 0
-    names = ["qh", "ql", "kh", "kl", "vh", "vl"] if plan.dtype == "f32" else ["kh", "vh"]
+    if plan.dtype == "f32":
+        names = (["kh", "kl", "vh", "vl"] if lay["q_tmem"] else
+                 ["qh", "ql", "kh", "kl", "vh", "vl"])
+    else:
+        names = ["kh", "vh"]
     for nm in names:
         off[nm] = cur
         cur += n
     return off, cur
 
 
-def _emit_pre(mod: Module, spec: KernelSpec, plan):
-    off, total = _ws_layout(plan)
+def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
+    off, total = _ws_layout(plan, lay)
     f32 = plan.dtype == "f32"
     pre = []
     S, D, BH = plan.s, plan.d, plan.bh
-    if f32:
+    if f32 and not lay["q_tmem"]:
         mod.kernels.append(_emit_split_copy(spec, plan, plan.q, off["qh"], off["ql"], "_pre_q"))
         pre.append({"entry": f"{spec.entry}_pre_q", "block": 256, "grid_per_sm": 8,
                     "grid_max": max(1, BH * S * D // 4 // 256)})
+    if f32:
         if plan.k_trans:
             mod.kernels.append(_emit_transpose(spec, plan, plan.k, D, S, off["kh"],
                                                off["kl"], "_pre_k"))
@@ -297,8 +318,10 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan):
 
     tm = []
     if f32:
-        tm += [tmap("tmap_qh", "@ws", off["qh"], D, S, BQ), tmap("tmap_ql", "@ws", off["ql"], D, S, BQ),
-               tmap("tmap_kh", "@ws", off["kh"], D, S, plan.bkv),
+        if not lay["q_tmem"]:
+            tm += [tmap("tmap_qh", "@ws", off["qh"], D, S, BQ),
+                   tmap("tmap_ql", "@ws", off["ql"], D, S, BQ)]
+        tm += [tmap("tmap_kh", "@ws", off["kh"], D, S, plan.bkv),
                tmap("tmap_kl", "@ws", off["kl"], D, S, plan.bkv),
                tmap("tmap_vh", "@ws", off["vh"], S, D, D), tmap("tmap_vl", "@ws", off["vl"], S, D, D)]
     else:
@@ -612,20 +635,32 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     units = BH * qblocks
     kvst = lay["kvst"]
     stage_k = lay[("k", 1, 0)] - lay[("k", 0, 0)] if kvst > 1 else 0
+
+    def k_addr(h, c):
+        """Byte offset (in stage 0) of column chunk ``c`` of K half ``h``.  For
+        f32 each chunk holds the hi rows then the lo rows, so one MMA with
+        N = 2 * BKV reads [K_hi; K_lo] as a single B operand."""
+        if f32:
+            return lay[("k", 0, 0)] + c * 2 * lay["k_chunk"] + h * lay["k_chunk"]
+        return lay[("k", 0, 0)] + c * lay["k_chunk"]
     cx = _Ctx(k)
-    for nm in ("q_full", "q_empty", "p_full", "pv_done", "drain"):
+    for nm in ("q_full", "q_empty", "pv_done", "o_full", "drain"):
         k.shared(f"\t.shared .align 8 .b64 bar_{nm};")
     for nm, cnt in (("k_full", kvst), ("k_empty", kvst), ("v_full", kvst), ("v_empty", kvst),
-                    ("s_full", 2), ("s_free", 2)):
+                    ("s_full", 2), ("s_free", 2), ("p_full", 2)):
         k.shared(f"\t.shared .align 8 .b64 bar_{nm}[{cnt}];")
     k.shared("\t.shared .align 4 .u32 tmem_slot;")
     k.shared("\t.shared .align 4 .u32 abort_flag;")
-    # TMEM: two S buffers (the MMA warp fills one while the softmax warps
-    # read the other), then O
-    # an S buffer: BKV f32 score columns; for f32 data also the TF32 lo half
-    # of P beside them (hi overwrites the scores)
-    s_cols = max(32, BKV * (2 if f32 else 1))
-    tcols = 1 << (2 * s_cols + D - 1).bit_length()
+    # TMEM columns: two S buffers (the MMA warp fills one while the softmax
+    # warps read the other), O, then (f32 with q_tmem) Q hi and Q lo.  An S
+    # buffer holds BKV f32 score columns; for f32 also the Q_hi.K_lo partial
+    # beside them, later overwritten by P hi and P lo.
+    q_tmem = lay["q_tmem"]
+    s_cols = lay["s_cols"]
+    o_col = 2 * s_cols
+    q_col = o_col + D
+    tcols = 1 << (q_col + (2 * D if q_tmem else 0) - 1).bit_length()
+    assert tcols <= 512
     warp, lane = k.reg("u32"), k.reg("u32")
     k(f"shr.u32 {warp}, {tid}, 5")
     k(f"and.b32 {lane}, {tid}, 31")
@@ -634,9 +669,8 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"mov.u32 {ring}, dsmem")
     k(f"add.u32 {ring}, {ring}, 1023")
     k(f"and.b32 {ring}, {ring}, -1024")
-    tnames = ["qh", "ql", "kh", "kl", "vh", "vl"] if f32 else ["qh", "kh", "vh"]
     tm = {}
-    for t in tnames:
+    for t in _tmap_names(plan, lay):
         r = k.reg("u64")
         k(f"mov.u64 {r}, tmap_{t}")
         k(f"cvta.global.u64 {r}, {r}")
@@ -646,11 +680,17 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"setp.ne.u32 {p}, {tid}, 0")
     k(f"@{p} bra {skip}")
     split = lay["split"]
-    for nm, cnt in (("q_full", 1), ("q_empty", 1), ("p_full", 128 * split), ("pv_done", 1),
-                    ("drain", 1)):
+    # q_full: one TMA arrival, or every softmax thread once its Q row is in TMEM
+    # Each barrier a role may wait on after skipping phases is either per
+    # S buffer (p_full: the softmax may run a block ahead of the MMA warp's
+    # wait) or per unit (o_full: the epilogue's wait for the unit's last
+    # P . V), so no waiter is ever two phases behind its barrier.
+    for nm, cnt in (("q_full", 128 * split if q_tmem else 1), ("q_empty", 1),
+                    ("pv_done", 1), ("o_full", 1), ("drain", 1)):
         k(f"mbarrier.init.shared::cta.b64 [bar_{nm}], {cnt}")
     for nm, n, cnt in (("k_full", kvst, 1), ("k_empty", kvst, 1), ("v_full", kvst, 1),
-                       ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1)):
+                       ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1),
+                       ("p_full", 2, 128 * split)):
         for i in range(n):
             k(f"mbarrier.init.shared::cta.b64 [bar_{nm}+{8 * i}], {cnt}")
     k("st.shared.u32 [abort_flag], 0")
@@ -681,14 +721,15 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         return bh, qb
 
     def stage_of(g):
-        """(stage index, parity of its full phase) of global key block ``g``."""
+        """(stage index, parity of its full phase) of global key block ``g``:
+        g % kvst and (g / kvst) & 1."""
         st, ph = k.reg("u32"), k.reg("u32")
         if kvst == 1:
             k(f"mov.u32 {st}, 0")
             k(f"and.b32 {ph}, {g}, 1")
         else:
-            k(f"and.b32 {st}, {g}, 1")
-            k(f"shr.u32 {ph}, {g}, 1")
+            k(f"rem.u32 {st}, {g}, {kvst}")
+            k(f"div.u32 {ph}, {g}, {kvst}")
             k(f"and.b32 {ph}, {ph}, 1")
         return st, ph
 
@@ -721,19 +762,20 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     bh, qb = unit_coords(u)
     qrow = k.reg("u32")
     k(f"mul.lo.u32 {qrow}, {qb}, {BQ}")
-    ph = k.reg("u32")
-    k(f"and.b32 {ph}, {uit}, 1")
-    k(f"xor.b32 {ph}, {ph}, 1")
-    cx.wait("bar_q_empty", ph, abort_l)
-    qbytes = lay["q_bytes"] * halves
-    k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [bar_q_full], {qbytes}")
-    for h in range(halves):
-        for c in range(D // atom):
-            dst, cc = k.reg("u32"), k.reg("u32")
-            k(f"add.u32 {dst}, {ring}, {lay[('q', h)] + c * lay['q_chunk']}")
-            k(f"mov.u32 {cc}, {c * atom}")
-            k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-              f"[{dst}], [{tm['qh' if h == 0 else 'ql']}, {{{cc}, {qrow}, {bh}}}], [bar_q_full]")
+    if not q_tmem:
+        ph = k.reg("u32")
+        k(f"and.b32 {ph}, {uit}, 1")
+        k(f"xor.b32 {ph}, {ph}, 1")
+        cx.wait("bar_q_empty", ph, abort_l)
+        qbytes = lay["q_bytes"] * halves
+        k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [bar_q_full], {qbytes}")
+        for h in range(halves):
+            for c in range(D // atom):
+                dst, cc = k.reg("u32"), k.reg("u32")
+                k(f"add.u32 {dst}, {ring}, {lay[('q', h)] + c * lay['q_chunk']}")
+                k(f"mov.u32 {cc}, {c * atom}")
+                k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                  f"[{dst}], [{tm['qh' if h == 0 else 'ql']}, {{{cc}, {qrow}, {bh}}}], [bar_q_full]")
     j = k.reg("u32")
     k(f"mov.u32 {j}, 0")
     jl = k.label("p_kv")
@@ -751,7 +793,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     for h in range(halves):
         for c in range(D // atom):
             dst, cc = k.reg("u32"), k.reg("u32")
-            k(f"add.u32 {dst}, {soff}, {lay[('k', 0, h)] + c * lay['k_chunk']}")
+            k(f"add.u32 {dst}, {soff}, {k_addr(h, c)}")
             k(f"mov.u32 {cc}, {c * atom}")
             k(f"@{pe} cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
               f"[{dst}], [{tm['kh' if h == 0 else 'kl']}, {{{cc}, {krow}, {bh}}}], [{kf}]")
@@ -789,11 +831,13 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     kmaj = _desc_const(16, 1024, 2)      # K-major, 128-byte swizzle, 8-row groups 1 KB apart
     id_s, id_o = k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {id_s}, {_idesc(kind, BQ, BKV)}")
+    id_s2 = k.reg("u32")                 # f32: N = 2 * BKV, B = [K_hi; K_lo]
+    k(f"mov.u32 {id_s2}, {_idesc(kind, BQ, 2 * BKV)}")
     k(f"mov.u32 {id_o}, {_idesc(kind, BQ, D)}")
     yes = k.reg("pred")
     k(f"setp.eq.u32 {yes}, 0, 0")
     o_t = k.reg("u32")
-    k(f"add.u32 {o_t}, {tmem}, {2 * s_cols}")
+    k(f"add.u32 {o_t}, {tmem}, {o_col}")
     uit2, g2, u2 = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {uit2}, 0")
     k(f"mov.u32 {g2}, 0")
@@ -813,15 +857,13 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         return r
 
     d_base = mkdesc(ring)
-    d_stage1 = k.reg("u64")
-    k(f"add.s64 {d_stage1}, {d_base}, {stage_k >> 4}")
 
     def stage_desc(st_):
-        ps, r = k.reg("pred"), k.reg("u64")
         if kvst == 1:
             return d_base
-        k(f"setp.ne.u32 {ps}, {st_}, 0")
-        k(f"selp.b64 {r}, {d_stage1}, {d_base}, {ps}")
+        t, r = k.reg("u64"), k.reg("u64")
+        k(f"mul.wide.u32 {t}, {st_}, {stage_k >> 4}")
+        k(f"add.s64 {r}, {d_base}, {t}")
         return r
 
     def dsc(base_d, off):
@@ -844,17 +886,27 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         cx.wait(bar_at("s_free", b), phs, abort_l)
         k("tcgen05.fence::after_thread_sync")
         first = True
-        for c in range(D // atom):
-            for kk in range(4):
-                for (ha, hb) in pairs:
-                    a_ = dsc(d_base, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
-                    b_ = dsc(ds, lay[("k", 0, hb)] + c * lay["k_chunk"] + kk * 32)
+        # f32: columns [0, BKV) get Q_hi.K_hi + Q_lo.K_hi and [BKV, 2 BKV)
+        # get Q_hi.K_lo (summed by the softmax), from 2 MMAs per K-step
+        # instead of 3; bf16: one product
+        groups = [(0, 0, id_s2), (1, 0, id_s)] if f32 else [(0, 0, id_s)]
+        for (ha, hb, idd) in groups:
+            for c in range(D // atom):
+                for kk in range(4):
+                    if q_tmem:
+                        # A (Q) from TMEM: 8 f32 columns per K-step, lo D on
+                        a_ = k.reg("u32")
+                        k(f"add.u32 {a_}, {tmem}, {q_col + ha * D + c * atom + kk * 8}")
+                        a_ = f"[{a_}]"
+                    else:
+                        a_ = dsc(d_base, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
+                    b_ = dsc(ds, k_addr(hb, c) + kk * 32)
                     acc = yes
                     if first:
                         acc = k.reg("pred")
                         k(f"setp.ne.u32 {acc}, 0, 0")
                         first = False
-                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a_}, {b_}, {id_s}, {acc}")
+                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a_}, {b_}, {idd}, {acc}")
         k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
           f"[{bar_at('s_full', b)}]")
         k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
@@ -862,12 +914,14 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
 
     def issue_pv(gr, jr):
         st_, phf_ = stage_of(gr)
-        php_ = k.reg("u32")
-        k(f"and.b32 {php_}, {gr}, 1")
+        pbuf, php_ = k.reg("u32"), k.reg("u32")
+        k(f"and.b32 {pbuf}, {gr}, 1")
+        k(f"shr.u32 {php_}, {gr}, 1")
+        k(f"and.b32 {php_}, {php_}, 1")
         ds = stage_desc(st_)
         firstb = k.reg("pred")
         k(f"setp.ne.u32 {firstb}, {jr}, 0")
-        cx.wait("bar_p_full", php_, abort_l)
+        cx.wait(bar_at("p_full", pbuf), php_, abort_l)
         cx.wait(bar_at("v_full", st_), phf_, abort_l)
         k("tcgen05.fence::after_thread_sync")
         pb, b2 = k.reg("u32"), k.reg("u32")   # P_g lives in S buffer g % 2
@@ -925,7 +979,10 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"mov.u32 {g2}, {gn}")
     k(f"mov.u32 {j2}, {jn}")
     k(f"@!{last} bra {mj}")
-    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_q_empty]")
+    # the unit's O is complete once its last P . V is
+    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_o_full]")
+    if not q_tmem:
+        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_q_empty]")
     k(f"add.u32 {uit2}, {uit2}, 1")
     k(f"add.u32 {u2}, {u2}, {ncta}")
     k(f"bra.uni {ml}")
@@ -957,7 +1014,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"add.u32 {s_row}, {tmem}, {lane_off}")
     k(f"mad.lo.u32 {s_row}, {half}, {hs}, {s_row}")
     k(f"add.u32 {o_row}, {tmem}, {lane_off}")
-    k(f"add.u32 {o_row}, {o_row}, {2 * s_cols}")
+    k(f"add.u32 {o_row}, {o_row}, {o_col}")
     k(f"mad.lo.u32 {o_row}, {half}, {ho}, {o_row}")
     if split == 2:
         # exchange slots: mine and my partner's (same row, other half)
@@ -980,6 +1037,39 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k.place(sl)
     k(f"setp.ge.u32 {p}, {u3}, {units}")
     k(f"@{p} bra {se}")
+    if q_tmem:
+        # this thread's half of its Q row -> TF32 hi/lo -> TMEM (the A operand
+        # of S = Q . K^T).  The previous unit's S = Q . K^T MMAs are done: this
+        # thread consumed the last S block of that unit before its epilogue.
+        bhq, qbq = unit_coords(u3)
+        qg = k.reg("u32")
+        k(f"mad.lo.u32 {qg}, {bhq}, {S}, {row}")
+        k(f"mad.lo.u32 {qg}, {qbq}, {BQ}, {qg}")
+        k(f"mul.lo.u32 {qg}, {qg}, {D}")
+        k(f"mad.lo.u32 {qg}, {half}, {ho}, {qg}")
+        qptr = k.addr(base[plan.q], qg, 4)
+        q_row_t = k.reg("u32")
+        k(f"add.u32 {q_row_t}, {tmem}, {lane_off}")
+        k(f"add.u32 {q_row_t}, {q_row_t}, {q_col}")
+        k(f"mad.lo.u32 {q_row_t}, {half}, {ho}, {q_row_t}")
+        for c0 in range(0, ho, 32):
+            cnt = min(32, ho - c0)
+            xs = k.regs("b32", cnt)
+            for v in range(cnt // 4):
+                k(f"ld.global.nc.v4.b32 {{{', '.join(xs[4 * v:4 * v + 4])}}}, "
+                  f"[{qptr}+{(c0 + 4 * v) * 4}]")
+            qh, ql = k.regs("b32", cnt), k.regs("f32", cnt)
+            for t in range(cnt):
+                k(f"and.b32 {qh[t]}, {xs[t]}, -8192")
+                k(f"sub.rn.f32 {ql[t]}, {xs[t]}, {qh[t]}")
+            ta, tb = k.reg("u32"), k.reg("u32")
+            k(f"add.u32 {ta}, {q_row_t}, {c0}")
+            k(f"add.u32 {tb}, {q_row_t}, {D + c0}")
+            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{ta}], {{{', '.join(qh)}}}")
+            k(f"tcgen05.st.sync.aligned.32x32b.x{cnt}.b32 [{tb}], {{{', '.join(ql)}}}")
+        k("tcgen05.wait::st.sync.aligned")
+        k("tcgen05.fence::before_thread_sync")
+        k("mbarrier.arrive.shared::cta.b64 _, [bar_q_full]")
     m_run, l_run = k.reg("f32"), k.reg("f32")
     k(f"mov.f32 {m_run}, {f32_hex(-1e30)}")
     k(f"mov.f32 {l_run}, 0f00000000")
@@ -1004,7 +1094,18 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         tad = k.reg("u32")
         k(f"add.u32 {tad}, {s_cur}, {c0}")
         k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(sv[c0:c0 + cnt])}}}, [{tad}]")
+    if f32:
+        # the Q_hi.K_lo partial sits BKV columns on
+        sv2 = k.regs("f32", nreg)
+        for c0 in range(0, nreg, 32):
+            cnt = min(32, nreg - c0)
+            tad = k.reg("u32")
+            k(f"add.u32 {tad}, {s_cur}, {BKV + c0}")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(sv2[c0:c0 + cnt])}}}, [{tad}]")
     k("tcgen05.wait::ld.sync.aligned")
+    if f32:
+        for t in range(nreg):
+            k(f"add.rn.f32 {sv[t]}, {sv[t]}, {sv2[t]}")
     # raw partial max in independent three-input chains; scaling by sc2 > 0
     # is monotone, so max(s) * sc2 == max(s * sc2) exactly
     nch = min(4, nreg)
@@ -1141,7 +1242,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k("tcgen05.wait::st.sync.aligned")
     k.place(nor2)
     k("tcgen05.fence::before_thread_sync")
-    k("mbarrier.arrive.shared::cta.b64 _, [bar_p_full]")
+    k(f"mbarrier.arrive.shared::cta.b64 _, [{bar_at('p_full', sb)}]")
     k(f"add.u32 {g3}, {g3}, 1")
     k(f"add.u32 {j3}, {j3}, 1")
     k(f"setp.lt.u32 {p}, {j3}, {nkv}")
@@ -1163,9 +1264,8 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     else:
         k(f"mov.f32 {lo_sum}, {l_run}")
     phl = k.reg("u32")
-    k(f"sub.u32 {phl}, {g3}, 1")
-    k(f"and.b32 {phl}, {phl}, 1")
-    cx.wait("bar_pv_done", phl, abort_l)
+    k(f"and.b32 {phl}, {uit3}, 1")
+    cx.wait("bar_o_full", phl, abort_l)
     k("bar.warp.sync -1")
     k("tcgen05.fence::after_thread_sync")
     rl = k.reg("f32")
