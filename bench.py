@@ -65,7 +65,10 @@ class Job:
     """One compiled kernel of a workload with its inputs and work figures."""
 
     def __init__(self, key, spec, inputs, algo_bytes, algo_flops=0.0, allreduce=None,
-                 check=None):
+                 check=None, local_ref=None, ref_div=1.0):
+        self.local_ref = local_ref    # this rank's f64 share of an all-reduced result
+        self.ref_div = ref_div        # global result = sum over ranks of local_ref / ref_div
+        self.inbox = None
         self.key = key
         self.spec = spec
         self.inputs = inputs          # host arrays (uploaded per step in e2e)
@@ -110,9 +113,11 @@ def workload_reductions(rank: int, world: int):
             raise AssertionError("row sums")
 
     return [
-        Job("sum", s_spec, {"x": x}, n * 4 + 4, allreduce="sum_1", check=chk_sum),
+        Job("sum", s_spec, {"x": x}, n * 4 + 4, allreduce="sum_1", check=chk_sum,
+            local_ref=local_sum),
         Job("mean", m_spec, {"x": x}, n * 4 + 4, allreduce="mean",
-            check=lambda o: chk_sum(o, "mean", float(total))),
+            check=lambda o: chk_sum(o, "mean", float(total)), local_ref=local_sum,
+            ref_div=float(total)),
         Job("row_sum", r_spec, {"x": xr}, rows * cols * 4 + rows * 4, check=chk_rows),
     ], {"workload": "configs[1] reductions: sum+mean over 2^26 f32 U[0,1], row sum 8192x8192 "
                     "f32 N(0,1)", "elements_per_rank": 2 * n + rows * cols}
@@ -351,15 +356,26 @@ def run_ours(args, dist: Dist):
         cfg["small"] = "reduced shapes for profiler captures; not a bench configuration"
     dev = Device.get(dist.local)
     comm = None
+    for j in jobs:
+        j.pk = PreparedKernel(j.spec, dev=dev)
+        j.pk.upload(j.inputs)
+    dev.sync()
+    if dist.world > 1 and args.collective == "p2p":
+        # full reductions exchange their totals inside the kernel, over
+        # peer inboxes (NVLink stores): no separate collective launch
+        from ptxgen.dist import PeerInbox
+        for j in jobs:
+            if j.allreduce and j.pk.plan.get("xgpu"):
+                j.inbox = PeerInbox(dev, dist.rdv)
+                j.pk.attach_peers(j.inbox)
+                j.allreduce = None
+        cfg["collective"] = "fused in-kernel exchange over NVLink peer inboxes"
     if dist.world > 1 and any(j.allreduce for j in jobs):
         from ptxgen.dist import NcclComm
         comm = NcclComm(dev, dist.rdv)
         nccl_stream = dev.new_stream()
         ev_ready, ev_done = dev.event(), dev.event()
-    for j in jobs:
-        j.pk = PreparedKernel(j.spec, dev=dev)
-        j.pk.upload(j.inputs)
-    dev.sync()
+        cfg["collective"] = "NCCL all-reduce on a second stream"
 
     last_ar = max((i for i, j in enumerate(jobs) if j.allreduce), default=-1)
 
@@ -392,9 +408,15 @@ def run_ours(args, dist: Dist):
     for _ in range(args.warmup):
         step()
     dev.sync()
-    # untimed ramp: keep the GPU busy ~0.3 s so it leaves idle clocks
+    # untimed ramp: keep the GPU busy ~0.3 s so it leaves idle clocks; the
+    # number of steps is agreed across ranks (each step of a multi-rank full
+    # reduction meets every other rank's)
     t_ramp = time.perf_counter()
-    while time.perf_counter() - t_ramp < 0.3:
+    for _ in range(16):
+        step()
+    dev.sync()
+    per16 = dist.max(time.perf_counter() - t_ramp)
+    for _ in range(max(1, int(0.3 / max(per16, 1e-4)))):
         for _ in range(16):
             step()
         dev.sync()
@@ -402,6 +424,12 @@ def run_ours(args, dist: Dist):
         j.pk.check_errors()
         if j.check is not None and dist.world == 1:
             j.check(j.pk.download())
+        elif j.local_ref is not None and dist.world > 1:
+            name = j.spec.outputs[0]
+            got = float(j.pk.download([name])[name].reshape(-1)[0])
+            want = dist.rdv.sum(j.local_ref) / j.ref_div
+            if abs(got - want) > 1e-5 * abs(want):
+                raise AssertionError(f"{j.key} over {dist.world} ranks: {got} vs {want}")
     # ---- timed region: device-resident inputs, events only at its ends ----
     t0, t1 = dev.event(), dev.event()
     dist.barrier()
@@ -547,6 +575,8 @@ def run_ours(args, dist: Dist):
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_budget)
     for j in jobs:
+        if j.inbox is not None:
+            j.inbox.close()
         j.pk.close()
     if comm is not None:
         dev.sync(nccl_stream)
@@ -725,6 +755,9 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
+                    help="multi-GPU full reductions: in-kernel exchange over peer inboxes "
+                         "(p2p) or an NCCL all-reduce after the kernel")
     ap.add_argument("--jobs", default="",
                     help="comma-separated job keys of the workload to run (default: all)")
     ap.add_argument("--small", action="store_true",

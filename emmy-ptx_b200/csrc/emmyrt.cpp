@@ -74,6 +74,9 @@ struct Driver {
   EMMY_FN(cuStreamWaitEvent)
   EMMY_FN(cuGetErrorString)
   EMMY_FN(cuTensorMapEncodeTiled)
+  EMMY_FN(cuIpcGetMemHandle)
+  EMMY_FN(cuIpcOpenMemHandle)
+  EMMY_FN(cuIpcCloseMemHandle)
 #undef EMMY_FN
 };
 
@@ -132,6 +135,9 @@ void load_driver() {
   EMMY_LOAD(cuStreamWaitEvent, "cuStreamWaitEvent")
   EMMY_LOAD(cuGetErrorString, "cuGetErrorString")
   EMMY_LOAD(cuTensorMapEncodeTiled, "cuTensorMapEncodeTiled")
+  EMMY_LOAD(cuIpcGetMemHandle, "cuIpcGetMemHandle")
+  EMMY_LOAD(cuIpcOpenMemHandle, "cuIpcOpenMemHandle_v2")
+  EMMY_LOAD(cuIpcCloseMemHandle, "cuIpcCloseMemHandle")
 #undef EMMY_LOAD
   if (!all) return;
   CUresult r = g_drv.cuInit(0);
@@ -541,6 +547,38 @@ int emmy_memcpy_dtoh(void *dst, emmy_dptr src, size_t bytes, emmy_stream stream)
 int emmy_memcpy_dtod(emmy_dptr dst, emmy_dptr src, size_t bytes, emmy_stream stream) {
   DRV_OR_FAIL();
   CU_TRY(g_drv.cuMemcpyDtoDAsync(dst, src, bytes, static_cast<CUstream>(stream)), "cuMemcpyDtoDAsync");
+  return EMMY_OK;
+}
+
+int emmy_ipc_handle(emmy_ctx *ctx, emmy_dptr ptr, void *out64) {
+  if (!ctx || !out64) return fail(EMMY_EINVAL, "null argument");
+  DRV_OR_FAIL();
+  CU_TRY(g_drv.cuCtxSetCurrent(ctx->cu), "cuCtxSetCurrent");
+  CUipcMemHandle h;
+  CU_TRY(g_drv.cuIpcGetMemHandle(&h, ptr), "cuIpcGetMemHandle");
+  static_assert(sizeof(h) == 64, "CUipcMemHandle is 64 bytes");
+  std::memcpy(out64, &h, sizeof(h));
+  return EMMY_OK;
+}
+
+int emmy_ipc_open(emmy_ctx *ctx, const void *handle64, emmy_dptr *out) {
+  if (!ctx || !handle64 || !out) return fail(EMMY_EINVAL, "null argument");
+  DRV_OR_FAIL();
+  CU_TRY(g_drv.cuCtxSetCurrent(ctx->cu), "cuCtxSetCurrent");
+  CUipcMemHandle h;
+  std::memcpy(&h, handle64, sizeof(h));
+  CUdeviceptr p = 0;
+  CU_TRY(g_drv.cuIpcOpenMemHandle(&p, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS),
+         "cuIpcOpenMemHandle");
+  *out = p;
+  return EMMY_OK;
+}
+
+int emmy_ipc_close(emmy_ctx *ctx, emmy_dptr ptr) {
+  if (!ctx) return fail(EMMY_EINVAL, "null ctx");
+  DRV_OR_FAIL();
+  CU_TRY(g_drv.cuCtxSetCurrent(ctx->cu), "cuCtxSetCurrent");
+  CU_TRY(g_drv.cuIpcCloseMemHandle(ptr), "cuIpcCloseMemHandle");
   return EMMY_OK;
 }
 

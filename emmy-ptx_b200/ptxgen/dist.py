@@ -1,10 +1,12 @@
-"""Multi-GPU plumbing: one process per GPU, sharding, the NCCL all-reduce.
+"""Multi-GPU plumbing: one process per GPU, sharding, peer inboxes, NCCL.
 
 The reference is single-GPU (no collective anywhere).  Here work that shards
 naturally is partitioned across the GPUs of one node with no exchange --
 element ranges for pointwise work, row blocks for row kernels, M rows for
-matmul, batch*head for attention -- and full reductions add one NCCL
-all-reduce of the per-rank results over NVLink.
+matmul, batch*head for attention.  Full reductions exchange their per-rank
+results inside the reduction kernel itself, through peer inboxes mapped over
+CUDA IPC (NVLink stores, no separate collective launch); an NCCL all-reduce
+of the per-rank results is the alternative path.
 
 Host-side coordination (rendezvous, timing reductions, the NCCL unique id)
 goes through ``torch.distributed`` with the ``gloo`` backend: plumbing only,
@@ -75,10 +77,68 @@ class Rendezvous:
         self.td.broadcast_object_list(obj, src=src)
         return obj[0]
 
+    def allgather_bytes(self, b: bytes) -> list[bytes]:
+        """Every rank's ``b``, in rank order."""
+        if self.td is None:
+            return [b]
+        out = [None] * self.world
+        self.td.all_gather_object(out, b)
+        return out
+
     def close(self) -> None:
         if self.td is not None:
             self.td.destroy_process_group()
             self.td = None
+
+
+def physical_gpu(ordinal: int) -> str:
+    """Host name and the physical GPU behind CUDA ordinal ``ordinal`` (the
+    ``CUDA_VISIBLE_DEVICES`` entry, or the ordinal when unset)."""
+    import socket
+    vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    gpu = vis[ordinal] if ordinal < len(vis) else str(ordinal)
+    return f"{socket.gethostname()}:{gpu}"
+
+
+class PeerInbox:
+    """A small device buffer on every rank, opened by every other rank over
+    CUDA IPC: the target of a kernel that publishes its partial result
+    straight into its peers' memory over NVLink and reads theirs from its own
+    (the fused cross-GPU reduction of the full-reduce template).  ``ptrs[r]``
+    addresses rank r's inbox from this rank's GPU."""
+
+    BYTES = 4096
+
+    def __init__(self, dev, rdv: Rendezvous):
+        self.dev, self.rank, self.world = dev, rdv.rank, rdv.world
+        # kernels of different ranks wait for one another: they must run on
+        # different GPUs, never as separate launches on one
+        ids = rdv.allgather_bytes(physical_gpu(dev.ordinal).encode())
+        if len(set(ids)) != len(ids):
+            raise RuntimeError(f"peer inboxes need one GPU per rank, got {[i.decode() for i in ids]}")
+        self.local = dev.alloc(self.BYTES)
+        dev.memset32(self.local, 0, self.BYTES // 4)
+        dev.sync()
+        handles = rdv.allgather_bytes(dev.ipc_handle(self.local))
+        self.ptrs, self.opened = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.local)
+            else:
+                p = dev.ipc_open(h)
+                self.opened.append(p)
+                self.ptrs.append(p)
+        rdv.barrier()            # every inbox zeroed and mapped before any kernel writes
+        self.rdv = rdv
+
+    def close(self) -> None:
+        if self.local:
+            self.dev.sync()
+            self.rdv.barrier()   # no peer is still writing into this inbox
+            for p in self.opened:
+                self.dev.ipc_close(p)
+            self.dev.free(self.local)
+            self.local, self.opened = 0, []
 
 
 class NcclComm:

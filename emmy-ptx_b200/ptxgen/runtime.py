@@ -76,6 +76,9 @@ def load_library():
         "emmy_memcpy_dtoh": (i32, [vp, u64, sz, vp]),
         "emmy_memcpy_dtod": (i32, [u64, u64, sz, vp]),
         "emmy_memset_d32": (i32, [u64, u32, sz, vp]),
+        "emmy_ipc_handle": (i32, [vp, u64, vp]),
+        "emmy_ipc_open": (i32, [vp, vp, C.POINTER(u64)]),
+        "emmy_ipc_close": (i32, [vp, u64]),
         "emmy_stream_create": (i32, [vp, C.POINTER(vp)]),
         "emmy_stream_destroy": (i32, [vp]),
         "emmy_stream_sync": (i32, [vp]),
@@ -175,6 +178,24 @@ class Device:
 
     def host_free(self, ptr: int) -> None:
         check(self.L.emmy_host_free(self.ctx, C.c_void_p(ptr)), "emmy_host_free")
+
+    def ipc_handle(self, ptr: int) -> bytes:
+        """64-byte handle another process can open to address ``ptr``."""
+        buf = C.create_string_buffer(64)
+        check(self.L.emmy_ipc_handle(self.ctx, C.c_uint64(ptr), buf), "ipc handle")
+        return buf.raw
+
+    def ipc_open(self, handle: bytes) -> int:
+        """Device pointer, valid in this context, to a peer's allocation."""
+        if len(handle) != 64:
+            raise EmmyError("an IPC handle is 64 bytes")
+        out = C.c_uint64()
+        buf = C.create_string_buffer(handle, 64)
+        check(self.L.emmy_ipc_open(self.ctx, buf, C.byref(out)), "ipc open")
+        return out.value
+
+    def ipc_close(self, ptr: int) -> None:
+        check(self.L.emmy_ipc_close(self.ctx, C.c_uint64(ptr)), "ipc close")
 
     def dtod(self, dst: int, src: int, nbytes: int, stream=None) -> None:
         check(self.L.emmy_memcpy_dtod(C.c_uint64(dst), C.c_uint64(src), nbytes,
@@ -370,6 +391,26 @@ class PreparedKernel:
         for f in self.plan.get("flags", []):
             ptr, size = self.mod.global_ptr(f["sym"])
             self.dev.htod(ptr, np.array([int(f["value"])], dtype=np.uint32))
+        self.dev.sync()
+
+    def attach_peers(self, inbox) -> None:
+        """Join a multi-GPU full reduction: the kernel's cross-GPU exchange
+        (plan ``xgpu``) publishes into and reads from ``inbox``'s buffers
+        (``ptxgen.dist.PeerInbox``).  Every rank must launch this kernel the
+        same number of times: each launch meets the others' once."""
+        x = self.plan.get("xgpu")
+        if not x:
+            raise EmmyError(f"{self.spec.entry}: this kernel has no cross-GPU exchange")
+        if not 1 <= inbox.world <= int(x["max_ranks"]):
+            raise EmmyError(f"cross-GPU exchange supports 1..{x['max_ranks']} ranks")
+        ptrs = np.zeros(int(x["max_ranks"]), dtype=np.uint64)
+        ptrs[:inbox.world] = inbox.ptrs
+        for sym, arr in ((x["peers"], ptrs),
+                         (x["rank"], np.array([inbox.rank], np.uint32)),
+                         (x["epoch"], np.array([0], np.uint32)),
+                         (x["world"], np.array([inbox.world], np.uint32))):
+            ptr, _ = self.mod.global_ptr(sym)
+            self.dev.htod(ptr, arr)
         self.dev.sync()
 
     def upload(self, inputs: dict[str, np.ndarray], stream=None) -> int:

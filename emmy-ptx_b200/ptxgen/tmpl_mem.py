@@ -496,6 +496,144 @@ def _block_combine(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, slots: str, parit
     lo.shuffle_combine(states, ws.state_b, ws.combine_states)
 
 
+# ---- fused cross-GPU reduction ---------------------------------------------
+# Inbox of one rank (``ptxgen.dist.PeerInbox``, one per kernel): partial
+# states at (parity * XG_MAX_RANKS + rank) * 16 bytes, flags at XG_FLAGS +
+# (parity * XG_MAX_RANKS + rank) * 4.  Parity is the launch epoch's low bit:
+# a rank one launch ahead writes the other half, and cannot be two ahead,
+# because finishing a launch needs every rank's flag of that launch.
+XG_MAX_RANKS = 8
+XG_MAX_STATES = 4
+XG_FLAGS = 2 * XG_MAX_RANKS * 16
+XG_WAIT_NS = 2_000_000_000
+ERR_PEER_TIMEOUT = 0x203
+
+
+def _xgpu_globals(mod: Module) -> dict:
+    mod.add_global(".visible .global .align 4 .u32 emmy_xworld;")
+    mod.add_global(".visible .global .align 4 .u32 emmy_xrank;")
+    mod.add_global(".visible .global .align 4 .u32 emmy_xepoch;")
+    mod.add_global(f".visible .global .align 8 .u64 emmy_xpeer[{XG_MAX_RANKS}];")
+    return {"world": "emmy_xworld", "rank": "emmy_xrank", "epoch": "emmy_xepoch",
+            "peers": "emmy_xpeer", "max_ranks": XG_MAX_RANKS}
+
+
+def _emit_xgpu_exchange(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, ident: list[Val],
+                        slots: str) -> None:
+    """With ``emmy_xworld`` > 1: thread 0 of the CTA holding this rank's
+    total stores it into every rank's inbox over NVLink, raises its flag
+    there (release, system scope) with the launch epoch, waits -- bounded by
+    %globaltimer -- for every rank's flag in its own inbox (acquire), folds
+    the ranks' partials in rank order with the IR's combine (the same result
+    on every rank) and shares it with the CTA through shared memory."""
+    states = list(ws.state)
+    ns = len(states)
+    kinds = [lo.env[s].kind for s in states]
+    tt = ["f32" if kd == "f32" else "b32" for kd in kinds]
+    tid = k.sreg("%tid.x")
+    p, q = k.reg("pred"), k.reg("pred")
+    world = k.reg("u32")
+    done, bcast = k.label("xdone"), k.label("xbcast")
+    k(f"ld.global.u32 {world}, [emmy_xworld]")
+    k(f"setp.le.u32 {p}, {world}, 1")
+    k(f"@{p} bra {done}")
+    k("bar.sync 0")                           # the CTA's combine reads of the slots are done
+    k(f"setp.ne.u32 {q}, {tid}, 0")
+    k(f"@{q} bra {bcast}")
+    rank, ep, par, slot = (k.reg("u32") for _ in range(4))
+    k(f"ld.global.u32 {rank}, [emmy_xrank]")
+    k(f"ld.global.u32 {ep}, [emmy_xepoch]")
+    k(f"add.u32 {ep}, {ep}, 1")
+    k(f"st.global.u32 [emmy_xepoch], {ep}")
+    k(f"and.b32 {par}, {ep}, 1")
+    k(f"mad.lo.u32 {slot}, {par}, {XG_MAX_RANKS}, {rank}")
+    voff, foff = k.reg("u64"), k.reg("u64")
+    k(f"mul.wide.u32 {voff}, {slot}, 16")
+    k(f"mul.wide.u32 {foff}, {slot}, 4")
+    k(f"add.u64 {foff}, {foff}, {XG_FLAGS}")
+    peers = k.reg("u64")
+    k(f"mov.u64 {peers}, emmy_xpeer")
+    # publish the partial states, then the flags
+    i, pa, a = k.reg("u32"), k.reg("u64"), k.reg("u64")
+    for phase in ("val", "flag"):
+        lp, end = k.label(f"x{phase}"), k.label(f"x{phase}end")
+        k(f"mov.u32 {i}, 0")
+        k.place(lp)
+        k(f"setp.ge.u32 {p}, {i}, {world}")
+        k(f"@{p} bra {end}")
+        k(f"mad.wide.u32 {pa}, {i}, 8, {peers}")
+        k(f"ld.global.u64 {pa}, [{pa}]")
+        if phase == "val":
+            k(f"add.u64 {a}, {pa}, {voff}")
+            for j, s in enumerate(states):
+                k(f"st.global.{tt[j]} [{a}+{4 * j}], {lo.env[s].reg}")
+        else:
+            k(f"add.u64 {a}, {pa}, {foff}")
+            k(f"st.global.release.sys.u32 [{a}], {ep}")
+        k(f"add.u32 {i}, {i}, 1")
+        k(f"bra.uni {lp}")
+        k.place(end)
+    # wait for every rank's flag of this epoch in the own inbox
+    own = k.reg("u64")
+    k(f"mad.wide.u32 {own}, {rank}, 8, {peers}")
+    k(f"ld.global.u64 {own}, [{own}]")
+    t0, t1 = k.reg("u64"), k.reg("u64")
+    k(f"mov.u64 {t0}, %globaltimer")
+    f, row = k.reg("u32"), k.reg("u32")
+    wl, wnext, wend, tout = k.label("xwait"), k.label("xwnext"), k.label("xwend"), k.label("xtout")
+    k(f"mov.u32 {i}, 0")
+    k.place(wl)
+    k(f"setp.ge.u32 {p}, {i}, {world}")
+    k(f"@{p} bra {wend}")
+    k(f"mad.lo.u32 {row}, {par}, {XG_MAX_RANKS}, {i}")
+    k(f"mad.wide.u32 {a}, {row}, 4, {own}")
+    k(f"add.u64 {a}, {a}, {XG_FLAGS}")
+    spin = k.label("xspin")
+    k.place(spin)
+    k(f"ld.global.acquire.sys.u32 {f}, [{a}]")
+    k(f"setp.eq.u32 {p}, {f}, {ep}")
+    k(f"@{p} bra {wnext}")
+    k(f"mov.u64 {t1}, %globaltimer")
+    k(f"sub.u64 {t1}, {t1}, {t0}")
+    k(f"setp.gt.u64 {p}, {t1}, {XG_WAIT_NS}")
+    k(f"@{p} bra {tout}")
+    k(f"bra.uni {spin}")
+    k.place(wnext)
+    k(f"add.u32 {i}, {i}, 1")
+    k(f"bra.uni {wl}")
+    k.place(tout)
+    k(f"st.global.u32 [emmy_err], {ERR_PEER_TIMEOUT}")
+    k.place(wend)
+    # fold the ranks' partials in rank order (a rank that timed out adds
+    # whatever its slot holds; the error word reports it)
+    for j, s in enumerate(states):
+        lo.bind(s, ident[j])
+    fl, fend = k.label("xfold"), k.label("xfoldend")
+    k(f"mov.u32 {i}, 0")
+    k.place(fl)
+    k(f"setp.ge.u32 {p}, {i}, {world}")
+    k(f"@{p} bra {fend}")
+    k(f"mad.lo.u32 {row}, {par}, {XG_MAX_RANKS}, {i}")
+    k(f"mad.wide.u32 {a}, {row}, 16, {own}")
+    for j, (s, sb) in enumerate(zip(states, ws.state_b)):
+        r = k.reg(kinds[j])
+        k(f"ld.global.relaxed.sys.{tt[j]} {r}, [{a}+{4 * j}]")
+        lo.bind(sb, Val(r, kinds[j]))
+    lo.run(ws.combine_states)
+    k(f"add.u32 {i}, {i}, 1")
+    k(f"bra.uni {fl}")
+    k.place(fend)
+    for j, s in enumerate(states):
+        k(f"st.shared.{tt[j]} [{slots}+{4 * j}], {lo.env[s].reg}")
+    k.place(bcast)
+    k("bar.sync 0")
+    for j, s in enumerate(states):
+        r = k.reg(kinds[j])
+        k(f"ld.shared.{tt[j]} {r}, [{slots}+{4 * j}]")
+        lo.bind(s, Val(r, kinds[j]))
+    k.place(done)
+
+
 def _preload_consts(lo: Lowerer, spec, base, lbs) -> dict:
     """Load every 1-element buffer the loops read, once, before any branch,
     so the register holds the value on every path."""
@@ -757,6 +895,10 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     k("bar.sync 0")  # red_slots are reused
     _block_combine(lo, k, ws, "red_slots", None, ident)
     k.place(single)
+    xg = None
+    if ns <= XG_MAX_STATES:
+        xg = _xgpu_globals(mod)
+        _emit_xgpu_exchange(lo, k, ws, ident, "red_slots")
     # epilogue: the IR's statements after the tree, with the cooperative
     # index equal to the thread index (so "coop == 0" is one thread)
     co = k.reg("s32")
@@ -768,6 +910,8 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": 512, "grid_per_sm": 4,
                 "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / 512))), "smem": 0,
                 "scratch": {"emmy_part": MAX_PARTIALS * 4, "emmy_ticket": 4}}
+    if xg is not None:
+        mod.plan["xgpu"] = xg
     return mod
 
 

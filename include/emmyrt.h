@@ -117,6 +117,15 @@ int emmy_memcpy_htod(emmy_dptr dst, const void *src, size_t bytes, emmy_stream s
 int emmy_memcpy_dtoh(void *dst, emmy_dptr src, size_t bytes, emmy_stream stream);
 int emmy_memcpy_dtod(emmy_dptr dst, emmy_dptr src, size_t bytes, emmy_stream stream);
 /* "zero_outputs": buffers re-zeroed before every launch (docs/API.md:31). */
+/* Peer inboxes for the fused cross-GPU reduction (no counterpart in the
+ * reference, which has no multi-GPU path): export a device allocation as a
+ * 64-byte IPC handle, open a peer process's handle (peer access enabled
+ * lazily; the returned pointer addresses the peer GPU's memory over
+ * NVLink), close it. */
+int emmy_ipc_handle(emmy_ctx *ctx, emmy_dptr ptr, void *out64);
+int emmy_ipc_open(emmy_ctx *ctx, const void *handle64, emmy_dptr *out);
+int emmy_ipc_close(emmy_ctx *ctx, emmy_dptr ptr);
+
 int emmy_memset_d32(emmy_dptr dst, uint32_t value, size_t count, emmy_stream stream);
 
 /* ---- streams and events (the runner's median_us timing) ---- */

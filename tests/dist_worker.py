@@ -5,7 +5,10 @@ Modes:
            CPU oracle, the partial results are summed over gloo, rank 0
            prints the global mean as JSON;
   bcast -- rank 0 broadcasts 128 bytes (the NCCL unique id path);
-  die   -- rank 1 exits before the rendezvous; rank 0 must fail on the host.
+  die   -- rank 1 exits before the rendezvous; rank 0 must fail on the host;
+  gather -- every rank all-gathers a 64-byte token (the IPC handle exchange of
+           the peer inboxes) and the physical GPU names of two layouts: one
+           GPU per rank, and two ranks on one GPU (which peer inboxes refuse).
 """
 
 import json
@@ -33,6 +36,17 @@ def main():
         b = bytes(range(128)) if rank == 0 else None
         got = rdv.bcast_bytes(b)
         print(json.dumps({"rank": rank, "ok": got == bytes(range(128))}), flush=True)
+    elif mode == "gather":
+        from ptxgen.dist import physical_gpu
+        tok = bytes([rank]) * 64
+        got = rdv.allgather_bytes(tok)
+        os.environ["CUDA_VISIBLE_DEVICES"] = "3,5"
+        distinct = rdv.allgather_bytes(physical_gpu(rank).encode())
+        shared = rdv.allgather_bytes(physical_gpu(0).encode())
+        print(json.dumps({"rank": rank, "ok": got == [bytes([r]) * 64 for r in range(rdv.world)],
+                          "distinct": len(set(distinct)) == len(distinct),
+                          "shared_detected": len(set(shared)) < len(shared),
+                          "names": [d.decode().split(":")[-1] for d in distinct]}), flush=True)
     elif mode == "mean":
         from oracle.interp import interpret
         from ptxgen import irgen

@@ -70,3 +70,15 @@ def test_missing_rank_fails_on_the_host():
     outs = _launch("die", timeout=90, extra_env={"RDV_TIMEOUT": "5"})
     assert outs[1][0] == 3
     assert outs[0][0] != 0, "the surviving rank must fail, not hang or succeed"
+
+
+def test_allgather_for_peer_inboxes():
+    """The IPC-handle exchange of ``PeerInbox`` and its one-GPU-per-rank check
+    (run on gloo ranks: no GPU is touched)."""
+    outs = _launch("gather")
+    assert len(outs) == 2
+    for rc, out, err in outs:
+        assert rc == 0, err
+        o = json.loads(out.strip().splitlines()[-1])
+        assert o["ok"] and o["distinct"] and o["shared_detected"]
+        assert o["names"] == ["3", "5"]
