@@ -148,6 +148,15 @@ def match_matmul(spec: KernelSpec) -> MatmulPlan:
     while plan.slices > 1 and (slice_k % BK or slice_k < 4 * BK):
         plan.slices //= 2
         slice_k = k // plan.slices
+    # A CTA accumulates its tile's K slices in TMEM before its one atomic add
+    # (the same sum, another association): keep only as many slice groups as
+    # the SMs need -- at least two waves of units on B200's 148 SMs.
+    if plan.atomic and plan.bn and m % BM == 0:
+        tiles = (m // BM) * (n // plan.bn)
+        while (plan.slices > 1 and plan.slices % 2 == 0
+               and tiles * (plan.slices // 2) >= 2 * SM_COUNT):
+            plan.slices //= 2
+            slice_k = k // plan.slices
     plan.slice_k = slice_k
     plan.tc = (m % BM == 0 and plan.bn > 0 and k % 32 == 0 and slice_k % BK == 0
                and m * n < 2 ** 31 and m * k < 2 ** 31 and k * n < 2 ** 31)
@@ -194,6 +203,7 @@ class _Ctx:
 
 
 SUSPEND_HINT_NS = 100000
+SM_COUNT = 148                   # B200 (sm_100a)
 
 
 def _desc_const(lbo: int, sbo: int, layout: int) -> int:
