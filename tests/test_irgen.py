@@ -47,3 +47,17 @@ def test_bench_kernels_parse():
         g, m = fn()
         spec = load_kernel_data(g, m, name)
         assert spec.entry
+
+
+def test_splitk_groups_slices_per_cta():
+    """The tcgen05 matmul template keeps only as many K-slice groups of a
+    split-K IR as two waves of units on 148 SMs need: a CTA accumulates the
+    rest in TMEM before its one atomic add."""
+    from ptxgen import tmpl_mma
+    from ptxgen.loader import load_kernel_data
+    big = load_kernel_data(*irgen.matmul_splitk(16384, 4096, 1024, slice_k=128), "big")
+    p = tmpl_mma.match_matmul(big)
+    assert p.tc and p.slices == 1 and p.slice_k == 1024      # 2048 tiles: no split needed
+    small = load_kernel_data(*irgen.matmul_splitk(256, 128, 256, slice_k=64), "small")
+    p = tmpl_mma.match_matmul(small)
+    assert p.slices == 4 and p.slice_k == 64                 # 2 tiles: keep the slices
