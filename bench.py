@@ -382,7 +382,8 @@ def run_ours(args, dist: Dist):
     # and joined back to the main stream every step): a reduction's last CTA
     # waiting for the other GPUs then overlaps the step's other kernels.  Only
     # that CTA waits, and only on other GPUs, so concurrent kernels cannot
-    # starve one another.
+    # starve one another.  (On one GPU the jobs stay on one stream: measured
+    # faster there.)
     concurrent = any(j.inbox is not None for j in jobs)
     if concurrent:
         ev_fork = dev.event()
