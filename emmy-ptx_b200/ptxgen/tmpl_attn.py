@@ -6,27 +6,31 @@ over the head dimension, coupled max/sum Accums, final multiply by the
 reciprocal of the sum).  K is given either transposed (``kt [D, S]``, the
 shipped problems) or as ``k [.., S, D]``.
 
-B200 kernel (one persistent CTA per SM, 192 threads; a unit is one
-batch*head and 128 query rows):
+B200 kernel (one persistent CTA per SM, 352 threads -- 224 when shared memory
+allows one softmax thread per row only; a unit is one batch*head and 128
+query rows):
 
-* warp 0 -- TMA: the unit's Q tile once, then per key block the K block and
-  the V^T block (all K-major, 128-byte swizzle), into two stages each when
-  shared memory holds them (bf16 up to D=128), else one, with separate
-  full/empty barriers for K and V so K_{g+1} streams in once S_g is done;
-* warp 1 -- allocates TMEM (two S blocks + O, f32) and issues
-  ``S = Q . K^T`` then ``O += P . V^T`` with ``tcgen05.mma`` (kind::tf32 in
-  three hi/lo passes for f32 data; kind::f16 on bf16 data).  With two K/V
-  stages it issues ``S_{g+1}`` ahead of ``O += P_g V_g``, so the tensor pipe
-  works on the next scores while the softmax warps exponentiate these;
-* warps 2-5 -- one thread per query row: ``tcgen05.ld`` of its S row, row max,
-  ``p = exp(s/c0 - m)``, running sum, P written to shared memory as the A
-  operand of the next MMA (hi/lo TF32 or bf16), rescale of its O row in TMEM
-  only when the row max grew by more than 8 (``m`` is otherwise kept, so
-  ``p <= e^8``; the result is the same sum, only rounded differently), and at
-  the end ``O / l`` to global memory.
+* the last warp -- TMA: the unit's Q tile once (bf16), then per key block the
+  K block and the V^T block (all K-major, 128-byte swizzle) into as many
+  stages as shared memory holds, with separate full/empty barriers for K and
+  V;
+* warp 0 -- issues ``S = Q . K^T`` into one of two TMEM S buffers as soon as
+  the K block is in and the buffer is free (f32: Q from TMEM, two MMAs per
+  K-step); warp 1 -- allocates TMEM and issues ``O += P . V^T`` with P read
+  from TMEM once the softmax warps have written it (kind::tf32 in hi/lo
+  passes for f32 data, kind::f16 on bf16 data).  Two issuing warps on two SM
+  sub-partitions split the issue cost;
+* warps 2-9 (2-5 when shared memory is short) -- one or two threads per
+  query row (f32: first its Q row, split into TF32 hi/lo, into TMEM):
+  ``tcgen05.ld`` of its S columns, row max (swapped with the partner thread),
+  ``p = exp(s/c0 - m)``, running sum, P written over its S columns in TMEM as
+  the A operand of the P . V MMA (hi/lo TF32 or packed bf16), rescale of its
+  O columns in TMEM only when the row max grew by more than 8 (``m`` is
+  otherwise kept, so ``p <= e^8``; the result is the same sum, only rounded
+  differently), and at the end ``O / l`` to global memory.
 
-A pre-pass writes the hi/lo TF32 halves of Q and K (f32 only) and V^T (and K
-from K^T when the IR gives K transposed) into a launcher-owned workspace.
+A pre-pass writes the hi/lo TF32 halves of K (f32 only) and V^T (and K from
+K^T when the IR gives K transposed) into a launcher-owned workspace.
 Every wait is bounded by ``%globaltimer`` and reports through ``emmy_err``.
 
 Any other launch -- meta.json's geometry, or shapes the tensor-core path
@@ -49,7 +53,7 @@ from .tmpl_mma import ERR_WAIT_TIMEOUT, PLAN_MAGIC, _Ctx, _desc_const
 LOG2E = 1.4426950408889634
 SMEM_MAX = 232448            # shared memory per CTA, static + dynamic
 XCH_STATIC = 4096            # static shared memory of the two-threads-per-row form
-W_PROD, W_MMA = 0, 1
+W_QK, W_PV = 0, 1           # S = Q.K^T issuer, O += P.V^T issuer (and TMEM owner)
 BQ = 128
 RESCALE_T = 8.0
 
@@ -184,7 +188,9 @@ def _layout(plan):
     # fit beside the dynamic layout, else one (warps 2-5)
     split = 2 if off + 1024 + XCH_STATIC <= SMEM_MAX else 1
     lay["split"] = split
-    lay["threads"] = 64 + 128 * split
+    # warps 0-1 MMA issue, 2 .. 1+4*split softmax, then one TMA warp
+    lay["threads"] = 96 + 128 * split
+    lay["w_prod"] = 2 + 4 * split
     lay.update(q_bytes=q_bytes, k_bytes=k_bytes, v_bytes=v_bytes,
                q_chunk=q_chunk, k_chunk=k_chunk, v_chunk=v_chunk,
                halves=halves, kvst=kvst)
@@ -644,7 +650,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
             return lay[("k", 0, 0)] + c * 2 * lay["k_chunk"] + h * lay["k_chunk"]
         return lay[("k", 0, 0)] + c * lay["k_chunk"]
     cx = _Ctx(k)
-    for nm in ("q_full", "q_empty", "pv_done", "o_full", "drain"):
+    for nm in ("q_full", "q_empty", "pv_done", "o_full", "drain", "drain_qk"):
         k.shared(f"\t.shared .align 8 .b64 bar_{nm};")
     for nm, cnt in (("k_full", kvst), ("k_empty", kvst), ("v_full", kvst), ("v_empty", kvst),
                     ("s_full", 2), ("s_free", 2), ("p_full", 2)):
@@ -686,7 +692,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     # wait) or per unit (o_full: the epilogue's wait for the unit's last
     # P . V), so no waiter is ever two phases behind its barrier.
     for nm, cnt in (("q_full", 128 * split if q_tmem else 1), ("q_empty", 1),
-                    ("pv_done", 1), ("o_full", 1), ("drain", 1)):
+                    ("pv_done", 1), ("o_full", 1), ("drain", 1), ("drain_qk", 1)):
         k(f"mbarrier.init.shared::cta.b64 [bar_{nm}], {cnt}")
     for nm, n, cnt in (("k_full", kvst, 1), ("k_empty", kvst, 1), ("v_full", kvst, 1),
                        ("v_empty", kvst, 1), ("s_full", 2, 1), ("s_free", 2, 1),
@@ -699,7 +705,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k("fence.mbarrier_init.release.cluster")
     k.place(skip)
     skip2 = k.label("noalloc")
-    k(f"setp.ne.u32 {p}, {warp}, {W_MMA}")
+    k(f"setp.ne.u32 {p}, {warp}, {W_PV}")
     k(f"@{p} bra {skip2}")
     slot = k.reg("u32")
     k(f"mov.u32 {slot}, tmem_slot")
@@ -712,7 +718,8 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     tmem = k.reg("u32")
     k(f"ld.shared.u32 {tmem}, [tmem_slot]")
     teardown, abort_l = k.label("teardown"), k.label("abort")
-    role_mma, role_sm = k.label("rmma"), k.label("rsm")
+    role_qk, role_pv, role_sm = k.label("rqk"), k.label("rpv"), k.label("rsm")
+    w_prod = lay["w_prod"]
 
     def unit_coords(u):
         bh, qb = k.reg("u32"), k.reg("u32")
@@ -745,8 +752,8 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         return r
 
     # ================= producer =================
-    k(f"setp.ne.u32 {p}, {warp}, {W_PROD}")
-    k(f"@{p} bra {role_mma}")
+    k(f"setp.ne.u32 {p}, {warp}, {w_prod}")
+    k(f"@{p} bra {role_qk}")
     # the whole warp runs the loop (converged, so its addresses stay
     # warp-uniform); one elected lane issues the copies
     pe = k.reg("pred")
@@ -817,177 +824,178 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k.place(ue)
     k(f"bra.uni {teardown}")
 
-    # ================= MMA issuer =================
-    # Key block g: S[g%2] = Q . K_g^T, then (once the softmax warps have
-    # written P_g) O (+)= P_g . V_g^T.  With two K/V stages the issue order is
-    # S_{g+1} before O += P_g V_g, so the tensor pipe computes the next scores
-    # while the softmax warps work on this block's.
-    k.place(role_mma)
-    k(f"setp.ne.u32 {p}, {warp}, {W_MMA}")
-    k(f"@{p} bra {role_sm}")
-    # converged warp, one elected lane issues (descriptors stay warp-uniform)
-    pm = k.reg("pred")
-    k(f"elect.sync _|{pm}, -1")
-    kmaj = _desc_const(16, 1024, 2)      # K-major, 128-byte swizzle, 8-row groups 1 KB apart
-    id_s, id_o = k.reg("u32"), k.reg("u32")
-    k(f"mov.u32 {id_s}, {_idesc(kind, BQ, BKV)}")
-    id_s2 = k.reg("u32")                 # f32: N = 2 * BKV, B = [K_hi; K_lo]
-    k(f"mov.u32 {id_s2}, {_idesc(kind, BQ, 2 * BKV)}")
-    k(f"mov.u32 {id_o}, {_idesc(kind, BQ, D)}")
-    yes = k.reg("pred")
-    k(f"setp.eq.u32 {yes}, 0, 0")
-    o_t = k.reg("u32")
-    k(f"add.u32 {o_t}, {tmem}, {o_col}")
-    uit2, g2, u2 = k.reg("u32"), k.reg("u32"), k.reg("u32")
-    k(f"mov.u32 {uit2}, 0")
-    k(f"mov.u32 {g2}, 0")
-    k(f"mov.u32 {u2}, {cta}")
-    pairs = [(0, 0), (0, 1), (1, 0)] if f32 else [(0, 0)]
+    # ================= MMA issuers =================
+    # Warp 0 issues S_g = Q . K_g^T into S buffer g % 2 as soon as K_g is in
+    # and the buffer is free; warp 1 issues O (+)= P_g . V_g^T once the softmax
+    # warps have written P_g.  Two issuing warps on two SM sub-partitions: the
+    # sub-partition that issues MMAs also runs a quarter of the softmax (TMEM
+    # lane quarters are tied to sub-partitions), so the issue cost is split.
+    # Every ordering between the two goes through a barrier (QK(g) waits
+    # s_free, committed when PV(g - 2) completes), none through program order.
+    def mma_role(which):
+        # converged warp, one elected lane issues (descriptors stay warp-uniform)
+        pm = k.reg("pred")
+        k(f"elect.sync _|{pm}, -1")
+        kmaj = _desc_const(16, 1024, 2)      # K-major, 128-byte swizzle, 8-row groups 1 KB apart
+        id_s, id_o = k.reg("u32"), k.reg("u32")
+        k(f"mov.u32 {id_s}, {_idesc(kind, BQ, BKV)}")
+        id_s2 = k.reg("u32")                 # f32: N = 2 * BKV, B = [K_hi; K_lo]
+        k(f"mov.u32 {id_s2}, {_idesc(kind, BQ, 2 * BKV)}")
+        k(f"mov.u32 {id_o}, {_idesc(kind, BQ, D)}")
+        yes = k.reg("pred")
+        k(f"setp.eq.u32 {yes}, 0, 0")
+        o_t = k.reg("u32")
+        k(f"add.u32 {o_t}, {tmem}, {o_col}")
+        pairs = [(0, 0), (0, 1), (1, 0)] if f32 else [(0, 0)]
 
-    # Shared-memory descriptors: one base per K/V stage, built once; an
-    # operand's descriptor is its stage base plus (byte offset >> 4) in the
-    # 14-bit start-address field (shared addresses stay below 2^18, so the
-    # field never carries).
-    def mkdesc(addr_reg):
-        ad, r = k.reg("u32"), k.reg("u64")
-        k(f"shr.u32 {ad}, {addr_reg}, 4")
-        k(f"and.b32 {ad}, {ad}, 16383")
-        k(f"cvt.u64.u32 {r}, {ad}")
-        k(f"or.b64 {r}, {r}, 0x{kmaj:016X}")
-        return r
+        # Shared-memory descriptors: one base per K/V stage, built once; an
+        # operand's descriptor is its stage base plus (byte offset >> 4) in the
+        # 14-bit start-address field (shared addresses stay below 2^18, so the
+        # field never carries).
+        def mkdesc(addr_reg):
+            ad, r = k.reg("u32"), k.reg("u64")
+            k(f"shr.u32 {ad}, {addr_reg}, 4")
+            k(f"and.b32 {ad}, {ad}, 16383")
+            k(f"cvt.u64.u32 {r}, {ad}")
+            k(f"or.b64 {r}, {r}, 0x{kmaj:016X}")
+            return r
 
-    d_base = mkdesc(ring)
+        d_base = mkdesc(ring)
 
-    def stage_desc(st_):
-        if kvst == 1:
-            return d_base
-        t, r = k.reg("u64"), k.reg("u64")
-        k(f"mul.wide.u32 {t}, {st_}, {stage_k >> 4}")
-        k(f"add.s64 {r}, {d_base}, {t}")
-        return r
+        def stage_desc(st_):
+            if kvst == 1:
+                return d_base
+            t, r = k.reg("u64"), k.reg("u64")
+            k(f"mul.wide.u32 {t}, {st_}, {stage_k >> 4}")
+            k(f"add.s64 {r}, {d_base}, {t}")
+            return r
 
-    def dsc(base_d, off):
-        assert off % 16 == 0
-        r = k.reg("u64")
-        k(f"add.s64 {r}, {base_d}, {off >> 4}")
-        return r
+        def dsc(base_d, off):
+            assert off % 16 == 0
+            r = k.reg("u64")
+            k(f"add.s64 {r}, {base_d}, {off >> 4}")
+            return r
 
-    def issue_qk(gr):
-        st_, phf_ = stage_of(gr)
-        b, phs = k.reg("u32"), k.reg("u32")
-        k(f"and.b32 {b}, {gr}, 1")
-        k(f"shr.u32 {phs}, {gr}, 1")
-        k(f"and.b32 {phs}, {phs}, 1")
-        k(f"xor.b32 {phs}, {phs}, 1")
-        ds = stage_desc(st_)
-        s_t = k.reg("u32")
-        k(f"mad.lo.u32 {s_t}, {b}, {s_cols}, {tmem}")
-        cx.wait(bar_at("k_full", st_), phf_, abort_l)
-        cx.wait(bar_at("s_free", b), phs, abort_l)
-        k("tcgen05.fence::after_thread_sync")
-        first = True
-        # f32: columns [0, BKV) get Q_hi.K_hi + Q_lo.K_hi and [BKV, 2 BKV)
-        # get Q_hi.K_lo (summed by the softmax), from 2 MMAs per K-step
-        # instead of 3; bf16: one product
-        groups = [(0, 0, id_s2), (1, 0, id_s)] if f32 else [(0, 0, id_s)]
-        for (ha, hb, idd) in groups:
-            for c in range(D // atom):
-                for kk in range(4):
-                    if q_tmem:
-                        # A (Q) from TMEM: 8 f32 columns per K-step, lo D on
+        def issue_qk(gr):
+            st_, phf_ = stage_of(gr)
+            b, phs = k.reg("u32"), k.reg("u32")
+            k(f"and.b32 {b}, {gr}, 1")
+            k(f"shr.u32 {phs}, {gr}, 1")
+            k(f"and.b32 {phs}, {phs}, 1")
+            k(f"xor.b32 {phs}, {phs}, 1")
+            ds = stage_desc(st_)
+            s_t = k.reg("u32")
+            k(f"mad.lo.u32 {s_t}, {b}, {s_cols}, {tmem}")
+            cx.wait(bar_at("k_full", st_), phf_, abort_l)
+            cx.wait(bar_at("s_free", b), phs, abort_l)
+            k("tcgen05.fence::after_thread_sync")
+            first = True
+            # f32: columns [0, BKV) get Q_hi.K_hi + Q_lo.K_hi and [BKV, 2 BKV)
+            # get Q_hi.K_lo (summed by the softmax), from 2 MMAs per K-step
+            # instead of 3; bf16: one product
+            groups = [(0, 0, id_s2), (1, 0, id_s)] if f32 else [(0, 0, id_s)]
+            for (ha, hb, idd) in groups:
+                for c in range(D // atom):
+                    for kk in range(4):
+                        if q_tmem:
+                            # A (Q) from TMEM: 8 f32 columns per K-step, lo D on
+                            a_ = k.reg("u32")
+                            k(f"add.u32 {a_}, {tmem}, {q_col + ha * D + c * atom + kk * 8}")
+                            a_ = f"[{a_}]"
+                        else:
+                            a_ = dsc(d_base, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
+                        b_ = dsc(ds, k_addr(hb, c) + kk * 32)
+                        acc = yes
+                        if first:
+                            acc = k.reg("pred")
+                            k(f"setp.ne.u32 {acc}, 0, 0")
+                            first = False
+                        k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a_}, {b_}, {idd}, {acc}")
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar_at('s_full', b)}]")
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar_at('k_empty', st_)}]")
+
+        def issue_pv(gr, jr):
+            st_, phf_ = stage_of(gr)
+            pbuf, php_ = k.reg("u32"), k.reg("u32")
+            k(f"and.b32 {pbuf}, {gr}, 1")
+            k(f"shr.u32 {php_}, {gr}, 1")
+            k(f"and.b32 {php_}, {php_}, 1")
+            ds = stage_desc(st_)
+            firstb = k.reg("pred")
+            k(f"setp.ne.u32 {firstb}, {jr}, 0")
+            cx.wait(bar_at("p_full", pbuf), php_, abort_l)
+            cx.wait(bar_at("v_full", st_), phf_, abort_l)
+            k("tcgen05.fence::after_thread_sync")
+            pb, b2 = k.reg("u32"), k.reg("u32")   # P_g lives in S buffer g % 2
+            k(f"and.b32 {b2}, {gr}, 1")
+            k(f"mov.u32 {pb}, {b2}")
+            k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
+            first = True
+            for c in range(max(1, BKV // atom)):
+                for kk in range(min(4, BKV * e // 32)):
+                    for (ha, hb) in pairs:
+                        # A (P) from TMEM: a 32-byte K-step is 8 columns (16 packed
+                        # bf16 or 8 f32); the f32 lo half sits BKV columns on
                         a_ = k.reg("u32")
-                        k(f"add.u32 {a_}, {tmem}, {q_col + ha * D + c * atom + kk * 8}")
+                        k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8 + ha * BKV}")
                         a_ = f"[{a_}]"
-                    else:
-                        a_ = dsc(d_base, lay[("q", ha)] + c * lay["q_chunk"] + kk * 32)
-                    b_ = dsc(ds, k_addr(hb, c) + kk * 32)
-                    acc = yes
-                    if first:
-                        acc = k.reg("pred")
-                        k(f"setp.ne.u32 {acc}, 0, 0")
+                        b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
+                        acc = firstb if first else yes
                         first = False
-                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{s_t}], {a_}, {b_}, {idd}, {acc}")
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-          f"[{bar_at('s_full', b)}]")
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-          f"[{bar_at('k_empty', st_)}]")
+                        k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{o_t}], {a_}, {b_}, {id_o}, {acc}")
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar_at('v_empty', st_)}]")
+            # P_g was read from S buffer g % 2: the buffer is free once this is done
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar_at('s_free', b2)}]")
+        uit2, g2, u2, j2 = (k.reg("u32") for _ in range(4))
+        k(f"mov.u32 {uit2}, 0")
+        k(f"mov.u32 {g2}, 0")
+        k(f"mov.u32 {u2}, {cta}")
+        ml, me, mj = k.label(f"{which}_unit"), k.label(f"{which}_unitend"), k.label(f"{which}_kv")
+        k.place(ml)
+        k(f"setp.ge.u32 {p}, {u2}, {units}")
+        k(f"@{p} bra {me}")
+        if which == "qk":
+            ph3 = k.reg("u32")
+            k(f"and.b32 {ph3}, {uit2}, 1")
+            cx.wait("bar_q_full", ph3, abort_l)
+        k(f"mov.u32 {j2}, 0")
+        k.place(mj)
+        if which == "qk":
+            issue_qk(g2)
+        else:
+            issue_pv(g2, j2)
+        k(f"add.u32 {g2}, {g2}, 1")
+        k(f"add.u32 {j2}, {j2}, 1")
+        k(f"setp.lt.u32 {p}, {j2}, {nkv}")
+        k(f"@{p} bra {mj}")
+        if which == "qk":
+            if not q_tmem:
+                # the unit's Q tile is free once its last S = Q . K^T is done
+                k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+                  f"[bar_q_empty]")
+        else:
+            # the unit's O is complete once its last P . V is
+            k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[bar_o_full]")
+        k(f"add.u32 {uit2}, {uit2}, 1")
+        k(f"add.u32 {u2}, {u2}, {ncta}")
+        k(f"bra.uni {ml}")
+        k.place(me)
+        k(f"bra.uni {teardown}")
 
-    def issue_pv(gr, jr):
-        st_, phf_ = stage_of(gr)
-        pbuf, php_ = k.reg("u32"), k.reg("u32")
-        k(f"and.b32 {pbuf}, {gr}, 1")
-        k(f"shr.u32 {php_}, {gr}, 1")
-        k(f"and.b32 {php_}, {php_}, 1")
-        ds = stage_desc(st_)
-        firstb = k.reg("pred")
-        k(f"setp.ne.u32 {firstb}, {jr}, 0")
-        cx.wait(bar_at("p_full", pbuf), php_, abort_l)
-        cx.wait(bar_at("v_full", st_), phf_, abort_l)
-        k("tcgen05.fence::after_thread_sync")
-        pb, b2 = k.reg("u32"), k.reg("u32")   # P_g lives in S buffer g % 2
-        k(f"and.b32 {b2}, {gr}, 1")
-        k(f"mov.u32 {pb}, {b2}")
-        k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
-        first = True
-        for c in range(max(1, BKV // atom)):
-            for kk in range(min(4, BKV * e // 32)):
-                for (ha, hb) in pairs:
-                    # A (P) from TMEM: a 32-byte K-step is 8 columns (16 packed
-                    # bf16 or 8 f32); the f32 lo half sits BKV columns on
-                    a_ = k.reg("u32")
-                    k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8 + ha * BKV}")
-                    a_ = f"[{a_}]"
-                    b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
-                    acc = firstb if first else yes
-                    first = False
-                    k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{o_t}], {a_}, {b_}, {id_o}, {acc}")
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-          f"[{bar_at('v_empty', st_)}]")
-        # P_g was read from S buffer g % 2: the buffer is free once this is done
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-          f"[{bar_at('s_free', b2)}]")
-
-    ml, me = k.label("m_unit"), k.label("m_unitend")
-    k.place(ml)
-    k(f"setp.ge.u32 {p}, {u2}, {units}")
-    k(f"@{p} bra {me}")
-    ph3 = k.reg("u32")
-    k(f"and.b32 {ph3}, {uit2}, 1")
-    cx.wait("bar_q_full", ph3, abort_l)
-    issue_qk(g2)
-    j2 = k.reg("u32")
-    k(f"mov.u32 {j2}, 0")
-    mj = k.label("m_kv")
-    k.place(mj)
-    gn, jn = k.reg("u32"), k.reg("u32")
-    k(f"add.u32 {gn}, {g2}, 1")
-    k(f"add.u32 {jn}, {j2}, 1")
-    last = k.reg("pred")
-    k(f"setp.ge.u32 {last}, {jn}, {nkv}")
-    nxt = k.label("m_noqk")
-    if kvst > 1:
-        k(f"@{last} bra {nxt}")
-        issue_qk(gn)
-        k.place(nxt)
-        issue_pv(g2, j2)
-    else:
-        issue_pv(g2, j2)
-        k(f"@{last} bra {nxt}")
-        issue_qk(gn)
-        k.place(nxt)
-    k(f"mov.u32 {g2}, {gn}")
-    k(f"mov.u32 {j2}, {jn}")
-    k(f"@!{last} bra {mj}")
-    # the unit's O is complete once its last P . V is
-    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_o_full]")
-    if not q_tmem:
-        k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_q_empty]")
-    k(f"add.u32 {uit2}, {uit2}, 1")
-    k(f"add.u32 {u2}, {u2}, {ncta}")
-    k(f"bra.uni {ml}")
-    k.place(me)
-    k(f"bra.uni {teardown}")
+    k.place(role_qk)
+    k(f"setp.ne.u32 {p}, {warp}, {W_QK}")
+    k(f"@{p} bra {role_pv}")
+    mma_role("qk")
+    k.place(role_pv)
+    k(f"setp.ne.u32 {p}, {warp}, {W_PV}")
+    k(f"@{p} bra {role_sm}")
+    mma_role("pv")
 
     # ================= softmax / correction / epilogue: warps 2-9 =================
     # Two threads per query row: warps 2-5 take the first half of the key
@@ -1323,27 +1331,30 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"setp.lt.u64 {p}, {t1}, 50000000")
     k(f"@{p} bra {lw}")
     k.place(drained)
-    k(f"setp.ne.u32 {q}, {tid}, {W_MMA * 32}")
-    nd = k.label("nodrain")
-    k(f"@{q} bra {nd}")
-    k("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_drain]")
-    pp2 = k.reg("pred")
-    t2, t3 = k.reg("u64"), k.reg("u64")
-    lw2, ld2 = k.label("mdrain"), k.label("mdraindone")
-    k(f"mov.u64 {t2}, %globaltimer")
-    k.place(lw2)
-    k(f"mbarrier.try_wait.parity.shared::cta.b64 {pp2}, [bar_drain], 0")
-    k(f"@{pp2} bra {ld2}")
-    k(f"mov.u64 {t3}, %globaltimer")
-    k(f"sub.u64 {t3}, {t3}, {t2}")
-    k(f"setp.lt.u64 {pp2}, {t3}, 1000000000")
-    k(f"@{pp2} bra {lw2}")
-    k(f"st.global.u32 [emmy_err], {ERR_WAIT_TIMEOUT + 1}")
-    k.place(ld2)
-    k.place(nd)
+    # each issuing lane (lane 0 of warps 0 and 1, the elect.sync leaders)
+    # waits, bounded, for its own MMAs to complete before TMEM is freed
+    for w_iss, dbar in ((W_QK, "bar_drain_qk"), (W_PV, "bar_drain")):
+        k(f"setp.ne.u32 {q}, {tid}, {w_iss * 32}")
+        nd = k.label("nodrain")
+        k(f"@{q} bra {nd}")
+        k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{dbar}]")
+        pp2 = k.reg("pred")
+        t2, t3 = k.reg("u64"), k.reg("u64")
+        lw2, ld2 = k.label("mdrain"), k.label("mdraindone")
+        k(f"mov.u64 {t2}, %globaltimer")
+        k.place(lw2)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {pp2}, [{dbar}], 0")
+        k(f"@{pp2} bra {ld2}")
+        k(f"mov.u64 {t3}, %globaltimer")
+        k(f"sub.u64 {t3}, {t3}, {t2}")
+        k(f"setp.lt.u64 {pp2}, {t3}, 1000000000")
+        k(f"@{pp2} bra {lw2}")
+        k(f"st.global.u32 [emmy_err], {ERR_WAIT_TIMEOUT + 1}")
+        k.place(ld2)
+        k.place(nd)
     k("barrier.sync 0")
     fin = k.label("fin")
-    k(f"setp.ne.u32 {p}, {warp}, {W_MMA}")
+    k(f"setp.ne.u32 {p}, {warp}, {W_PV}")
     k(f"@{p} bra {fin}")
     k("bar.warp.sync -1")
     k("tcgen05.fence::after_thread_sync")
