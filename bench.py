@@ -12,10 +12,16 @@ Other workloads: ``pointwise`` (c = a + b, 2**28), ``rows`` (RMSNorm,
 softmax, L2-norm on 65536 x 4096), ``matmul``, ``attention``.
 
 Multi-GPU (launched by torch.distributed.run): one process per GPU, weak
-scaling -- each rank owns a full-size shard; full reductions add an NCCL
-all-reduce of the per-rank results (the mean's divisor is the global count,
-so the reduced value is the global mean).  Time is taken on the device with
-events on the launching stream, and the reported time is the max over ranks.
+scaling -- each rank owns a full-size shard; full reductions exchange their
+per-rank totals inside the reduction kernel over NVLink peer inboxes
+(``--collective p2p``, default) or with an NCCL all-reduce after it
+(``--collective nccl``); the mean's divisor is the global count, so the
+reduced value is the global mean.  Time is taken on the device with events
+on the launching stream, and the reported time is the max over ranks.
+
+``value`` comes from a loop of K steps with events only at its ends;
+``kernels_ms`` and the roofline from a second pass that times each job alone
+over K back-to-back launches, again with events only at the batch ends.
 
 ``--impl reference`` times the reference's own CPU algorithm -- the CPU
 oracle restating ``ptxgen/interp.py`` -- on the same configuration, rank 0
@@ -391,8 +397,8 @@ def run_ours(args, dist: Dist):
             j.stream, j.ev_join = dev.new_stream(), dev.event()
         cfg["streams"] = "one stream per job, forked and joined every step"
 
-    def step(events=None):
-        if concurrent and events is None:
+    def step():
+        if concurrent:
             dev.record(ev_fork)
             for j in jobs:
                 dev.wait_event(j.stream, ev_fork)
@@ -406,14 +412,8 @@ def run_ours(args, dist: Dist):
         pending = []
         for i, j in enumerate(jobs):
             if j.pk.has_pre:
-                if events is not None:
-                    dev.record(events[i][2])
                 j.pk.launch_pre()
-            if events is not None:
-                dev.record(events[i][0])
             j.pk.launch_main()
-            if events is not None:
-                dev.record(events[i][1])
             if comm is not None and j.allreduce:
                 pending.append(j)
             if pending and i == last_ar:
@@ -468,20 +468,24 @@ def run_ours(args, dist: Dist):
         dev.sync()
     dist.barrier()
     total_ms = dev.elapsed_ms(t0, t1)
-    # ---- per-kernel durations: a second timed pass with events around each
-    # launch (they add a few microseconds per launch, so they stay out of
-    # the headline timing) ----
-    evs = [[(dev.event(), dev.event(), dev.event()) for _ in jobs] for _ in range(args.steps)]
+    # ---- per-kernel durations: each job alone, ``steps`` back-to-back
+    # launches between two events on the launching stream (an event at every
+    # launch would add microseconds that a 45 us kernel carries; every input
+    # is larger than L2, so a repeated launch re-reads HBM).  Every rank
+    # issues the same batches in the same order. ----
+    per_kernel = {}
     dev.sync()
-    for s in range(args.steps):
-        step(evs[s])
-    dev.sync()
-    per_kernel = {j.key: [dev.elapsed_ms(evs[s][i][0], evs[s][i][1]) for s in range(args.steps)]
-                  for i, j in enumerate(jobs)}
-    for i, j in enumerate(jobs):
-        if j.pk.has_pre:
-            per_kernel[j.key + ".pre"] = [dev.elapsed_ms(evs[s][i][2], evs[s][i][0])
-                                          for s in range(args.steps)]
+    for j in jobs:
+        batches = ([(j.key + ".pre", j.pk.launch_pre)] if j.pk.has_pre else [])
+        batches.append((j.key, j.pk.launch_main))
+        for key, launch in batches:
+            a, b = dev.event(), dev.event()
+            dev.record(a)
+            for _ in range(args.steps):
+                launch()
+            dev.record(b)
+            dev.sync()
+            per_kernel[key] = [dev.elapsed_ms(a, b) / args.steps]
     for j in jobs:
         j.pk.check_errors()
     ms = dist.max(total_ms) / args.steps

@@ -907,7 +907,9 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     lo.run(plan.post)
     k.place(exit_l)
     mod.kernels.append(k)
-    mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": 512, "grid_per_sm": 4,
+    # 512 threads x 2 CTAs per SM: measured fastest on B200 for 2^26 f32
+    # (43.8 us back to back, against 45.5 with 4 CTAs per SM)
+    mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": 512, "grid_per_sm": 2,
                 "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / 512))), "smem": 0,
                 "scratch": {"emmy_part": MAX_PARTIALS * 4, "emmy_ticket": 4}}
     if xg is not None:
