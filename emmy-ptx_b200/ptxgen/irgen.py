@@ -180,9 +180,13 @@ PROGRAMS = {
 
 def pointwise(n: int, unroll: int, program="add", block: int = 256,
               out: str = "add", arg_order=None, constants=(), entry="k_add_pointwise",
-              rtol=0.0, atol=0.0, pid="pointwise"):
-    """``program``: a name in PROGRAMS or a list of steps in that format."""
+              rtol=0.0, atol=0.0, pid="pointwise", dtype="f32"):
+    """``program``: a name in PROGRAMS or a list of steps in that format.
+    ``dtype`` is the element type of the vector inputs, of every op (each
+    result is coerced to it, as ``Assign.dtype`` asks) and of the output;
+    constants stay f32 as the graph's ConstantOps are."""
     steps = PROGRAMS[program] if isinstance(program, str) else list(program)
+    dt = datatype(dtype)
     if n % unroll:
         raise ValueError("n must be a multiple of the unroll factor")
     cells = n // unroll
@@ -192,13 +196,15 @@ def pointwise(n: int, unroll: int, program="add", block: int = 256,
         for st in steps:
             if st[0] == "load":
                 _, base, buf, kind = st
-                body.append(load(f"{base}__u{k}", buf, (idx,) if kind == "vec" else (L(0),)))
+                body.append(load(f"{base}__u{k}", buf, (idx,) if kind == "vec" else (L(0),),
+                                 dtype=dt if kind == "vec" else F32))
             else:
                 _, base, opname, *args = st
-                body.append(assign(f"{base}__u{k}", opname, *[f"{a}__u{k}" for a in args]))
+                body.append(assign(f"{base}__u{k}", opname, *[f"{a}__u{k}" for a in args],
+                                   dtype=dt))
     last = [s for s in steps if s[0] == "op"][-1][1]
     body.append(write(out, (ADD(MUL(V("a0"), L(unroll)), L(0)),),
-                      tuple(f"{last}__u{k}" for k in range(unroll))))
+                      tuple(f"{last}__u{k}" for k in range(unroll)), dtype=dt))
     t = tile([ax("a0", cells)], body)
     vec_inputs = []
     seen = set()
@@ -209,10 +215,10 @@ def pointwise(n: int, unroll: int, program="add", block: int = 256,
     scalar_inputs = sorted({st[2] for st in steps if st[0] == "load" and st[3] == "scalar"})
     if arg_order is None:
         arg_order = [c[0] for c in constants] + vec_inputs + scalar_inputs + [out]
-    inputs = [(b, (n,), "f32", i) for i, b in enumerate(sorted(vec_inputs))]
+    inputs = [(b, (n,), dtype, i) for i, b in enumerate(sorted(vec_inputs))]
     inputs += [(b, (1,), "f32", len(inputs) + i) for i, b in enumerate(scalar_inputs)]
     grid = (math.ceil(cells / block), 1, 1)
-    return package(entry, out, [t], inputs, list(constants), (out, (n,), "f32"), arg_order,
+    return package(entry, out, [t], inputs, list(constants), (out, (n,), dtype), arg_order,
                    grid, (block, 1, 1), rtol=rtol, atol=atol, pid=pid)
 
 
@@ -263,25 +269,32 @@ def _block_combine(tid_axis: str, threads: int, states=("acc0",), kind="add"):
     return out
 
 
-def reduce_full(n: int, threads: int = 128, mean: bool = False, entry=None, pid="reduce_full"):
-    """Full-array sum (r01/r02) or mean (r03) by one CTA of ``threads``."""
+def reduce_full(n: int, threads: int = 128, mean: bool = False, entry=None, pid="reduce_full",
+                dtype="f32", acc_dtype="f32"):
+    """Full-array sum (r01/r02) or mean (r03) by one CTA of ``threads``.
+    ``dtype`` is the input's and the result's element type, ``acc_dtype``
+    the per-thread accumulator's: f32 or f16, the float states the
+    reference's WarpShuffle takes (``ptxgen/emit.py:1385-1395``; the combine
+    itself promotes to f32)."""
     body = [strided("a0", n, V("a0_co"), L(threads),
-                    [load("in0", "x", (V("a0"),)), accum("acc0", "in0", "add", ("a0",))])]
+                    [load("in0", "x", (V("a0"),), dtype=datatype(dtype)),
+                     accum("acc0", "in0", "add", ("a0",), dtype=datatype(acc_dtype))])]
     body += _block_combine("a0_co", threads)
     if mean:
         tail = [load("in1", "mean_keepdim_count", (L(0),)),
-                assign("v0", "divide", "acc0", "in1"), write("mean", (), "v0")]
+                assign("v0", "divide", "acc0", "in1"),
+                write("mean", (), "v0", dtype=datatype(dtype))]
         out, entry = "mean", entry or "k_mean_ffcca3"
         constants = [("mean_keepdim_count", float(n))]
         arg_order = ["x", "mean_keepdim_count", "mean"]
     else:
-        tail = [write("sum_1", (), "acc0")]
+        tail = [write("sum_1", (), "acc0", dtype=datatype(dtype))]
         out, entry = "sum_1", entry or "k_sum_1_reduce"
         constants = []
         arg_order = ["x", "sum_1"]
     body.append(Cond(cond=EQ(V("a0_co"), L(0)), body=tuple(tail), else_body=()))
     t = tile([ax("a0_co", threads)], body, block_threads=threads)
-    return package(entry, out, [t], [("x", (n,), "f32", 0)], constants, (out, (1,), "f32"),
+    return package(entry, out, [t], [("x", (n,), dtype, 0)], constants, (out, (1,), dtype),
                    arg_order, (1, 1, 1), (threads, 1, 1), rtol=1e-4, atol=1e-4, pid=pid,
                    graph_out_shape=())
 
@@ -315,18 +328,34 @@ def write_problem(pdir, graphs: dict, meta: dict) -> None:
 
 
 def reduce_rows(rows: int, cols: int, threads: int = 128, entry="k_sum_1_reduce",
-                pid="reduce_rows"):
-    """Row sum (r04): one row per CTA."""
+                pid="reduce_rows", dtype="f32"):
+    """Row sum (r04): one row per CTA; ``dtype`` as in ``reduce_full``."""
+    dt = datatype(dtype)
     body = [strided("a1", cols, V("a1_co"), L(threads),
-                    [load("in0", "x", (V("a0"), V("a1"))),
+                    [load("in0", "x", (V("a0"), V("a1")), dtype=dt),
                      accum("acc0", "in0", "add", ("a1",))])]
     body += _block_combine("a1_co", threads)
-    body.append(Cond(cond=EQ(V("a1_co"), L(0)), body=(write("sum_1", (V("a0"),), "acc0"),),
-                     else_body=()))
+    body.append(Cond(cond=EQ(V("a1_co"), L(0)),
+                     body=(write("sum_1", (V("a0"),), "acc0", dtype=dt),), else_body=()))
     t = tile([ax("a0", rows), ax("a1_co", threads)], body, block_threads=threads)
-    return package(entry, "sum_1", [t], [("x", (rows, cols), "f32", 0)], [],
-                   ("sum_1", (rows,), "f32"), ["x", "sum_1"], (rows, 1, 1), (threads, 1, 1),
+    return package(entry, "sum_1", [t], [("x", (rows, cols), dtype, 0)], [],
+                   ("sum_1", (rows,), dtype), ["x", "sum_1"], (rows, 1, 1), (threads, 1, 1),
                    rtol=1e-4, atol=1e-4, pid=pid)
+
+
+def reduce_cols(rows: int, cols: int, block: int = 128, dtype="f64", entry="k_sum_0_reduce",
+                pid="reduce_cols"):
+    """Column sum with a per-thread accumulator: one column per thread, a
+    ``Loop`` over the rows folding into an ``Accum`` of ``dtype`` -- the form
+    an f64 reduction takes, since no cross-lane combine is needed."""
+    dt = datatype(dtype)
+    body = [loop("a0", rows, [load("in0", "x", (V("a0"), V("a1")), dtype=dt),
+                              accum("acc0", "in0", "add", ("a0",), dtype=dt)]),
+            write("sum_0", (V("a1"),), "acc0", dtype=dt)]
+    t = tile([ax("a1", cols)], body)
+    return package(entry, "sum_0", [t], [("x", (rows, cols), dtype, 0)], [],
+                   ("sum_0", (cols,), dtype), ["x", "sum_0"], (math.ceil(cols / block), 1, 1),
+                   (block, 1, 1), rtol=1e-5, atol=1e-5, pid=pid)
 
 
 # ---------------------------------------------------------------------------
@@ -695,6 +724,23 @@ def golden_cases():
     add("gen_splitk_32x64x64_s16", matmul_splitk(32, 64, 64, slice_k=16, pid="gen_splitk"))
     add("gen_attn_64x32", attention(64, 32, pid="gen_attn"))
     add("gen_attn_bhsd_2x2x32x32", attention_bhsd(2, 2, 32, 32, pid="gen_attn_bhsd"))
+    # f16 and f64 data paths (``ptxgen/model.py:8-31``, ``ptxgen/interp.py:115-141``)
+    add("gen_add_f64_u2_1000", pointwise(1000, 2, "add", dtype="f64", pid="gen_add_f64"))
+    add("gen_relu_mul_f64_u2_1000", pointwise(1000, 2, "relu_mul", out="mul", dtype="f64",
+                                              entry="k_mul_pointwise", pid="gen_relu_mul_f64"))
+    add("gen_add_f16_u4_4096", pointwise(4096, 4, "add", dtype="f16", pid="gen_add_f16"), 0,
+        "uniform")
+    add("gen_relu_mul_f16_u2_1000", pointwise(1000, 2, "relu_mul", out="mul", dtype="f16",
+                                              entry="k_mul_pointwise", pid="gen_relu_mul_f16"))
+    add("gen_sum_f16_5000", reduce_full(5000, dtype="f16", pid="gen_sum_f16"), 0, "uniform01")
+    add("gen_sum_f16acc_f16_3000", reduce_full(3000, dtype="f16", acc_dtype="f16",
+                                               pid="gen_sum_f16acc"))
+    add("gen_mean_f16_8192_t256", reduce_full(8192, threads=256, mean=True, dtype="f16",
+                                              pid="gen_mean_f16"), 0, "uniform01")
+    add("gen_rowsum_f16_48x300", reduce_rows(48, 300, dtype="f16", pid="gen_rowsum_f16"))
+    add("gen_colsum_f64_64x300", reduce_cols(64, 300, dtype="f64", pid="gen_colsum_f64"))
+    add("gen_colsum_f16_64x300", reduce_cols(64, 300, dtype="f16", pid="gen_colsum_f16"), 0,
+        "uniform01")
     return cases
 
 

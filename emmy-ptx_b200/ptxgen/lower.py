@@ -37,6 +37,20 @@ L2E_HI = float(__import__("numpy").float32(LOG2E))
 L2E_LO = float(__import__("numpy").float32(LOG2E - L2E_HI))
 
 
+def _round_storage(v: float, store: str | None) -> float:
+    """``v`` rounded to f32, then to ``store`` when that is f16 or bf16
+    (round to nearest even; bf16 keeps the top 16 bits of the f32)."""
+    import numpy as np
+    f = np.float32(v)
+    if store == "f16":
+        return float(np.float16(f))
+    if store == "bf16" and np.isfinite(f):
+        b = int(f.view(np.uint32))
+        b = (b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000
+        return float(np.uint32(b).view(np.float32))
+    return float(f)
+
+
 class LowerError(NotImplementedError):
     """The IR uses something this lowering does not handle."""
 
@@ -473,13 +487,25 @@ class Lowerer:
 
     # -- scalar statements -------------------------------------------------
 
-    def identity(self, op_or_value, kind: str) -> Val:
+    def identity(self, op_or_value, kind: str, store: str | None = None) -> Val:
+        """An accumulator's start value: the op's identity or a literal,
+        made an f32 first and then stored in ``kind`` -- and rounded to f16
+        or bf16 when that is the accumulator's storage type
+        (``interp.py:732-739``)."""
         if kind in ("s32", "s64"):
             v = int(ops.identity(op_or_value)) if isinstance(op_or_value, str) else int(op_or_value)
             return self.const(v, kind)
-        if isinstance(op_or_value, str):
-            return self.const(ops.identity(op_or_value), kind)
-        return self.const(float(op_or_value), kind)
+        v = ops.identity(op_or_value) if isinstance(op_or_value, str) else float(op_or_value)
+        v = _round_storage(v, store)
+        return self.const(v, kind)
+
+    def _round(self, v: Val, dtype) -> Val:
+        """Coerce to the value kind of ``dtype`` and, for f16/bf16, round to
+        the storage precision (``interp.py:128-131``, one ``cvt.rn``)."""
+        v = self.coerce(v, value_kind(dtype))
+        if storage_kind(dtype) in ("f16", "bf16"):
+            v = self.coerce(v, storage_kind(dtype))
+        return v
 
     def do_assign(self, st: ir.Assign) -> None:
         for a in st.args:
@@ -487,31 +513,31 @@ class Lowerer:
                 raise LowerError(f"undefined name {a!r}")
         r = self.apply(st.op.name, [self.env[a] for a in st.args])
         if st.dtype is not None:
-            r = self.coerce(r, value_kind(st.dtype))
-            if storage_kind(st.dtype) in ("f16", "bf16"):
-                r = self.coerce(r, storage_kind(st.dtype))
+            r = self._round(r, st.dtype)
         self.bind(st.name, r)
 
     def do_let(self, st: ir.Let) -> None:
         v = self.ev(st.value)
         if st.dtype is not None:
-            v = self.coerce(v, value_kind(st.dtype))
+            v = self._round(v, st.dtype)
         self.bind(st.name, v)
 
     def do_init(self, st: ir.Init) -> None:
-        self.bind(st.name, self.identity(st.identity, value_kind(st.dtype)))
+        self.bind(st.name, self.identity(st.identity, value_kind(st.dtype),
+                                         storage_kind(st.dtype)))
 
     def do_accum(self, st: ir.Accum) -> None:
         kind = value_kind(st.dtype) if st.dtype is not None else "f32"
+        store = storage_kind(st.dtype) if st.dtype is not None else None
         acc = self.env.get(st.name)
         if acc is None or acc.kind != kind:
-            acc = self.bind(st.name, self.identity(st.op.name, kind))
+            acc = self.bind(st.name, self.identity(st.op.name, kind, store))
         left = self.env[st.base] if st.base is not None else acc
         if st.value not in self.env:
             raise LowerError(f"undefined name {st.value!r}")
         r = self.apply(st.op.name, [left, self.env[st.value]])
         if st.dtype is not None:
-            r = self.coerce(r, kind)
+            r = self._round(r, st.dtype)
         self.bind(st.name, r)
 
     def seed_accums(self, body, enabled: bool) -> None:
@@ -527,7 +553,8 @@ class Lowerer:
                     seen.add(st.name)
                     if enabled:
                         kind = value_kind(st.dtype) if st.dtype is not None else "f32"
-                        self.bind(st.name, self.identity(st.op.name, kind))
+                        store = storage_kind(st.dtype) if st.dtype is not None else None
+                        self.bind(st.name, self.identity(st.op.name, kind, store))
                 elif isinstance(st, (ir.Loop, ir.StridedLoop)):
                     continue
                 else:

@@ -164,8 +164,12 @@ class Device:
     # -- memory ------------------------------------------------------------
 
     def alloc(self, nbytes: int) -> int:
+        """Device memory rounded up to 16 bytes, so word-wise zeroing of a
+        buffer whose size is not a multiple of 4 (an odd count of f16)
+        stays inside the allocation."""
         p = C.c_uint64()
-        check(self.L.emmy_mem_alloc(self.ctx, max(16, int(nbytes)), C.byref(p)), "emmy_mem_alloc")
+        check(self.L.emmy_mem_alloc(self.ctx, max(16, (int(nbytes) + 15) & ~15), C.byref(p)),
+              "emmy_mem_alloc")
         return p.value
 
     def free(self, ptr: int) -> None:

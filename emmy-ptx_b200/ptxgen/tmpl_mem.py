@@ -648,7 +648,10 @@ def _preload_consts(lo: Lowerer, spec, base, lbs) -> dict:
 
 def _state_identities(lo: Lowerer, loop_body, states) -> list[Val]:
     """Neutral element per combined state: the identity of the Accum that
-    defines it in the reduction loop."""
+    defines it in the reduction loop.  An accumulator stored as f16 or bf16
+    is rounded after every step, so its per-thread partials depend on which
+    elements each thread folds: such IR keeps its own thread mapping (the
+    generic lowering) instead of a template's re-partitioned grid."""
     acc = {}
     for st in ir.walk(loop_body):
         if isinstance(st, ir.Accum):
@@ -658,6 +661,8 @@ def _state_identities(lo: Lowerer, loop_body, states) -> list[Val]:
         if s not in acc:
             raise NoMatch(f"combined state {s} has no Accum in the loop")
         st = acc[s]
+        if st.dtype is not None and storage_kind(st.dtype) in ("f16", "bf16"):
+            raise NoMatch(f"state {s} accumulates in {storage_kind(st.dtype)}")
         kind = value_kind(st.dtype) if st.dtype is not None else "f32"
         out.append(lo.identity(st.op.name, kind))
     return out

@@ -12,6 +12,12 @@ reference's own tests use for that family.
 Random pointwise DAGs stay finite by construction: every value carries an
 upper bound on its magnitude and an op whose result could pass 1e30 is not
 drawn, divisors are |b| + 1, and the ex2-based ops only see loaded inputs.
+
+A second generator, seeded apart from the one that draws the program, picks
+the element type of pointwise cases (f32, f64, or f16 when the program is
+exactly rounded and its bound stays below f16's range) and of full and row
+sums (f32 or f16 input): the reference's f16/f64 value kinds
+(``ptxgen/interp.py:115-141``) under the same families.
 """
 
 from __future__ import annotations
@@ -27,6 +33,7 @@ EXACT_UNARY = ("negative", "absolute", "relu", "square")
 EXACT_BINARY = ("add", "subtract", "multiply", "maximum", "minimum", "divide")
 APPROX_UNARY = ("exp", "tanh", "sigmoid")
 FAMILIES = ("pointwise", "reduce_full", "rows", "matmul", "splitk", "attention")
+_NPT = {"f32": np.float32, "f64": np.float64, "f16": np.float16}
 
 
 @dataclasses.dataclass
@@ -99,34 +106,43 @@ def _pointwise_program(rng):
     if need_one:
         steps.insert(0, ("load", "one", "c_one", "const"))
         consts.append(("c_one", 1.0))
-    return steps, consts, exact
+    return steps, consts, exact, max(bound.values())
 
 
 def _draw(rng, family, seed):
     f32 = np.float32
+    drng = np.random.default_rng(50_000 + seed)      # element-type draws only
     if family == "pointwise":
-        steps, consts, exact = _pointwise_program(rng)
+        steps, consts, exact, top = _pointwise_program(rng)
         unroll = int(rng.choice([1, 2, 4]))
         n = unroll * int(rng.integers(1, 1 << 15))
         vec = sorted({s[2] for s in steps if s[0] == "load" and s[3] == "vec"})
+        r = drng.random()
+        dt = "f64" if r < 0.2 else ("f16" if r < 0.4 and exact and top < 3e4 else "f32")
         g, m = irgen.pointwise(n, unroll, steps, out="out", constants=consts,
                                block=int(rng.choice([64, 128, 256, 512])),
-                               entry="k_fuzz_pointwise", pid=f"fuzz{seed}")
-        ins = {b: rng.standard_normal(n).astype(f32) for b in vec}
-        return g, m, ins, exact, 1e-5, {"n": n, "program": steps}
+                               entry="k_fuzz_pointwise", pid=f"fuzz{seed}", dtype=dt)
+        ins = {b: rng.standard_normal(n).astype(f32).astype(_NPT[dt]) for b in vec}
+        return g, m, ins, exact, 1e-5, {"n": n, "program": steps, "dtype": dt}
     if family == "reduce_full":
         n = int(rng.integers(1, 1 << 18))
         threads = int(rng.choice([32, 64, 128, 256, 512, 1024]))
         mean = bool(rng.random() < 0.3)
-        g, m = irgen.reduce_full(n, threads=threads, mean=mean, pid=f"fuzz{seed}")
-        return g, m, {"x": rng.uniform(-1, 1, n).astype(f32)}, False, 1e-5, {"n": n}
+        dt = "f16" if drng.random() < 0.25 else "f32"
+        g, m = irgen.reduce_full(n, threads=threads, mean=mean, pid=f"fuzz{seed}", dtype=dt)
+        x = rng.uniform(-1, 1, n).astype(f32).astype(_NPT[dt])
+        return g, m, {"x": x}, False, 1e-5, {"n": n, "dtype": dt}
     if family == "rows":
         kind = str(rng.choice(["rowsum", "rmsnorm", "softmax", "l2norm"]))
         rows = int(rng.integers(1, 200))
         cols = int(rng.integers(1, 3000))
         threads = int(rng.choice([32, 64, 128, 256]))
         if kind == "rowsum":
-            g, m = irgen.reduce_rows(rows, cols, threads=threads, pid=f"fuzz{seed}")
+            dt = "f16" if drng.random() < 0.25 else "f32"
+            g, m = irgen.reduce_rows(rows, cols, threads=threads, pid=f"fuzz{seed}", dtype=dt)
+            x = rng.standard_normal((rows, cols)).astype(f32).astype(_NPT[dt])
+            return g, m, {"x": x}, False, 1e-5, {"kind": kind, "rows": rows, "cols": cols,
+                                                  "dtype": dt}
         elif kind == "rmsnorm":
             g, m = irgen.rmsnorm(rows, cols, threads=threads, pid=f"fuzz{seed}")
         elif kind == "softmax":
@@ -208,6 +224,8 @@ def compare(c: Case, got: dict, want: dict) -> None:
             if name == "mean":
                 total = total / c.extra["n"]
             bound = c.tol * np.maximum(total, 1e-3)
+            if c.extra.get("dtype") == "f16":   # the sum order may move the f16 rounding
+                bound = bound + np.spacing(np.abs(np.asarray(ref))).astype(np.float64)
         else:
             bound = c.tol * np.maximum(np.abs(r), 1.0)
         err = np.abs(g - r)

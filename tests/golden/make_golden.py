@@ -77,16 +77,21 @@ def import_reference(ref: Path):
 
 def rebuild_inputs(spec, seed_offset: int, dist: str) -> dict[str, np.ndarray]:
     """Deterministic inputs for a case: runner argument forms with each
-    ``seed`` shifted by ``seed_offset``; ``dist`` picks the distribution."""
+    ``seed`` shifted by ``seed_offset``; ``dist`` picks the distribution.
+    Values are drawn in f64, rounded to f32 and then stored in the
+    argument's own dtype (f16 and f64 arguments included)."""
+    from ptxgen.runtime import _np_dtype
     out: dict[str, np.ndarray] = {}
     for name in spec.arg_order:
         a = spec.args[name]
         if a.scalar:
             continue
+        dt = _np_dtype(a.dtype)
         if a.output:
-            out[name] = np.zeros(a.shape, dtype=np.float32)
+            out[name] = np.zeros(a.shape, dtype=dt)
         elif a.data is not None:
-            out[name] = np.asarray(a.data, dtype=np.float64).astype(np.float32).reshape(a.shape)
+            out[name] = np.asarray(a.data, dtype=np.float64).astype(np.float32).astype(
+                dt).reshape(a.shape)
         else:
             rng = np.random.default_rng(int(a.seed or 0) + seed_offset)
             if dist == "normal":
@@ -95,7 +100,7 @@ def rebuild_inputs(spec, seed_offset: int, dist: str) -> dict[str, np.ndarray]:
                 x = rng.random(a.shape)
             else:
                 x = rng.uniform(-1.0, 1.0, a.shape)
-            out[name] = x.astype(np.float32)
+            out[name] = x.astype(np.float32).astype(dt)
     for name in spec.zero_outputs:
         if name in out:
             out[name][...] = 0
