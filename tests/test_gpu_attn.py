@@ -64,7 +64,8 @@ def _bhsd(b, h, s, d, dtype, seed=0):
 @pytest.mark.parametrize("dtype,shape", [("f32", (2, 2, 256, 64)), ("f32", (1, 3, 384, 128)),
                                          ("f32", (1, 2, 256, 32)),
                                          ("bf16", (2, 2, 256, 128)), ("bf16", (1, 2, 512, 64)),
-                                         ("bf16", (1, 2, 256, 256))])
+                                         ("bf16", (1, 2, 256, 256)), ("bf16", (1, 2, 384, 128)),
+                                         ("bf16", (2, 1, 256, 32)), ("bf16", (1, 3, 128, 128))])
 def test_generated(dtype, shape):
     b, h, s, d = shape
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "att")
@@ -76,9 +77,26 @@ def test_generated(dtype, shape):
     assert np.abs(out - ref).max() <= tol * scale, float(np.abs(out - ref).max() / scale)
 
 
-@pytest.mark.parametrize("share", [2, 4])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_rescale_path(dtype):
+    """Keys scaled by 1 + 6 j / S: each row's max keeps growing over the key
+    blocks, so O in TMEM is rescaled (max grown by more than 8 in log2
+    units) several times per row."""
+    b, h, s, d = 1, 2, 1024, 128
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "attr")
+    q, k, v = _bhsd(b, h, s, d, dtype, seed=5)
+    grow = (1.0 + 6.0 * np.arange(s) / s)[None, None, :, None]
+    k = (k.astype(np.float64) * grow).astype(k.dtype)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
+    ref = _ref(q, k, v)
+    tol = 1e-4 if dtype == "f32" else 2e-2
+    assert np.abs(out - ref).max() <= tol * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("share", [0, 4])
 def test_bf16_polynomial_exp2(share, monkeypatch):
-    """bf16 P with part (or all) of exp2 evaluated by the FMA-pipe polynomial."""
+    """bf16 P with none or all of exp2 on the FMA-pipe polynomial (the
+    default, two pairs of every four, runs in every other bf16 test)."""
     monkeypatch.setenv("EMMY_ATTN_EXP_POLY", str(share))
     b, h, s, d = 2, 2, 512, 128
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "attp")
