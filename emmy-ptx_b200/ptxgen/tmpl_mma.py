@@ -9,23 +9,23 @@ in TF32) and ``lo = x - hi`` (exact in f32), and the tile product is
 2^-21 relative error per product, well inside the 1e-4 budget for fp32
 contractions (the dropped ``lo.lo`` term is ~2^-22 relative).
 
-Kernel (one persistent CTA per SM, 320 threads):
+Pre-passes write the TF32 hi/lo halves of A and of B (B transposed to
+K-major) into a launcher-owned workspace.  Kernel (one persistent CTA per SM,
+192 threads):
 
-* warp 0, one lane -- TMA producer: per K block of 16, one 128x16 A box
-  (K-major, 64-byte swizzle) and BN/32 16x32 B boxes (N-major, 128-byte
-  swizzle) into a 4-stage shared-memory ring, ``mbarrier`` complete_tx;
-* warps 2-5 -- converters: rewrite each landed stage in place to ``hi`` and
-  write ``lo`` beside it (the split is elementwise, so the swizzled layout of
-  ``lo`` is the layout of the stage), then ``fence.proxy.async`` so the
-  tensor core sees it;
+* warp 0, one lane -- TMA producer: per K block of 16, the A hi/lo boxes
+  (128x16) and the B hi/lo boxes (BNx16), K-major with the 64-byte swizzle,
+  into a 4-stage shared-memory ring, ``mbarrier`` complete_tx;
 * warp 1 -- allocates 2 x BN TMEM columns (two accumulators) and issues, per
   8-deep K step, three ``tcgen05.mma.cta_group::1.kind::tf32`` (M=128,
   N=BN) reading smem matrix descriptors; ``tcgen05.commit`` frees the stage
   and, after the last K block, publishes the accumulator;
-* warps 6-9 -- epilogue: ``tcgen05.ld.32x32b`` of the accumulator (each warp
-  its 32-lane quadrant), 16-byte stores to C (``red.global.add.v4.f32`` for
-  split-K), then hand the accumulator back -- overlapping the next tile's
-  main loop.
+* warps 2-5 -- epilogue: ``tcgen05.ld.32x32b`` of the accumulator (each warp
+  its 32-lane quadrant) 32 columns at a time, written into one of two
+  shared-memory staging buffers (128-byte swizzle) and stored by one thread
+  with a TMA tensor store (``cp.reduce.async.bulk.tensor .add`` for split-K
+  into the launcher-zeroed C), then the accumulator is handed back --
+  overlapping the next tile's main loop.
 
 Every wait is an ``mbarrier.try_wait`` loop bounded by ``%globaltimer``; on
 expiry the kernel raises a shared abort flag and writes ``emmy_err``, every
@@ -33,10 +33,11 @@ role leaves its loop, in-flight copies and MMAs are drained with bounded
 waits, TMEM is freed and the kernel returns.
 
 The tcgen05 path needs the launcher's plan: tensor maps filled in module
-globals, ``emmy_plan`` set, 320 threads and the stated dynamic shared
-memory.  Any other launch (for example meta.json's geometry) takes a SIMT
-path that computes each C element as the IR does -- ``acc = acc + b*a`` in
-K order, rounded per op -- so the PTX is correct under every launch.
+globals (the operand halves in the workspace, and C), ``emmy_plan`` set, 192
+threads and the stated dynamic shared memory.  Any other launch (for
+example meta.json's geometry) takes a SIMT path that computes each C element
+as the IR does -- ``acc = acc + b*a`` in K order, rounded per op -- so the
+PTX is correct under every launch.
 """
 
 from __future__ import annotations
@@ -55,6 +56,9 @@ WAIT_LIMIT_NS = 4_000_000_000    # 4 s: far above any legal wait in these kernel
 BM, BK, STAGES = 128, 16, 4
 THREADS = 192                    # warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 EPI_THREADS = 128
+EPI_COLS = 32                    # C columns per epilogue chunk (128 bytes of f32)
+EPI_BUF = BM * EPI_COLS * 4      # one staging buffer: 128 rows x 128 bytes, 128-byte swizzle
+EPI_ISSUER = 64                  # thread that issues the C stores (warp 2, lane 0)
 W_PROD, W_MMA = 0, 1
 
 
@@ -254,14 +258,15 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
     mod.add_global(".visible .global .align 4 .u32 emmy_err;")
     mod.add_global(".visible .global .align 4 .u32 emmy_plan;")
     mod.add_global(".visible .global .align 8 .u64 emmy_ws;")
-    for t in ("ahi", "alo", "bhi", "blo"):
+    for t in ("ahi", "alo", "bhi", "blo", "c"):
         mod.add_global(f".visible .global .align 64 .b8 tmap_{t}[128];")
     M, N, K = plan.m, plan.n, plan.k
     BN = plan.bn or 32
     a_bytes = BM * BK * 4
     b_bytes = BN * BK * 4
     stage_bytes = 2 * (a_bytes + b_bytes)
-    dyn_smem = STAGES * stage_bytes + 1024
+    # the operand ring, then two staging buffers for the TMA stores of C
+    dyn_smem = STAGES * stage_bytes + 2 * EPI_BUF + 1024
     tcols = max(32, 1 << (2 * BN - 1).bit_length())
     mt, nt = M // BM, (N // BN if plan.bn else 1)
     units = mt * nt * plan.slices
@@ -313,7 +318,10 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
                  "grid_max": (K // 32) * (N // 32)},
             ],
             "tmaps": [tm("tmap_ahi", 0, M, BM), tm("tmap_alo", o_alo, M, BM),
-                      tm("tmap_bhi", o_bhi, N, BN), tm("tmap_blo", o_blo, N, BN)],
+                      tm("tmap_bhi", o_bhi, N, BN), tm("tmap_blo", o_blo, N, BN),
+                      {"sym": "tmap_c", "buf": plan.c, "offset": 0, "dtype": "f32",
+                       "dims": [N, M], "strides": [N * 4], "box": [EPI_COLS, BM],
+                       "swizzle": 128}],
             "flags": [{"sym": "emmy_plan", "value": PLAN_MAGIC}],
             "flops": 2 * M * N * K, "tile": [BM, BN, BK], "stages": STAGES,
             "split_k": plan.slices,
@@ -492,7 +500,7 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     k(f"add.u32 {ring}, {ring}, 1023")
     k(f"and.b32 {ring}, {ring}, -1024")
     tmaps = {}
-    for t in ("ahi", "alo", "bhi", "blo"):
+    for t in ("ahi", "alo", "bhi", "blo", "c"):
         r = k.reg("u64")
         k(f"mov.u64 {r}, tmap_{t}")
         k(f"cvta.global.u64 {r}, {r}")
@@ -664,6 +672,21 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     acc_e, u4 = k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {acc_e}, 0")
     k(f"mov.u32 {u4}, {cta}")
+    is_iss = k.reg("pred")
+    k(f"setp.eq.u32 {is_iss}, {tid}, {EPI_ISSUER}")
+    ec, epi_base = k.reg("u32"), k.reg("u32")
+    k(f"mov.u32 {ec}, 0")
+    k(f"add.u32 {epi_base}, {ring}, {STAGES * stage_bytes}")
+    # this thread's row in a staging buffer: 16-byte chunk j at j ^ (row % 8)
+    swz_off = []
+    r7 = k.reg("u32")
+    k(f"and.b32 {r7}, {rowq}, 7")
+    for j in range(EPI_COLS // 4):
+        o = k.reg("u32")
+        k(f"xor.b32 {o}, {r7}, {j}")
+        k(f"shl.b32 {o}, {o}, 4")
+        k(f"mad.lo.u32 {o}, {rowq}, {EPI_COLS * 4}, {o}")
+        swz_off.append(o)
     el, ee = k.label("e_unit"), k.label("e_unitend")
     k.place(el)
     k(f"setp.ge.u32 {p}, {u4}, {units}")
@@ -676,26 +699,46 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     cx.wait(bar("bar_tfull", a4), aph4, abort_l)
     k("bar.warp.sync -1")
     k("tcgen05.fence::after_thread_sync")
-    row, col0, rbase = k.reg("u32"), k.reg("u32"), k.reg("u32")
-    k(f"mad.lo.u32 {row}, {tm4}, {BM}, {rowq}")
+    col0 = k.reg("u32")
     k(f"mul.lo.u32 {col0}, {tn4}, {BN}")
-    k(f"mad.lo.u32 {rbase}, {row}, {N}, {col0}")
-    cptr = k.reg("u64")
-    k(f"mad.wide.u32 {cptr}, {rbase}, 4, {C}")
     tbase = k.reg("u32")
     k(f"mad.lo.u32 {tbase}, {a4}, {BN}, {tmem}")
     k(f"add.u32 {tbase}, {tbase}, {lane_off}")
-    for c in range(BN // 16):
-        regs = k.regs("f32", 16)
+    row0 = k.reg("u32")
+    k(f"mul.lo.u32 {row0}, {tm4}, {BM}")
+    # C leaves through shared memory: per 32 columns every thread writes its
+    # accumulator row (128 bytes, 128-byte swizzle) into one of two staging
+    # buffers and one thread issues a TMA tensor store of the 128 x 32 box
+    # (a TMA reduce-add for split-K), so C is written in whole lines instead
+    # of one 16-byte piece per row per store
+    for c in range(BN // EPI_COLS):
+        regs = k.regs("f32", EPI_COLS)
         tad = k.reg("u32")
-        k(f"add.u32 {tad}, {tbase}, {c * 16}")
-        k(f"tcgen05.ld.sync.aligned.32x32b.x16.b32 {{{', '.join(regs)}}}, [{tad}]")
+        k(f"add.u32 {tad}, {tbase}, {c * EPI_COLS}")
+        k(f"tcgen05.ld.sync.aligned.32x32b.x{EPI_COLS}.b32 {{{', '.join(regs)}}}, [{tad}]")
         k("tcgen05.wait::ld.sync.aligned")
-        for v in range(4):
-            vals = ", ".join(regs[4 * v:4 * v + 4])
-            off = (c * 16 + 4 * v) * 4
-            op = "red.global.add.v4.f32" if plan.atomic else "st.global.v4.f32"
-            k(f"{op} [{cptr}+{off}], {{{vals}}}")
+        # the buffer is free once the store that used it two chunks ago read it
+        k(f"@{is_iss} cp.async.bulk.wait_group.read 1")
+        k(f"bar.sync 1, {EPI_THREADS}")
+        sbuf = k.reg("u32")
+        k(f"and.b32 {sbuf}, {ec}, 1")
+        k(f"mad.lo.u32 {sbuf}, {sbuf}, {EPI_BUF}, {epi_base}")
+        for j in range(EPI_COLS // 4):
+            sa = k.reg("u32")
+            k(f"add.u32 {sa}, {sbuf}, {swz_off[j]}")
+            k(f"st.shared.v4.f32 [{sa}], {{{', '.join(regs[4 * j:4 * j + 4])}}}")
+        k("fence.proxy.async.shared::cta")
+        k(f"bar.sync 1, {EPI_THREADS}")
+        cc = k.reg("u32")
+        k(f"add.u32 {cc}, {col0}, {c * EPI_COLS}")
+        if plan.atomic:
+            k(f"@{is_iss} cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group "
+              f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
+        else:
+            k(f"@{is_iss} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group "
+              f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
+        k(f"@{is_iss} cp.async.bulk.commit_group")
+        k(f"add.u32 {ec}, {ec}, 1")
     k("tcgen05.fence::before_thread_sync")
     teb = bar("bar_tempty", a4)
     k(f"mbarrier.arrive.shared::cta.b64 _, [{teb}]")
@@ -709,6 +752,12 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     k.place(abort_l)
     k("st.volatile.shared.u32 [abort_flag], 1")
     k.place(teardown)
+    # the C store issuer: every TMA store it issued has completed
+    k(f"setp.ne.u32 {q}, {tid}, {EPI_ISSUER}")
+    nw = k.label("nostorewait")
+    k(f"@{q} bra {nw}")
+    k("cp.async.bulk.wait_group 0")
+    k.place(nw)
     k("barrier.sync 0")
     ab = k.reg("u32")
     k(f"ld.volatile.shared.u32 {ab}, [abort_flag]")
