@@ -708,9 +708,11 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     k(f"mul.lo.u32 {row0}, {tm4}, {BM}")
     # C leaves through shared memory: per 32 columns every thread writes its
     # accumulator row (128 bytes, 128-byte swizzle) into one of two staging
-    # buffers and one thread issues a TMA tensor store of the 128 x 32 box
-    # (a TMA reduce-add for split-K), so C is written in whole lines instead
-    # of one 16-byte piece per row per store
+    # buffers and one thread issues a TMA tensor store of the 128 x 32 box,
+    # so C is written in whole lines instead of one 16-byte piece per row per
+    # store.  Split-K IR adds into a zeroed C: a TMA reduce-add while several
+    # CTAs share a tile, a plain store once each tile's K slices are all
+    # accumulated in one CTA (0 + x == x; only a -0.0 sum keeps its sign)
     for c in range(BN // EPI_COLS):
         regs = k.regs("f32", EPI_COLS)
         tad = k.reg("u32")
@@ -731,7 +733,7 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
         k(f"bar.sync 1, {EPI_THREADS}")
         cc = k.reg("u32")
         k(f"add.u32 {cc}, {col0}, {c * EPI_COLS}")
-        if plan.atomic:
+        if plan.atomic and plan.slices > 1:
             k(f"@{is_iss} cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group "
               f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
         else:
