@@ -56,6 +56,7 @@ XCH_STATIC = 4096            # static shared memory of the two-threads-per-row f
 W_QK, W_PV = 0, 1           # S = Q.K^T issuer, O += P.V^T issuer (and TMEM owner)
 BQ = 128
 RESCALE_T = 8.0
+SPLIT_O_DEFAULT = True
 
 
 class AttnPlan:
@@ -149,6 +150,11 @@ def _idesc(kind: str, m: int, n: int) -> int:
     return (1 << 4) | (fmt << 7) | (fmt << 10) | ((n >> 3) << 17) | ((m >> 4) << 24)
 
 
+def _split_o_on() -> bool:
+    v = os.environ.get("EMMY_ATTN_SPLIT_O")
+    return SPLIT_O_DEFAULT if v is None else v not in ("0", "")
+
+
 def _layout(plan):
     """Shared-memory regions (bytes) of one unit: Q (resident), ``kvst``
     stages of the K block and the V^T block, and P; each ``halves`` deep
@@ -188,6 +194,12 @@ def _layout(plan):
     # fit beside the dynamic layout, else one (warps 2-5)
     split = 2 if off + 1024 + XCH_STATIC <= SMEM_MAX else 1
     lay["split"] = split
+    # split O (bf16): the row's two threads keep their own running max and
+    # sum over their half of each key block and accumulate into their own O
+    # (O_A: keys [0, BKV/2), O_B: the rest), merged once in the epilogue --
+    # no per-block exchange of partial maxima.  TMEM: 2 S + 2 O columns.
+    lay["split_o"] = (plan.dtype != "f32" and split == 2 and bkv // atom == 2
+                      and 2 * s_cols + 2 * d <= 512 and _split_o_on())
     # warps 0-1 MMA issue, 2 .. 1+4*split softmax, then one TMA warp
     lay["threads"] = 96 + 128 * split
     lay["w_prod"] = 2 + 4 * split
@@ -665,9 +677,10 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     # buffer holds BKV f32 score columns; for f32 also the Q_hi.K_lo partial
     # beside them, later overwritten by P hi and P lo.
     q_tmem = lay["q_tmem"]
+    split_o = lay["split_o"]
     s_cols = lay["s_cols"]
     o_col = 2 * s_cols
-    q_col = o_col + D
+    q_col = o_col + (2 * D if split_o else D)     # split O: O_A then O_B
     tcols = 1 << (q_col + (2 * D if q_tmem else 0) - 1).bit_length()
     assert tcols <= 512
     warp, lane = k.reg("u32"), k.reg("u32")
@@ -937,6 +950,14 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
             k(f"mad.lo.u32 {pb}, {pb}, {s_cols}, {tmem}")
             first = True
             for c in range(max(1, BKV // atom)):
+                if split_o:
+                    # key chunk c (the half written by softmax threads of half c)
+                    # accumulates into O_c, started afresh at the unit's first block
+                    first = True
+                    o_acc = k.reg("u32")
+                    k(f"add.u32 {o_acc}, {o_t}, {c * D}")
+                else:
+                    o_acc = o_t
                 for kk in range(min(4, BKV * e // 32)):
                     for (ha, hb) in pairs:
                         # A (P) from TMEM: a 32-byte K-step is 8 columns (16 packed
@@ -947,7 +968,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
                         b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
                         acc = firstb if first else yes
                         first = False
-                        k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{o_t}], {a_}, {b_}, {id_o}, {acc}")
+                        k(f"@{pm} tcgen05.mma.cta_group::1.kind::{kind} [{o_acc}], {a_}, {b_}, {id_o}, {acc}")
             k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [bar_pv_done]")
             k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bar_at('v_empty', st_)}]")
@@ -1002,15 +1023,19 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
 
     # ================= softmax / correction / epilogue: warps 2-9 =================
     # Two threads per query row: warps 2-5 take the first half of the key
-    # block's columns (and of O's), warps 6-9 the second half.  A warp may only
-    # touch TMEM lanes 32 * (warp % 4) .. +31, so both warps of a row pair sit
-    # on the same lane quarter; they swap partial row maxima through shared
-    # memory under a 64-thread named barrier (id 1 + quarter), the running
-    # sums stay per thread and are added once, in the epilogue.
+    # block's columns, warps 6-9 the second half.  A warp may only touch TMEM
+    # lanes 32 * (warp % 4) .. +31, so both warps of a row pair sit on the
+    # same lane quarter.  Split O (bf16): each thread keeps its own running
+    # max m_h and sum l_h over its half of the keys and its own accumulator
+    # O_h; once per unit the pair swaps (m, l) under a 64-thread named
+    # barrier (id 1 + quarter) and each writes half of the output columns of
+    #   (O_A 2^(m_A - m) + O_B 2^(m_B - m)) / (l_A 2^(m_A - m) + l_B 2^(m_B - m)).
+    # Otherwise the pair swaps partial row maxima every block and shares one
+    # O (each thread owning half of its columns); the sums are added once.
     k.place(role_sm)
     if split == 2:
         k.shared("\t.shared .align 16 .f32 xch_max[512];")    # [parity][half][row]
-        k.shared("\t.shared .align 16 .f32 xch_sum[256];")    # [half][row]
+        k.shared(f"\t.shared .align 16 .f32 xch_sum[{512 if split_o else 256}];")
     quad, row, half = k.reg("u32"), k.reg("u32"), k.reg("u32")
     k(f"and.b32 {quad}, {warp}, 3")
     k(f"mad.lo.u32 {row}, {quad}, 32, {lane}")
@@ -1027,6 +1052,14 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"add.u32 {o_row}, {tmem}, {lane_off}")
     k(f"add.u32 {o_row}, {o_row}, {o_col}")
     k(f"mad.lo.u32 {o_row}, {half}, {ho}, {o_row}")
+    if split_o:
+        # the O rescale covers this thread's own accumulator, all D columns
+        o_resc, resc_cols = k.reg("u32"), D
+        k(f"add.u32 {o_resc}, {tmem}, {lane_off}")
+        k(f"add.u32 {o_resc}, {o_resc}, {o_col}")
+        k(f"mad.lo.u32 {o_resc}, {half}, {D}, {o_resc}")
+    else:
+        o_resc, resc_cols = o_row, ho
     if split == 2:
         # exchange slots: mine and my partner's (same row, other half)
         x_me, x_pa = k.reg("u32"), k.reg("u32")
@@ -1135,7 +1168,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         k(f"max.f32 {mb}, {mb}, {mx[i]}")
     # swap partial maxima with the partner thread (slots double-buffered by
     # block parity, so a slot is rewritten only after the partner read it)
-    if split == 2:
+    if split == 2 and not split_o:
         xo = k.reg("u32")
         k(f"mul.lo.u32 {xo}, {sb}, 1024")
         xa, xb = k.reg("u32"), k.reg("u32")
@@ -1240,11 +1273,11 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"and.b32 {php}, {php}, 1")
     cx.wait("bar_pv_done", php, abort_l)
     k("tcgen05.fence::after_thread_sync")
-    for c0 in range(0, ho, 32):
-        cnt = min(32, ho - c0)
+    for c0 in range(0, resc_cols, 32):
+        cnt = min(32, resc_cols - c0)
         ov = k.regs("f32", cnt)
         tad = k.reg("u32")
-        k(f"add.u32 {tad}, {o_row}, {c0}")
+        k(f"add.u32 {tad}, {o_resc}, {c0}")
         k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
         k("tcgen05.wait::ld.sync.aligned")
         for t in range(cnt):
@@ -1260,7 +1293,45 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k(f"@{p} bra {sj}")
     # epilogue: the two partial sums, last P . V done, out = O * (1/l)
     lo_sum = k.reg("f32")
-    if split == 2:
+    if split_o:
+        # swap (m, l) with the partner (slots double-buffered by unit parity)
+        xoff, xq = k.reg("u32"), k.reg("u32")
+        k(f"and.b32 {xoff}, {uit3}, 1")
+        k(f"mul.lo.u32 {xoff}, {xoff}, 1024")
+        k(f"mad.lo.u32 {xoff}, {row}, 4, {xoff}")
+        k(f"xor.b32 {xq}, {half}, 1")
+        am, al, bm, bl = (k.reg("u32") for _ in range(4))
+        k(f"mov.u32 {am}, xch_max")
+        k(f"mov.u32 {al}, xch_sum")
+        k(f"add.u32 {am}, {am}, {xoff}")
+        k(f"add.u32 {al}, {al}, {xoff}")
+        k(f"mad.lo.u32 {bm}, {xq}, 512, {am}")
+        k(f"mad.lo.u32 {bl}, {xq}, 512, {al}")
+        k(f"mad.lo.u32 {am}, {half}, 512, {am}")
+        k(f"mad.lo.u32 {al}, {half}, 512, {al}")
+        k(f"st.shared.f32 [{am}], {m_run}")
+        k(f"st.shared.f32 [{al}], {l_run}")
+        k(f"barrier.sync {bar_id}, 64")
+        mo, lo2 = k.reg("f32"), k.reg("f32")
+        k(f"ld.shared.f32 {mo}, [{bm}]")
+        k(f"ld.shared.f32 {lo2}, [{bl}]")
+        # half A's numbers first on both threads, so both compute the same
+        is1 = k.reg("pred")
+        k(f"setp.ne.u32 {is1}, {half}, 0")
+        m0, m1, l0, l1 = (k.reg("f32") for _ in range(4))
+        k(f"selp.f32 {m0}, {mo}, {m_run}, {is1}")
+        k(f"selp.f32 {m1}, {m_run}, {mo}, {is1}")
+        k(f"selp.f32 {l0}, {lo2}, {l_run}, {is1}")
+        k(f"selp.f32 {l1}, {l_run}, {lo2}, {is1}")
+        mm, a0, a1 = k.reg("f32"), k.reg("f32"), k.reg("f32")
+        k(f"max.f32 {mm}, {m0}, {m1}")
+        k(f"sub.rn.f32 {a0}, {m0}, {mm}")
+        k(f"sub.rn.f32 {a1}, {m1}, {mm}")
+        k(f"ex2.approx.ftz.f32 {a0}, {a0}")
+        k(f"ex2.approx.ftz.f32 {a1}, {a1}")
+        k(f"mul.rn.f32 {lo_sum}, {l0}, {a0}")
+        k(f"fma.rn.f32 {lo_sum}, {l1}, {a1}, {lo_sum}")
+    elif split == 2:
         xs, xp = k.reg("u32"), k.reg("u32")
         k(f"mov.u32 {xs}, xch_sum")
         k(f"mad.lo.u32 {xs}, {row}, 4, {xs}")
@@ -1281,6 +1352,10 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
     k("tcgen05.fence::after_thread_sync")
     rl = k.reg("f32")
     k(f"rcp.rn.f32 {rl}, {lo_sum}")
+    if split_o:
+        w0, w1 = k.reg("f32"), k.reg("f32")
+        k(f"mul.rn.f32 {w0}, {a0}, {rl}")
+        k(f"mul.rn.f32 {w1}, {a1}, {rl}")
     bh3, qb3 = unit_coords(u3)
     grow = k.reg("u32")
     k(f"mad.lo.u32 {grow}, {bh3}, {S}, {row}")
@@ -1294,9 +1369,18 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         tad = k.reg("u32")
         k(f"add.u32 {tad}, {o_row}, {c0}")
         k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ov)}}}, [{tad}]")
+        if split_o:
+            ob = k.regs("f32", cnt)
+            tb = k.reg("u32")
+            k(f"add.u32 {tb}, {tad}, {D}")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x{cnt}.b32 {{{', '.join(ob)}}}, [{tb}]")
         k("tcgen05.wait::ld.sync.aligned")
         for t in range(cnt):
-            k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {rl}")
+            if split_o:
+                k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {w0}")
+                k(f"fma.rn.f32 {ov[t]}, {ob[t]}, {w1}, {ov[t]}")
+            else:
+                k(f"mul.rn.f32 {ov[t]}, {ov[t]}, {rl}")
         if f32:
             for v in range(cnt // 4):
                 k(f"st.global.v4.f32 [{optr}+{(c0 + 4 * v) * 4}], {{{', '.join(ov[4 * v:4 * v + 4])}}}")

@@ -93,6 +93,18 @@ def test_rescale_path(dtype):
     assert np.abs(out - ref).max() <= tol * np.abs(ref).max()
 
 
+def test_bf16_shared_o(monkeypatch):
+    """The bf16 form with one shared O and a per-block max exchange between
+    a row's two threads (split O off) stays correct."""
+    monkeypatch.setenv("EMMY_ATTN_SPLIT_O", "0")
+    b, h, s, d = 2, 2, 512, 128
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "atto")
+    q, k, v = _bhsd(b, h, s, d, "bf16", seed=9)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
+    ref = _ref(q, k, v)
+    assert np.abs(out - ref).max() <= 2e-2 * np.abs(ref).max()
+
+
 @pytest.mark.parametrize("share", [0, 4])
 def test_bf16_polynomial_exp2(share, monkeypatch):
     """bf16 P with none or all of exp2 on the FMA-pipe polynomial (the
