@@ -590,9 +590,10 @@ def _emit_simt(k: Kernel, spec, plan, base, tid, ntid, cta, ncta):
 EXP2_POLY = (0.9999280571937561, 0.6932609677314758, 0.2426111251115799,
              0.0551716685295105)
 # pairs out of every four on the polynomial, measured on B200 for bf16
-# [16,32,4096,128] (two passes each): 0 -> 4.40-4.43 ms, 1 -> 4.39,
-# 2 -> 4.33, 3 -> 4.79-4.84, 4 -> 5.15-5.21
-EXP_POLY_DEFAULT = 2
+# [16,32,4096,128] with split O (two passes each): 1 -> 4.09-4.15 ms,
+# 2 -> 4.21-4.37, 3 -> 4.42-4.70 (one shared O: 0 -> 4.40-4.43, 1 -> 4.39,
+# 2 -> 4.33, 3 -> 4.79-4.84, 4 -> 5.15-5.21)
+EXP_POLY_DEFAULT = 1
 
 
 def _exp_poly_share() -> int:

@@ -108,7 +108,7 @@ def test_bf16_shared_o(monkeypatch):
 @pytest.mark.parametrize("share", [0, 4])
 def test_bf16_polynomial_exp2(share, monkeypatch):
     """bf16 P with none or all of exp2 on the FMA-pipe polynomial (the
-    default, two pairs of every four, runs in every other bf16 test)."""
+    default, one pair of every four, runs in every other bf16 test)."""
     monkeypatch.setenv("EMMY_ATTN_EXP_POLY", str(share))
     b, h, s, d = 2, 2, 512, 128
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "attp")
