@@ -445,7 +445,14 @@ class PreparedKernel:
             self.launches += 1
 
     def launch_main(self, stream=None) -> None:
+        # zero_outputs are cleared before every launch, except outputs the
+        # plan's kernel writes in full without reading them (``overwrites``:
+        # e.g. split-K whose slices one CTA accumulates before a plain store,
+        # where 0 + x == x); under meta.json's geometry they are always cleared
+        skip = set(self.plan.get("overwrites", [])) if self.geometry != "meta" else set()
         for name in self.spec.zero_outputs:
+            if name in skip:
+                continue
             a = self.spec.args[name]
             self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4, stream)
         ptrs = [self.bufs[n] for n in self.spec.arg_order]

@@ -326,6 +326,10 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
             "flops": 2 * M * N * K, "tile": [BM, BN, BK], "stages": STAGES,
             "split_k": plan.slices,
         })
+        if plan.slices == 1:
+            # every C element is written once by a plain TMA store: C needs
+            # no clearing before a launch even when the IR adds into it
+            plan_d["overwrites"] = [plan.c]
     mod.plan = plan_d
     return mod
 

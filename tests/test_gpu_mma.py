@@ -89,6 +89,34 @@ def test_splitk_generated():
     assert ok, rel
 
 
+@pytest.mark.parametrize("mnk", [(4096, 4096, 512), (256, 256, 1024)])
+def test_splitk_repeated_launches(mnk):
+    """Split-K IR adds into a C cleared before every launch.  With the slices
+    grouped into one CTA per tile (4096x4096x512) the kernel stores C in full
+    and the launcher skips the clearing (plan ``overwrites``); with slices
+    spread over CTAs (256x256x1024) it clears C and the kernel reduce-adds.
+    Three launches on the same buffers must each give A.B, not a sum."""
+    from ptxgen.runtime import PreparedKernel
+    m, n, k = mnk
+    spec = load_kernel_data(*irgen.matmul_splitk(m, n, k, slice_k=128), "skr")
+    rng = np.random.default_rng(4)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    pk = PreparedKernel(spec)
+    try:
+        assert ("overwrites" in pk.plan) == (m == 4096)
+        pk.upload({"x0": a, "x1": b})
+        for _ in range(3):
+            pk.launch()
+        pk.check_errors()
+        got = pk.download()["matmul"]
+    finally:
+        pk.close()
+    rows = np.random.default_rng(5).choice(m, min(m, 64), replace=False)
+    ok, rel = _bound_ok(got, a, b, rows)
+    assert ok, rel
+
+
 @pytest.mark.parametrize("shape", ["square", "splitk8"])
 def test_baseline_shapes_sampled(shape):
     if shape == "square":

@@ -61,3 +61,16 @@ def test_splitk_groups_slices_per_cta():
     small = load_kernel_data(*irgen.matmul_splitk(256, 128, 256, slice_k=64), "small")
     p = tmpl_mma.match_matmul(small)
     assert p.slices == 4 and p.slice_k == 64                 # 2 tiles: keep the slices
+
+
+def test_splitk_overwrites_only_when_slices_grouped():
+    """A split-K plan lists C under ``overwrites`` (no clearing needed) only
+    when each tile's slices are accumulated by one CTA and stored once."""
+    import json
+    import re
+    from ptxgen.emit import compile_kernel
+    from ptxgen.loader import load_kernel_data
+    for (m, n, k), grouped in (((16384, 4096, 1024), True), ((256, 256, 1024), False)):
+        spec = load_kernel_data(*irgen.matmul_splitk(m, n, k, slice_k=128), "sk")
+        plan = json.loads(re.search(r"// @emmy-plan (\{.*\})", compile_kernel(spec)).group(1))
+        assert (plan.get("overwrites") == ["matmul"]) == grouped, (m, n, k, plan.get("split_k"))
