@@ -542,7 +542,11 @@ class Lowerer:
 
     def seed_accums(self, body, enabled: bool) -> None:
         """Loop-entry seeding of the loop's own accumulators
-        (``interp.py:782-801``)."""
+        (``interp.py:782-801``).  The reference seeds them on every lane, not
+        only the active ones (``interp.py:794`` assigns the identity without
+        the mask), so a loop inside a ``Cond`` resets its accumulator to the
+        identity on lanes that do not take the branch too: the seed is an
+        unpredicated move."""
         seen: set[str] = set()
 
         def visit(stmts):
@@ -554,7 +558,9 @@ class Lowerer:
                     if enabled:
                         kind = value_kind(st.dtype) if st.dtype is not None else "f32"
                         store = storage_kind(st.dtype) if st.dtype is not None else None
+                        saved, self.mask = self.mask, None
                         self.bind(st.name, self.identity(st.op.name, kind, store))
+                        self.mask = saved
                 elif isinstance(st, (ir.Loop, ir.StridedLoop)):
                     continue
                 else:

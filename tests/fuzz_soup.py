@@ -1,0 +1,245 @@
+"""Random statement mixes for the generic lowering (test infrastructure).
+
+``case(seed)`` draws one kernel that is not shaped like any shipped family:
+a ``Tile`` over N cells whose body is a random mix of
+
+* ``Load`` of the cell's element of ``x0``/``x1`` or of a gathered element of
+  a small table ``t`` (index ``(a0 * p + q) % K``, or ``(a0 + j * s) % K``
+  inside a loop over ``j``);
+* ``Let`` of a float literal and ``Assign`` of exactly rounded ops;
+* ``Cond`` with and without an else body, nested up to depth 2, its
+  predicate an integer test of the cell index or a float test of an earlier
+  value -- names first defined inside a branch stay visible after it and
+  hold 0 on the lanes that did not run it (``ptxgen/interp.py:458-468``);
+* ``Select`` chains of two or three branches (``ptxgen/interp.py:960-972``);
+* ``Loop`` over a short axis folding an ``Accum`` (add, max or min) that the
+  loop seeds (``ptxgen/interp.py:803-821``);
+* unconditional and conditional ``Write``s of ``out[a0]`` (the last write a
+  lane performs wins).
+
+Every op is exactly rounded (add, subtract, multiply, max, min, negative,
+absolute, relu, divide by ``|b| + 1``), so the GPU result must equal the
+oracle's bit for bit.  Magnitudes stay below 1e30 by construction (each
+value carries a bound; an op that could exceed it is not drawn).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+from ptxgen import irgen
+from ptxgen.ir import (Accum, Assign, BinaryExpr, Cond, ElementwiseImpl, Let, Literal, Load,
+                       Loop, Select, SelectBranch, Var, Write, datatype)
+from ptxgen.loader import load_kernel_data
+
+F32 = datatype("f32")
+BINARY = ("add", "subtract", "multiply", "maximum", "minimum", "divide")
+UNARY = ("negative", "absolute", "relu")
+
+
+@dataclasses.dataclass
+class Soup:
+    name: str
+    spec: object
+    inputs: dict
+    graph: dict
+    meta: dict
+
+
+def _lit_i(v):
+    return Literal(value=int(v), dtype="int")
+
+
+def _lit_f(v):
+    return Literal(value=float(v), dtype="float")
+
+
+def _b(op, a, b):
+    return BinaryExpr(op=op, left=a, right=b)
+
+
+class _Gen:
+    def __init__(self, rng, n, k):
+        self.rng, self.n, self.k = rng, n, k
+        self.count = 0
+        self.bound: dict[str, float] = {}      # name -> magnitude bound
+
+    def fresh(self, prefix="v"):
+        self.count += 1
+        return f"{prefix}{self.count}"
+
+    def int_pred(self):
+        r = self.rng.random()
+        a0 = Var(name="a0")
+        if r < 0.4:
+            m = int(self.rng.integers(2, 9))
+            return _b("==", _b("%", a0, _lit_i(m)), _lit_i(int(self.rng.integers(0, m))))
+        if r < 0.7:
+            return _b("<", a0, _lit_i(int(self.rng.integers(0, self.n + 1))))
+        m = int(self.rng.integers(2, 9))
+        return _b("<", _b("%", a0, _lit_i(m)), _lit_i(int(self.rng.integers(1, m))))
+
+    def pred(self, scope):
+        if scope and self.rng.random() < 0.4:
+            v = str(self.rng.choice(scope))
+            return _b("<", Var(name=v), _lit_f(float(np.float32(self.rng.uniform(-1, 1)))))
+        return self.int_pred()
+
+    def pick(self, scope):
+        return str(self.rng.choice(scope))
+
+    def assign(self, scope, out):
+        for _ in range(20):
+            if self.rng.random() < 0.7 and len(scope) >= 1:
+                op = str(self.rng.choice(BINARY))
+                a, b = self.pick(scope), self.pick(scope)
+                ba, bb = self.bound[a], self.bound[b]
+                if op == "divide":
+                    bnd = ba                          # a / (|b| + 1)
+                elif op == "multiply":
+                    bnd = ba * bb
+                elif op in ("add", "subtract"):
+                    bnd = ba + bb
+                else:
+                    bnd = max(ba, bb)
+                if bnd >= 1e30:
+                    continue
+                if op == "divide":
+                    d, e = self.fresh("d"), self.fresh("e")
+                    one = self.fresh("one")
+                    out.append(Assign(name=d, op=ElementwiseImpl("absolute"), args=(b,), dtype=F32))
+                    out.append(Let(name=one, value=_lit_f(1.0), dtype=F32))
+                    out.append(Assign(name=e, op=ElementwiseImpl("add"), args=(d, one), dtype=F32))
+                    b = e
+                name = self.fresh()
+                out.append(Assign(name=name, op=ElementwiseImpl(op), args=(a, b), dtype=F32))
+            else:
+                op = str(self.rng.choice(UNARY))
+                a = self.pick(scope)
+                bnd = self.bound[a]
+                name = self.fresh()
+                out.append(Assign(name=name, op=ElementwiseImpl(op), args=(a,), dtype=F32))
+            self.bound[name] = bnd
+            scope.append(name)
+            return
+        # nothing fitted: a plain negation keeps the mix going
+        a = self.pick(scope)
+        name = self.fresh()
+        out.append(Assign(name=name, op=ElementwiseImpl("negative"), args=(a,), dtype=F32))
+        self.bound[name] = self.bound[a]
+        scope.append(name)
+
+    def load(self, scope, out, index=None):
+        name = self.fresh("in")
+        if index is not None:
+            out.append(Load(names=(name,), input="t", index=(index,), dtype=F32))
+        elif self.rng.random() < 0.7:
+            buf = str(self.rng.choice(["x0", "x1"]))
+            out.append(Load(names=(name,), input=buf, index=(Var(name="a0"),), dtype=F32))
+        else:
+            p, q = int(self.rng.integers(1, 7)), int(self.rng.integers(0, 7))
+            idx = _b("%", _b("+", _b("*", Var(name="a0"), _lit_i(p)), _lit_i(q)), _lit_i(self.k))
+            out.append(Load(names=(name,), input="t", index=(idx,), dtype=F32))
+        self.bound[name] = 6.0
+        scope.append(name)
+
+    def block(self, scope, depth, nstmts):
+        out = []
+        for _ in range(nstmts):
+            r = self.rng.random()
+            if r < 0.18 or not scope:
+                self.load(scope, out)
+            elif r < 0.45:
+                self.assign(scope, out)
+            elif r < 0.50:
+                name = self.fresh("c")
+                v = float(np.float32(self.rng.uniform(-2, 2)))
+                out.append(Let(name=name, value=_lit_f(v), dtype=F32))
+                self.bound[name] = abs(v)
+                scope.append(name)
+            elif r < 0.64 and depth < 2:
+                pred = self.pred(scope)
+                inner = list(scope)
+                body = self.block(inner, depth + 1, int(self.rng.integers(1, 4)))
+                else_body = ()
+                inner2 = list(scope)
+                if self.rng.random() < 0.5:
+                    else_body = tuple(self.block(inner2, depth + 1, int(self.rng.integers(1, 4))))
+                out.append(Cond(cond=pred, body=tuple(body), else_body=else_body))
+                # names defined in a branch stay visible (0 where it did not run)
+                for nm in inner + inner2:
+                    if nm not in scope:
+                        scope.append(nm)
+            elif r < 0.74 and len(scope) >= 2:
+                nb = int(self.rng.integers(2, 4))
+                vals = [self.pick(scope) for _ in range(nb)]
+                branches = [SelectBranch(value=v, select=self.pred(scope)) for v in vals[:-1]]
+                branches.append(SelectBranch(value=vals[-1], select=None))
+                name = self.fresh("s")
+                out.append(Select(name=name, branches=tuple(branches)))
+                self.bound[name] = max(self.bound[v] for v in vals)
+                scope.append(name)
+            elif r < 0.84 and depth < 2 and scope:
+                ext = int(self.rng.integers(1, 7))
+                ax = self.fresh("j")
+                s_ = int(self.rng.integers(1, 5))
+                idx = _b("%", _b("+", Var(name="a0"), _b("*", Var(name=ax), _lit_i(s_))),
+                         _lit_i(self.k))
+                body, inner = [], list(scope)
+                self.load(inner, body, index=idx)
+                loaded = inner[-1]
+                other = self.pick(scope)
+                op = str(self.rng.choice(["add", "multiply", "maximum"]))
+                t = self.fresh("t")
+                bt = (self.bound[loaded] * self.bound[other] if op == "multiply"
+                      else self.bound[loaded] + self.bound[other])
+                if bt * ext >= 1e30:
+                    op, bt = "maximum", max(self.bound[loaded], self.bound[other])
+                body.append(Assign(name=t, op=ElementwiseImpl(op), args=(loaded, other), dtype=F32))
+                aop = str(self.rng.choice(["add", "maximum", "minimum"]))
+                acc = self.fresh("acc")
+                body.append(Accum(name=acc, value=t, op=ElementwiseImpl(aop), dtype=F32,
+                                  axes=(ax,), base=None))
+                out.append(Loop(axis=irgen.ax(ax, ext), body=tuple(body), unroll=False, seed=True))
+                # the loop runs 1..6 times: a max/min fold is one of its
+                # values, a sum at most ext of them (lanes that skip the loop
+                # under a Cond hold 0)
+                self.bound[acc] = bt * ext if aop == "add" else bt
+                scope.append(acc)
+            else:
+                if scope:
+                    v = self.pick(scope)
+                    if depth == 0 or self.rng.random() < 0.5:
+                        out.append(Write(output="out", index=(Var(name="a0"),), values=(v,),
+                                         value_dtype=F32, atomic=False, swizzle="NONE"))
+                    else:
+                        out.append(Cond(cond=self.pred(scope), body=(
+                            Write(output="out", index=(Var(name="a0"),), values=(v,),
+                                  value_dtype=F32, atomic=False, swizzle="NONE"),), else_body=()))
+        return out
+
+
+def case(seed: int) -> Soup:
+    rng = np.random.default_rng(77_000 + seed)
+    n = int(rng.integers(1, 5000))
+    k = int(rng.integers(1, 65))
+    block = int(rng.choice([32, 64, 128, 256]))
+    g = _Gen(rng, n, k)
+    scope: list[str] = []
+    body = g.block(scope, 0, int(rng.integers(4, 14)))
+    # every lane writes at least once, at the end
+    body.append(Write(output="out", index=(Var(name="a0"),), values=(scope[-1],),
+                      value_dtype=F32, atomic=False, swizzle="NONE"))
+    t = irgen.tile([irgen.ax("a0", n)], body)
+    inputs = [("t", (k,), "f32", 2), ("x0", (n,), "f32", 0), ("x1", (n,), "f32", 1)]
+    graph, meta = irgen.package("k_soup", "out", [t], inputs, [], ("out", (n,), "f32"),
+                                ["x0", "x1", "t", "out"], (math.ceil(n / block), 1, 1),
+                                (block, 1, 1), rtol=0.0, atol=0.0, pid=f"soup{seed}")
+    spec = load_kernel_data(graph, meta, f"soup{seed}")
+    ins = {"x0": rng.standard_normal(n).astype(np.float32),
+           "x1": rng.standard_normal(n).astype(np.float32),
+           "t": rng.standard_normal(k).astype(np.float32)}
+    return Soup(f"soup{seed}", spec, ins, graph, meta)

@@ -9,7 +9,8 @@ Run in a container where the reference checkout exists (default
   results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
 * ``ref_interp/<case>.npz``: outputs of the reference's golden model
   ``ptxgen/interp.py`` run here on extra inputs (every problem reseeded, plus
-  IR that ``ptxgen.irgen`` generates at other shapes).  The reference
+  IR that ``ptxgen.irgen`` generates at other shapes, plus random statement
+  mixes from ``tests/fuzz_soup.py``).  The reference
   interpreter is imported from the checkout and fed IR objects built by this
   repository's own deserialiser, which stands in for the absent ``emmy-ml``
   package.  Inputs are not stored: ``cases.json`` records how to rebuild them.
@@ -107,6 +108,9 @@ def rebuild_inputs(spec, seed_offset: int, dist: str) -> dict[str, np.ndarray]:
     return out
 
 
+SOUP_CASES = 24
+
+
 def generated_cases():
     """Extra IR at other shapes, produced by ``ptxgen.irgen``."""
     from ptxgen import irgen
@@ -165,6 +169,19 @@ def main() -> int:
         np.savez_compressed(odst / f"{name}.npz", **{n: np.asarray(v) for n, v in outs.items()})
         cases.append({"case": name, "ir": f"generated/{name}.ir.json",
                       "meta": f"generated/{name}.meta.json", "seed_offset": off, "dist": dist})
+    # random statement mixes (Cond/Select/Loop/Let/Accum, tests/fuzz_soup.py)
+    from tests import fuzz_soup
+    for seed in range(SOUP_CASES):
+        c = fuzz_soup.case(seed)
+        name = f"soup_{seed:02d}"
+        gdir = HERE / "generated"
+        (gdir / f"{name}.ir.json").write_text(json.dumps(c.graph, indent=1) + "\n")
+        (gdir / f"{name}.meta.json").write_text(json.dumps(c.meta, indent=1) + "\n")
+        inputs = rebuild_inputs(c.spec, 0, "normal")
+        outs = ref_interp.interpret(c.spec, inputs)
+        np.savez_compressed(odst / f"{name}.npz", **{n: np.asarray(v) for n, v in outs.items()})
+        cases.append({"case": name, "ir": f"generated/{name}.ir.json",
+                      "meta": f"generated/{name}.meta.json", "seed_offset": 0, "dist": "normal"})
     (HERE / "cases.json").write_text(json.dumps(cases, indent=1) + "\n")
     print(f"{len(cases)} reference-interpreter cases written")
     return 0
