@@ -14,13 +14,19 @@ a ``Tile`` over N cells whose body is a random mix of
 * ``Select`` chains of two or three branches (``ptxgen/interp.py:960-972``);
 * ``Loop`` over a short axis folding an ``Accum`` (add, max or min) that the
   loop seeds (``ptxgen/interp.py:803-821``);
+* integer values: ``Let`` of an int literal or of an index expression of
+  the cell, ``Assign`` of s32 add, subtract, multiply, max, min, divide (by
+  zero gives 0), remainder, bit and/or/xor and shifts (count masked to 5
+  bits) -- ``ptxgen/interp.py:180-200``, ``:359-373`` -- integer
+  predicates, and integers mixed into float ops (promoted to f32);
 * unconditional and conditional ``Write``s of ``out[a0]`` (the last write a
   lane performs wins).
 
 Every op is exactly rounded (add, subtract, multiply, max, min, negative,
-absolute, relu, divide by ``|b| + 1``), so the GPU result must equal the
-oracle's bit for bit.  Magnitudes stay below 1e30 by construction (each
-value carries a bound; an op that could exceed it is not drawn).
+absolute, relu, divide by ``|b| + 1``, and the integer ops), so the GPU
+result must equal the oracle's bit for bit.  Float magnitudes stay below
+1e30 and integer ones below 2^30 by construction (each value carries a
+bound; an op that could exceed it is not drawn), so nothing overflows.
 """
 
 from __future__ import annotations
@@ -38,6 +44,9 @@ from ptxgen.loader import load_kernel_data
 F32 = datatype("f32")
 BINARY = ("add", "subtract", "multiply", "maximum", "minimum", "divide")
 UNARY = ("negative", "absolute", "relu")
+INT_BINARY = ("add", "subtract", "multiply", "maximum", "minimum", "divide", "remainder",
+              "bitand", "bitor", "bitxor", "shl", "shr")
+INT_LIMIT = float(1 << 30)
 
 
 @dataclasses.dataclass
@@ -66,6 +75,8 @@ class _Gen:
         self.rng, self.n, self.k = rng, n, k
         self.count = 0
         self.bound: dict[str, float] = {}      # name -> magnitude bound
+        self.ints: set[str] = set()            # names of s32 values
+        self.nonneg: set[str] = set()          # s32 names known to be >= 0
 
     def fresh(self, prefix="v"):
         self.count += 1
@@ -83,10 +94,74 @@ class _Gen:
         return _b("<", _b("%", a0, _lit_i(m)), _lit_i(int(self.rng.integers(1, m))))
 
     def pred(self, scope):
-        if scope and self.rng.random() < 0.4:
+        ints = [v for v in scope if v in self.ints]
+        r = self.rng.random()
+        if ints and r < 0.2:
+            v = str(self.rng.choice(ints))
+            c = int(self.rng.integers(-20, 21))
+            return _b(str(self.rng.choice(["<", "=="])), Var(name=v), _lit_i(c))
+        if scope and r < 0.5:
             v = str(self.rng.choice(scope))
             return _b("<", Var(name=v), _lit_f(float(np.float32(self.rng.uniform(-1, 1)))))
         return self.int_pred()
+
+    def int_let(self, scope, out):
+        name = self.fresh("i")
+        if self.rng.random() < 0.5:
+            v = int(self.rng.integers(-40, 41))
+            out.append(Let(name=name, value=_lit_i(v), dtype=None))
+            self.bound[name] = float(abs(v))
+            nonneg = v >= 0
+        else:
+            p, q = int(self.rng.integers(1, 5)), int(self.rng.integers(-9, 10))
+            m = int(self.rng.integers(2, 17))
+            if self.rng.random() < 0.5:
+                e = _b("+", _b("*", Var(name="a0"), _lit_i(p)), _lit_i(q))
+                self.bound[name] = float(4 * self.n + 10)
+                nonneg = q >= 0
+            else:
+                e = _b("%", Var(name="a0"), _lit_i(m))
+                self.bound[name] = float(m)
+                nonneg = True
+            out.append(Let(name=name, value=e, dtype=None))
+        self.ints.add(name)
+        if nonneg:
+            self.nonneg.add(name)
+        scope.append(name)
+
+    def int_assign(self, scope, out):
+        ints = [v for v in scope if v in self.ints]
+        for _ in range(20):
+            op = str(self.rng.choice(INT_BINARY))
+            a, b = str(self.rng.choice(ints)), str(self.rng.choice(ints))
+            ba, bb = self.bound[a], self.bound[b]
+            na, nb = a in self.nonneg, b in self.nonneg
+            if op in ("shl", "shr"):
+                # the count is masked to 5 bits: only a count known to lie
+                # in [0, 31) keeps the bound
+                if not nb or bb >= 31:
+                    continue
+                bnd = ba * 2.0 ** bb if op == "shl" else ba
+            else:
+                bnd = {"add": ba + bb, "subtract": ba + bb, "multiply": ba * bb,
+                       "maximum": max(ba, bb), "minimum": max(ba, bb), "divide": ba,
+                       "remainder": min(ba, bb) if nb else ba, "bitand": max(ba, bb),
+                       "bitor": 2 * max(ba, bb), "bitxor": 2 * max(ba, bb)}[op]
+            if bnd >= INT_LIMIT:
+                continue
+            name = self.fresh("i")
+            out.append(Assign(name=name, op=ElementwiseImpl(op), args=(a, b), dtype=None))
+            self.bound[name] = bnd
+            self.ints.add(name)
+            nonneg = {"add": na and nb, "multiply": na and nb, "maximum": na or nb,
+                      "minimum": na and nb, "divide": na and nb, "remainder": na,
+                      "bitand": na or nb, "bitor": na and nb, "bitxor": na and nb,
+                      "shl": na, "shr": na}.get(op, False)
+            if nonneg:
+                self.nonneg.add(name)
+            scope.append(name)
+            return
+        self.int_let(scope, out)
 
     def pick(self, scope):
         return str(self.rng.choice(scope))
@@ -150,10 +225,15 @@ class _Gen:
         out = []
         for _ in range(nstmts):
             r = self.rng.random()
-            if r < 0.18 or not scope:
+            if r < 0.16 or not scope:
                 self.load(scope, out)
-            elif r < 0.45:
+            elif r < 0.36:
                 self.assign(scope, out)
+            elif r < 0.46:
+                if not any(v in self.ints for v in scope) or self.rng.random() < 0.3:
+                    self.int_let(scope, out)
+                else:
+                    self.int_assign(scope, out)
             elif r < 0.50:
                 name = self.fresh("c")
                 v = float(np.float32(self.rng.uniform(-2, 2)))
