@@ -13,7 +13,10 @@ a ``Tile`` over N cells whose body is a random mix of
   hold 0 on the lanes that did not run it (``ptxgen/interp.py:458-468``);
 * ``Select`` chains of two or three branches (``ptxgen/interp.py:960-972``);
 * ``Loop`` over a short axis folding an ``Accum`` (add, max or min) that the
-  loop seeds (``ptxgen/interp.py:803-821``);
+  loop seeds (``ptxgen/interp.py:803-821``), and ``StridedLoop``s whose
+  start depends on the cell (``a0 % m``), so each lane runs its own trip
+  count -- none at all when the start is past the extent, which leaves the
+  accumulator at its identity (``ptxgen/interp.py:828-856``);
 * integer values: ``Let`` of an int literal or of an index expression of
   the cell, ``Assign`` of s32 add, subtract, multiply, max, min, divide (by
   zero gives 0), remainder, bit and/or/xor and shifts (count masked to 5
@@ -221,6 +224,32 @@ class _Gen:
         self.bound[name] = 6.0
         scope.append(name)
 
+    def strided(self, scope, out):
+        """A per-lane loop: j = a0 % m, a0 % m + step, ... while j < ext."""
+        ext = int(self.rng.integers(1, 12))
+        m = int(self.rng.integers(1, 5))
+        step = int(self.rng.integers(1, 4))
+        ax = self.fresh("j")
+        idx = _b("%", _b("+", Var(name="a0"), Var(name=ax)), _lit_i(self.k))
+        body, inner = [], list(scope)
+        self.load(inner, body, index=idx)
+        loaded = inner[-1]
+        other = self.pick(scope)
+        bo = self.bound[other]
+        op = "add" if bo + 6.0 < 1e29 else "maximum"
+        t = self.fresh("t")
+        body.append(Assign(name=t, op=ElementwiseImpl(op), args=(loaded, other), dtype=F32))
+        aop = str(self.rng.choice(["add", "maximum", "minimum"]))
+        acc = self.fresh("acc")
+        body.append(Accum(name=acc, value=t, op=ElementwiseImpl(aop), dtype=F32,
+                          axes=(ax,), base=None))
+        out.append(irgen.strided(ax, ext, _b("%", Var(name="a0"), _lit_i(m)), _lit_i(step),
+                                 body))
+        bt = 6.0 + bo
+        # a lane whose start is past ext keeps the identity (+-1e30 for max/min)
+        self.bound[acc] = bt * ext if aop == "add" else max(bt, 1e30)
+        scope.append(acc)
+
     def block(self, scope, depth, nstmts):
         out = []
         for _ in range(nstmts):
@@ -289,6 +318,8 @@ class _Gen:
                 # under a Cond hold 0)
                 self.bound[acc] = bt * ext if aop == "add" else bt
                 scope.append(acc)
+            elif r < 0.90 and depth < 2 and scope:
+                self.strided(scope, out)
             else:
                 if scope:
                     v = self.pick(scope)
