@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures under ``tests/golden/`` from the reference.
 
-Run in a container where the reference checkout exists (default
-``/root/reference``, or ``--ref PATH``).  It writes:
+Run where the reference checkout exists (``--ref PATH``; the default is the
+checkout's location in the build container).  It writes:
 
 * ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
   ``expected.npz`` -- the reference's own golden vectors (numpy float64
