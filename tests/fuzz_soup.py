@@ -22,6 +22,10 @@ a ``Tile`` over N cells whose body is a random mix of
   zero gives 0), remainder, bit and/or/xor and shifts (count masked to 5
   bits) -- ``ptxgen/interp.py:180-200``, ``:359-373`` -- integer
   predicates, and integers mixed into float ops (promoted to f32);
+* shared memory (a seeded 40 % of the cases, every lane active): rounds of
+  ``Write`` of a value to the lane's slot ``a0 % B`` of an ``Smem`` array,
+  ``Sync``, ``Load`` of another lane's slot ``(a0 + s) % B`` -- a barrier
+  also precedes each rewrite, and every slot is written before it is read;
 * unconditional and conditional ``Write``s of ``out[a0]`` (the last write a
   lane performs wins).
 
@@ -41,7 +45,7 @@ import numpy as np
 
 from ptxgen import irgen
 from ptxgen.ir import (Accum, Assign, BinaryExpr, Cond, ElementwiseImpl, Let, Literal, Load,
-                       Loop, Select, SelectBranch, Var, Write, datatype)
+                       Loop, Select, SelectBranch, Smem, Sync, Var, Write, datatype)
 from ptxgen.loader import load_kernel_data
 
 F32 = datatype("f32")
@@ -79,6 +83,8 @@ class _Gen:
         self.count = 0
         self.bound: dict[str, float] = {}      # name -> magnitude bound
         self.ints: set[str] = set()            # names of s32 values
+        self.block_threads = 0                 # > 0: shared-memory rounds on
+        self.smem_written = False
         self.nonneg: set[str] = set()          # s32 names known to be >= 0
 
     def fresh(self, prefix="v"):
@@ -250,9 +256,30 @@ class _Gen:
         self.bound[acc] = bt * ext if aop == "add" else max(bt, 1e30)
         scope.append(acc)
 
+    def smem_round(self, scope, out):
+        """Each lane writes its slot, a barrier, each lane reads another's."""
+        b = self.block_threads
+        v = self.pick(scope)
+        if self.smem_written:
+            out.append(Sync(barrier_id=0, count=None, warp=False))   # reads done before rewrite
+        out.append(Write(output="sm", index=(_b("%", Var(name="a0"), _lit_i(b)),), values=(v,),
+                         value_dtype=F32, atomic=False, swizzle="NONE"))
+        out.append(Sync(barrier_id=0, count=None, warp=False))
+        s_ = int(self.rng.integers(1, b + 1))
+        name = self.fresh("sh")
+        out.append(Load(names=(name,), input="sm",
+                        index=(_b("%", _b("+", Var(name="a0"), _lit_i(s_)), _lit_i(b)),),
+                        dtype=F32))
+        self.smem_written = True
+        self.bound[name] = self.bound[v]
+        scope.append(name)
+
     def block(self, scope, depth, nstmts):
         out = []
         for _ in range(nstmts):
+            if depth == 0 and self.block_threads and scope and self.rng.random() < 0.15:
+                self.smem_round(scope, out)
+                continue
             r = self.rng.random()
             if r < 0.16 or not scope:
                 self.load(scope, out)
@@ -338,9 +365,19 @@ def case(seed: int) -> Soup:
     n = int(rng.integers(1, 5000))
     k = int(rng.integers(1, 65))
     block = int(rng.choice([32, 64, 128, 256]))
+    srng = np.random.default_rng(88_000 + seed)       # shared-memory draws only
+    shared = srng.random() < 0.4
+    if shared:
+        n = block * int(srng.integers(1, 21))         # every lane of every CTA active
     g = _Gen(rng, n, k)
+    if shared:
+        g.block_threads = block
     scope: list[str] = []
     body = g.block(scope, 0, int(rng.integers(4, 14)))
+    if shared and not g.smem_written:
+        g.smem_round(scope, body)
+    if g.smem_written:
+        body.insert(0, Smem(name="sm", extents=(block,), dtype="float", align=0))
     # every lane writes at least once, at the end
     body.append(Write(output="out", index=(Var(name="a0"),), values=(scope[-1],),
                       value_dtype=F32, atomic=False, swizzle="NONE"))
