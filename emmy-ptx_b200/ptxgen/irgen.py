@@ -299,6 +299,30 @@ def reduce_full(n: int, threads: int = 128, mean: bool = False, entry=None, pid=
                    graph_out_shape=())
 
 
+def scalar_affine(n: int, s: float, t: float, lim: int, block: int = 256,
+                  entry="k_affine_scalar", pid="scalar_affine"):
+    """``out[i] = x[i] * s + t`` for ``i < lim``, else ``x[i]``, with ``s``,
+    ``t`` (f32) and ``lim`` (s32) passed by value -- the runner's
+    ``"scalar": true`` argument form (``docs/API.md:49``), which the kernel
+    body names like any SSA value."""
+    body = [load("in0", "x", (V("a0"),)),
+            Cond(cond=LT(V("a0"), V("lim")),
+                 body=(assign("v0", "multiply", "in0", "s"), assign("v1", "add", "v0", "t"),
+                       write("out", (V("a0"),), "v1")),
+                 else_body=(write("out", (V("a0"),), "in0"),))]
+    tl = tile([ax("a0", n)], body)
+    graph, meta = package(entry, "out", [tl], [("x", (n,), "f32", 0)], [],
+                          ("out", (n,), "f32"), ["x", "s", "t", "lim", "out"],
+                          (math.ceil(n / block), 1, 1), (block, 1, 1), rtol=0.0, atol=0.0,
+                          pid=pid, kernel_inputs=["x", "s", "t", "lim"])
+    scal = {"s": ("f32", float(s)), "t": ("f32", float(t)), "lim": ("i32", int(lim))}
+    k0 = meta["kernels"][0]
+    k0["args"] = [({"name": a["name"], "dtype": scal[a["name"]][0], "shape": [],
+                    "scalar": True, "value": scal[a["name"]][1]} if a["name"] in scal else a)
+                  for a in k0["args"]]
+    return graph, meta
+
+
 def center(n: int, threads: int = 128, unroll: int = 4, pid="center"):
     """A two-kernel problem: ``mean = sum(x) / n`` (r03 schedule), then
     ``y = x - mean`` (pointwise) with ``mean`` an intermediate the runner
@@ -732,6 +756,7 @@ def golden_cases():
         "uniform")
     add("gen_relu_mul_f16_u2_1000", pointwise(1000, 2, "relu_mul", out="mul", dtype="f16",
                                               entry="k_mul_pointwise", pid="gen_relu_mul_f16"))
+    add("gen_scalar_affine_3000", scalar_affine(3000, 1.75, -0.5, 2222, pid="gen_scalar"))
     add("gen_sum_f16_5000", reduce_full(5000, dtype="f16", pid="gen_sum_f16"), 0, "uniform01")
     add("gen_sum_f16acc_f16_3000", reduce_full(3000, dtype="f16", acc_dtype="f16",
                                                pid="gen_sum_f16acc"))

@@ -25,6 +25,12 @@ import numpy as np
 
 from .model import KernelSpec, dtype_info
 
+
+def _value_kind(dtype) -> str:
+    """Register kind of a value of ``dtype`` (f16/bf16 values live in f32)."""
+    k = dtype_info(dtype)[0]
+    return "f32" if k in ("f16", "bf16") else k
+
 _LIBDIR = Path(__file__).resolve().parent / "_lib"
 _lib = None
 
@@ -303,12 +309,23 @@ class LoadedModule:
         check(self.dev.L.emmy_tmap_fill(self.h, sym.encode(), C.byref(d), self.dev.stream),
               f"tensor map {sym}")
 
-    def launch(self, entry: str, grid, block, smem: int, ptrs: list[int], stream=None) -> None:
+    def launch(self, entry: str, grid, block, smem: int, ptrs: list, stream=None) -> None:
+        """``ptrs``: one kernel argument per parameter, in ``arg_order``: a
+        buffer address (int) or a by-value scalar (a ctypes value, the
+        runner's ``"scalar": true`` argument form, ``docs/API.md:49``)."""
         g = (C.c_uint32 * 3)(*[int(x) for x in grid])
         b = (C.c_uint32 * 3)(*[int(x) for x in block])
-        arr = (C.c_uint64 * max(1, len(ptrs)))(*[int(p) for p in ptrs])
-        check(self.dev.L.emmy_launch_ptrs(self.h, entry.encode(), g, b, int(smem), arr,
-                                          len(ptrs), stream or self.dev.stream), f"launch {entry}")
+        if all(isinstance(p, int) for p in ptrs):
+            arr = (C.c_uint64 * max(1, len(ptrs)))(*[int(p) for p in ptrs])
+            check(self.dev.L.emmy_launch_ptrs(self.h, entry.encode(), g, b, int(smem), arr,
+                                              len(ptrs), stream or self.dev.stream),
+                  f"launch {entry}")
+            return
+        vals = [C.c_uint64(p) if isinstance(p, int) else p for p in ptrs]
+        argv = (C.c_void_p * max(1, len(vals)))(
+            *[C.cast(C.pointer(v), C.c_void_p) for v in vals])
+        check(self.dev.L.emmy_launch(self.h, entry.encode(), g, b, int(smem), argv,
+                                     stream or self.dev.stream), f"launch {entry}")
 
     def error_word(self, clear: bool = True) -> int:
         if not self.has_global("emmy_err"):
@@ -364,13 +381,24 @@ class PreparedKernel:
         self.geometry = geometry
         self.ws = 0
         self.bufs: dict[str, int] = {}
+        self.scalars: dict[str, object] = {}
         for name in spec.arg_order:
             a = spec.args[name]
             if a.scalar:
-                raise EmmyError("scalar parameters are not supported by the launcher")
+                # passed by value, in the parameter type the kernel declares
+                # for the argument's value kind (0 when meta.json gives none)
+                ct = {"f32": C.c_float, "f64": C.c_double, "s32": C.c_int32,
+                      "s64": C.c_int64}.get(_value_kind(a.dtype))
+                if ct is None:
+                    raise EmmyError(f"scalar argument {name} of dtype {a.dtype}")
+                v = a.value if a.value is not None else 0
+                self.scalars[name] = ct(float(v) if ct in (C.c_float, C.c_double) else int(v))
+                continue
             self.bufs[name] = self.dev.alloc(a.nbytes)
         for name in spec.arg_order:
             a = spec.args[name]
+            if a.scalar:
+                continue
             if a.output:
                 self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4)
             elif a.data is not None:
@@ -438,11 +466,17 @@ class PreparedKernel:
         """The plan's preparatory launches (operand splitting), if any."""
         if self.geometry == "meta":
             return
-        ptrs = [self.bufs[n] for n in self.spec.arg_order]
+        ptrs = self.kernel_args()
         for pre in self.plan.get("pre", []):
             g, b, sm = plan_geometry(pre, self.dev)
             self.mod.launch(pre["entry"], g, b, sm, ptrs, stream)
             self.launches += 1
+
+    def kernel_args(self) -> list:
+        """The launch's arguments in ``arg_order``: buffer addresses, and
+        scalars by value."""
+        return [self.scalars[n] if n in self.scalars else self.bufs[n]
+                for n in self.spec.arg_order]
 
     def launch_main(self, stream=None) -> None:
         # zero_outputs are cleared before every launch, except outputs the
@@ -455,7 +489,7 @@ class PreparedKernel:
                 continue
             a = self.spec.args[name]
             self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4, stream)
-        ptrs = [self.bufs[n] for n in self.spec.arg_order]
+        ptrs = self.kernel_args()
         self.mod.launch(self.spec.entry, self.grid, self.block, self.smem, ptrs, stream)
         self.launches += 1
 

@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).parent / "golden"
 PROBS = sorted(p.name for p in (GOLDEN / "problems").iterdir() if (p / "meta.json").exists())
 GEN = [c for c in json.loads((GOLDEN / "cases.json").read_text()) if "meta" in c]
-EXACT = ("p0", "gen_add", "gen_relu", "gen_colsum", "gen_sum_f16acc", "soup_")
+EXACT = ("p0", "gen_add", "gen_relu", "gen_colsum", "gen_sum_f16acc", "soup_", "gen_scalar")
 
 
 def _check(spec, inputs, exact, checked=False):
