@@ -340,6 +340,41 @@ def center(n: int, threads: int = 128, unroll: int = 4, pid="center"):
     return {k1["entry"]: g1, k2["entry"]: g2}, meta
 
 
+def zero_chain(n: int, m: int, c: float = 0.75, block: int = 256, pid="zero_chain"):
+    """A two-kernel problem with a delegated zero-init (``TASK.md:95``,
+    ``ptxgen/emit.py:1518-1540``): the first kernel computes ``y = x * c``
+    and, with a ``ZeroPrologue``, clears ``acc`` (m words) for the second,
+    which adds ``y[i]`` into ``acc[i % m]`` with atomic writes and lists
+    ``acc`` under ``zero_delegated`` -- so neither the runner nor the second
+    kernel clears it.  ``y`` and ``acc`` are intermediates chained from the
+    first kernel.  Returns ``({entry: graph}, meta)``."""
+    from .ir import ZeroPrologue
+    b1 = [load("in0", "x", (V("a0"),)), load("in1", "c", (L(0),)),
+          assign("v0", "multiply", "in0", "in1"), write("y", (V("a0"),), "v0")]
+    g1, m1 = package("k_scale_zero", "y", [ZeroPrologue(dst="acc", words=m),
+                                           tile([ax("a0", n)], b1)],
+                     [("x", (n,), "f32", 0)], [("c", float(c))], ("y", (n,), "f32"),
+                     ["x", "c", "y", "acc"], (math.ceil(n / block), 1, 1), (block, 1, 1),
+                     rtol=1e-5, atol=1e-5, pid=pid, kernel_inputs=["x", "c"])
+    k1 = m1["kernels"][0]
+    k1["final"] = False
+    k1["args"] = [a for a in k1["args"] if a["name"] != "acc"] + [
+        {"name": "acc", "dtype": "f32", "shape": [m], "output": True}]
+    b2 = [load("in0", "y", (V("a0"),)),
+          write("acc", (MOD(V("a0"), L(m)),), "in0", atomic=True)]
+    g2, m2 = package("k_accum_into", "acc", [tile([ax("a0", n)], b2)], [], [],
+                     ("acc", (m,), "f32"), ["y", "acc"], (math.ceil(n / block), 1, 1),
+                     (block, 1, 1), rtol=1e-5, atol=1e-5, pid=pid, kernel_inputs=["y", "acc"])
+    g2["nodes"]["acc"]["op_fields"]["zero_delegated"] = ["acc"]
+    k2 = m2["kernels"][0]
+    k2["args"] = [{"name": "y", "dtype": "f32", "shape": [n], "intermediate": True},
+                  {"name": "acc", "dtype": "f32", "shape": [m], "intermediate": True,
+                   "output": True}]
+    meta = {"id": pid, "code": "", "rtol": 1e-5, "atol": 1e-5, "graph_inputs": ["x"],
+            "graph_outputs": ["acc"], "kernels": [k1, k2]}
+    return {k1["entry"]: g1, k2["entry"]: g2}, meta
+
+
 def write_problem(pdir, graphs: dict, meta: dict) -> None:
     """Write ``<entry>.ir.json`` per kernel and ``meta.json`` into ``pdir``."""
     import json

@@ -80,3 +80,35 @@ def test_missing_producer_is_one_line_error(tmp_path):
                                               .parent.parent / "emmy-ptx_b200")})
     assert r.returncode == 1 and r.stdout == ""
     assert len(r.stderr.strip().splitlines()) == 1
+
+
+def write_zero_chain(pdir, n=5000, m=37):
+    """The zero-chain problem plus its expected.npz from the chained oracle."""
+    graphs, meta = irgen.zero_chain(n, m)
+    irgen.write_problem(pdir, graphs, meta)
+    _, specs = load_problem(pdir)
+    produced = _oracle_chain(specs)
+    np.savez(pdir / "expected.npz", acc=produced["acc"])
+    return specs, produced
+
+
+def test_zero_chain_loads_and_chains(tmp_path):
+    """ZeroPrologue in the first kernel, zero_delegated and atomic writes in
+    the second, y and acc chained as intermediates."""
+    specs, produced = write_zero_chain(tmp_path)
+    assert [s.entry for s in specs] == ["k_scale_zero", "k_accum_into"]
+    assert type(specs[0].op.body[0]).__name__ == "ZeroPrologue"
+    assert tuple(specs[1].op.zero_delegated) == ("acc",) and not specs[1].zero_outputs
+    assert specs[1].args["acc"].intermediate and specs[1].args["acc"].output
+    x = np.random.default_rng(0).standard_normal(5000).astype(np.float32)
+    want = np.zeros(37)
+    np.add.at(want, np.arange(5000) % 37, (x * np.float32(0.75)).astype(np.float64))
+    np.testing.assert_allclose(produced["acc"], want, rtol=1e-5, atol=1e-5)
+    if shutil.which("ptxas") is None:
+        return
+    for s in specs:
+        ptx = tmp_path / f"{s.entry}.ptx"
+        ptx.write_text(compile_kernel(s))
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(ptx)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
