@@ -21,3 +21,20 @@ def test_reference_arm_line():
         assert key in line, key
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched as the driver launches it for N > 1 (torchrun, two ranks,
+    gloo rendezvous on 127.0.0.1): rank 0 alone runs and prints one line,
+    the other rank exits 0 without work."""
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                        "--master-port", "29631", str(ROOT / "bench.py"), "--gpus", "2",
+                        "--impl", "reference", "--workload", "pointwise", "--steps", "1",
+                        "--warmup", "3"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
