@@ -26,6 +26,8 @@ a ``Tile`` over N cells whose body is a random mix of
   ``Write`` of a value to the lane's slot ``a0 % B`` of an ``Smem`` array,
   ``Sync``, ``Load`` of another lane's slot ``(a0 + s) % B`` -- a barrier
   also precedes each rewrite, and every slot is written before it is read;
+  and in the same cases ``WarpShuffle`` butterflies folding a copy of a
+  value over 2 to 32 lanes with add, max or min (``ptxgen/interp.py:868-885``);
 * unconditional and conditional ``Write``s of ``out[a0]`` (the last write a
   lane performs wins).
 
@@ -45,7 +47,8 @@ import numpy as np
 
 from ptxgen import irgen
 from ptxgen.ir import (Accum, Assign, BinaryExpr, Cond, ElementwiseImpl, Let, Literal, Load,
-                       Loop, Select, SelectBranch, Smem, Sync, Var, Write, datatype)
+                       Loop, Select, SelectBranch, Smem, Sync, Var, WarpShuffle, Write,
+                       datatype)
 from ptxgen.loader import load_kernel_data
 
 F32 = datatype("f32")
@@ -274,11 +277,37 @@ class _Gen:
         self.bound[name] = self.bound[v]
         scope.append(name)
 
+    def shuffle_round(self, scope, out):
+        """A copy of a loaded value folded over ``length`` lanes by a
+        butterfly (a loaded value differs per lane; the reference shuffles
+        per-lane values only)."""
+        loaded = [n for n in scope if n.startswith(("in", "sh"))]
+        if not loaded:
+            self.smem_round(scope, out)
+            return
+        v = str(self.rng.choice(loaded))
+        length = int(self.rng.choice([2, 4, 8, 16, 32]))
+        op = str(self.rng.choice(["add", "maximum", "minimum"]))
+        if op == "add" and self.bound[v] * length >= 1e30:
+            op = "maximum"
+        w = self.fresh("w")
+        out.append(Assign(name=w, op=ElementwiseImpl("copy"), args=(v,), dtype=F32))
+        wb = f"{w}__o"
+        out.append(WarpShuffle(state=(w,), state_b=(wb,),
+                               combine_states=(Assign(name=w, op=ElementwiseImpl(op),
+                                                      args=(w, wb), dtype=None),),
+                               length=length, dtype=F32))
+        self.bound[w] = self.bound[v] * (length if op == "add" else 1)
+        scope.append(w)
+
     def block(self, scope, depth, nstmts):
         out = []
         for _ in range(nstmts):
             if depth == 0 and self.block_threads and scope and self.rng.random() < 0.15:
-                self.smem_round(scope, out)
+                if self.rng.random() < 0.5:
+                    self.smem_round(scope, out)
+                else:
+                    self.shuffle_round(scope, out)
                 continue
             r = self.rng.random()
             if r < 0.16 or not scope:
