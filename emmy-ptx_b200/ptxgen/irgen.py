@@ -18,7 +18,9 @@ re-derives the shape-dependent literals:
                      atomic writes into a zeroed C);
 * ``attention``   -- a02 (one output element per thread, online softmax)
                      and its ``[B, H, S, D]`` generalisation with K given
-                     untransposed.
+                     untransposed;
+* ``attention_tiled`` -- a01 (the same online softmax, a 4 x 2 output tile
+                     per thread).
 
 At the shipped shapes the generated bodies equal the shipped ones byte for
 byte (``tests/test_irgen.py``); that pins the generator to the reference's
@@ -653,9 +655,12 @@ def matmul_splitk(m: int, n: int, k: int, slice_k: int = 8, entry="k_matmul",
 # ---------------------------------------------------------------------------
 
 
-def _online_step(score_name: str, vload: Load, key_axis: str):
-    """The per-key online-softmax update of a02, for one output element."""
-    s = "__c0_0"
+def _online_step(score_name: str, vload: Load | None, key_axis: str, cell=(0, 0),
+                 vname: str = "in7__bc0"):
+    """The per-key online-softmax update of a02 for one output element; with
+    ``cell`` = (r, c) the update of output (row r, column c) of a01's
+    register tile, whose ``v`` row is loaded once, in cell (0, 0)."""
+    s = f"__c{cell[0]}_{cell[1]}"
     return [
         assign(f"v4{s}", "multiply", score_name, "v1"),
         Let(name=f"one{s}", value=Lf(1.0), dtype=F32),
@@ -668,8 +673,8 @@ def _online_step(score_name: str, vload: Load, key_axis: str):
         assign(f"v4__acc3_sb{s}", "multiply", f"one{s}", f"v4__beta{s}"),
         accum(f"acc3{s}", f"v4__acc3_sb{s}", "add", (key_axis,), base=f"v4__acc3_sa{s}"),
         assign(f"v4__acc5__sum_sa{s}", "multiply", f"acc5__sum{s}", f"v4__alpha{s}"),
-        vload,
-        assign(f"v4__acc5__sum_sb{s}", "multiply", "in7__bc0", f"v4__beta{s}"),
+    ] + ([vload] if vload is not None else []) + [
+        assign(f"v4__acc5__sum_sb{s}", "multiply", vname, f"v4__beta{s}"),
         accum(f"acc5__sum{s}", f"v4__acc5__sum_sb{s}", "add", (key_axis,),
               base=f"v4__acc5__sum_sa{s}"),
         accum(f"acc1{s}", f"v4{s}", "maximum", (key_axis,)),
@@ -702,6 +707,46 @@ def attention(s: int, d: int, scale_div: float | None = None,
                    [("div_c1", c)], ("matmul_1", (s, d), "f32"),
                    ["div_c1", "q", "kt", "v", "matmul_1"], (s * d // 32, 1, 1), (32, 1, 1),
                    rtol=1e-3, atol=1e-4, pid=pid)
+
+
+def attention_tiled(s: int, d: int, scale_div: float | None = None,
+                    entry="k_matmul_softmax_reduce_b55365", pid="attention_tiled"):
+    """softmax(q.kt / c) . v for one head (a01): the a02 online softmax with
+    each of a CTA's 128 threads holding a 4 x 2 register tile of the output
+    (8 x 16 threads over a 32 x 32 block), one q.kt dot product per tile row,
+    one paired ``v`` load per key and the key loop unrolled."""
+    if s % 32 or d % 32:
+        raise ValueError("sequence length and head dim must be multiples of 32")
+    c = float(scale_div) if scale_div is not None else math.sqrt(d)
+    rows = [ADD(ADD(MUL(V("a0_b"), L(32)), MUL(V("a0_u"), L(4))), L(r)) for r in range(4)]
+    cols = [ADD(ADD(MUL(V("a5_b"), L(32)), MUL(V("a5_u"), L(2))), L(j)) for j in range(2)]
+    key = []
+    for r in range(4):
+        key.append(loop("a2", d, [load(f"in2__ar{r}", "q", (rows[r], V("a2"))),
+                                  load(f"in1__ar{r}", "kt", (V("a2"), V("a1"))),
+                                  assign(f"v3__ar{r}", "multiply", f"in1__ar{r}", f"in2__ar{r}"),
+                                  accum(f"acc0__ar{r}", f"v3__ar{r}", "add", ("a2",))]))
+    vload = load(("in7__bc0", "in7__bc1"), "v", (V("a1"), cols[0]))
+    for r in range(4):
+        for j in range(2):
+            key += _online_step(f"acc0__ar{r}", vload if (r, j) == (0, 0) else None, "a1",
+                                cell=(r, j), vname=f"in7__bc{j}")
+    body = [load("in0", "div_c1", (L(0),)), assign("v1", "reciprocal", "in0"),
+            loop("a1", s, key, unroll=True)]
+    for r in range(4):
+        for j in range(2):
+            cs = f"__c{r}_{j}"
+            body += [assign(f"v9{cs}", "reciprocal", f"acc3{cs}"),
+                     assign(f"acc5{cs}", "multiply", f"acc5__sum{cs}", f"v9{cs}"),
+                     write("matmul_1", (rows[r], cols[j]), f"acc5{cs}")]
+    t = tile([ax("a0_b", s // 32, win("a0", s)), ax("a5_b", d // 32, win("a5", d)),
+              ax("a0_u", 8), ax("a5_u", 16)], body, block_threads=128,
+             raster_axes=("a0_b", "a5_b"))
+    return package(entry, "matmul_1", [t],
+                   [("kt", (d, s), "f32", 1), ("q", (s, d), "f32", 0), ("v", (s, d), "f32", 2)],
+                   [("div_c1", c)], ("matmul_1", (s, d), "f32"),
+                   ["div_c1", "q", "kt", "v", "matmul_1"], ((s // 32) * (d // 32), 1, 1),
+                   (128, 1, 1), rtol=1e-3, atol=1e-4, pid=pid)
 
 
 def attention_bhsd(b: int, h: int, s: int, d: int, dtype: str = "f32",
@@ -782,6 +827,7 @@ def golden_cases():
     add("gen_matmul_64x128x192", matmul(64, 128, 192, pid="gen_matmul"), 0, "uniform")
     add("gen_splitk_32x64x64_s16", matmul_splitk(32, 64, 64, slice_k=16, pid="gen_splitk"))
     add("gen_attn_64x32", attention(64, 32, pid="gen_attn"))
+    add("gen_attn_tiled_96x64", attention_tiled(96, 64, pid="gen_attn_tiled"))
     add("gen_attn_bhsd_2x2x32x32", attention_bhsd(2, 2, 32, 32, pid="gen_attn_bhsd"))
     # f16 and f64 data paths (``ptxgen/model.py:8-31``, ``ptxgen/interp.py:115-141``)
     add("gen_add_f64_u2_1000", pointwise(1000, 2, "add", dtype="f64", pid="gen_add_f64"))

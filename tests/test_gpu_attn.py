@@ -77,6 +77,22 @@ def test_generated(dtype, shape):
     assert np.abs(out - ref).max() <= tol * scale, float(np.abs(out - ref).max() / scale)
 
 
+@pytest.mark.parametrize("geometry", ["plan", "meta"])
+@pytest.mark.parametrize("shape", [(96, 64), (128, 32), (256, 128), (512, 64)])
+def test_tiled_generated(shape, geometry):
+    """a01's schedule (4 x 2 outputs per thread) at other shapes: against the
+    oracle where it is quick, and against float64 numpy everywhere."""
+    s, d = shape
+    spec = load_kernel_data(*irgen.attention_tiled(s, d), "attt")
+    inputs = make_inputs(spec)
+    got = _run(spec, inputs, geometry)["matmul_1"]
+    if s * d <= 128 * 64:
+        want = interpret(spec, {k: v.copy() for k, v in inputs.items()})["matmul_1"]
+        assert np.allclose(got, want, rtol=1e-4, atol=1e-5), float(np.abs(got - want).max())
+    ref = _ref(inputs["q"], np.swapaxes(inputs["kt"], 0, 1), inputs["v"])
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_rescale_path(dtype):
     """Keys scaled by 1 + 6 j / S: each row's max keeps growing over the key

@@ -26,6 +26,7 @@ CASES = {
     "f03_l2norm": lambda: irgen.l2norm(64, 512),
     "m01_matmul_512": lambda: irgen.matmul(512, 512, 512),
     "m02_matmul_rect": lambda: irgen.matmul_splitk(128, 64, 256, slice_k=8),
+    "a01_attention": lambda: irgen.attention_tiled(64, 64, 8.0),
     "a02_attention_128": lambda: irgen.attention(128, 32, 5.656854),
 }
 
