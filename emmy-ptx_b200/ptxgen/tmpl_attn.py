@@ -150,6 +150,17 @@ def _idesc(kind: str, m: int, n: int) -> int:
     return (1 << 4) | (fmt << 7) | (fmt << 10) | ((n >> 3) << 17) | ((m >> 4) << 24)
 
 
+def _p_col(key: int, bkv: int, split: int, f32: bool) -> int:
+    """TMEM column (from the S buffer's first) of P for key ``key`` of a key
+    block: each softmax thread of a row writes P over its own ``bkv // split``
+    score columns -- f32 one column per key, bf16 two keys per column in the
+    first half of them."""
+    if f32:
+        return key
+    hs = bkv // split
+    return (key // hs) * hs + (key % hs) // 2
+
+
 def _split_o_on() -> bool:
     v = os.environ.get("EMMY_ATTN_SPLIT_O")
     return SPLIT_O_DEFAULT if v is None else v not in ("0", "")
@@ -964,7 +975,7 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
                         # A (P) from TMEM: a 32-byte K-step is 8 columns (16 packed
                         # bf16 or 8 f32); the f32 lo half sits BKV columns on
                         a_ = k.reg("u32")
-                        k(f"add.u32 {a_}, {pb}, {(c * 4 + kk) * 8 + ha * BKV}")
+                        k(f"add.u32 {a_}, {pb}, {_p_col(c * atom + kk * 32 // e, BKV, split, f32) + ha * BKV}")
                         a_ = f"[{a_}]"
                         b_ = dsc(ds, lay[("v", 0, hb)] + c * lay["v_chunk"] + kk * 32)
                         acc = firstb if first else yes
@@ -1248,14 +1259,11 @@ def _emit_tc(k: Kernel, spec, plan, lay, base, tid, cta, ncta):
         for t in range(nreg // 2):
             k(f"cvt.rn.bf16x2.f32 {pk[t]}, {sv[2 * t + 1]}, {sv[2 * t]}")
         pieces = [(pk, 0)]
-    # P over this row's S columns in S buffer g % 2: f32 hi over the thread's
-    # own score columns and lo BKV columns on; bf16 packed into the first half
-    # of the row, whose partner-owned scores were loaded before the max
-    # exchange above
+    # P over this thread's own S columns in S buffer g % 2 (the partner may
+    # not have loaded its scores yet): f32 hi over the score columns and lo
+    # BKV columns on; bf16 packed into the first half of them
     p_cur = k.reg("u32")
-    k(f"mad.lo.u32 {p_cur}, {sb}, {s_cols}, {tmem}")
-    k(f"add.u32 {p_cur}, {p_cur}, {lane_off}")
-    k(f"mad.lo.u32 {p_cur}, {half}, {hs if f32 else hs // 2}, {p_cur}")
+    k(f"mad.lo.u32 {p_cur}, {sb}, {s_cols}, {s_row}")
     for regs, off in pieces:
         for c0 in range(0, len(regs), 32):
             cnt = min(32, len(regs) - c0)
