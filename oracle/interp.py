@@ -262,7 +262,8 @@ def apply_op(name: str, args: list[Val]) -> Val:
             with np.errstate(all="ignore"):
                 return Val("f32", np.fmod(af.astype(np.float64), bf.astype(np.float64))
                            .astype(np.float32))
-        return Val("s32", np.fmod(coerce(a, "s32").a, coerce(b, "s32").a).astype(np.int32))
+        with np.errstate(divide="ignore"):     # integer fmod by 0 gives 0
+            return Val("s32", np.fmod(coerce(a, "s32").a, coerce(b, "s32").a).astype(np.int32))
     if name in ("logical_and", "logical_or"):
         p, q = truthy(args[0]), truthy(args[1])
         return Val("pred", (p & q) if name == "logical_and" else (p | q))
@@ -274,7 +275,8 @@ def apply_op(name: str, args: list[Val]) -> Val:
     if name in ("remainder", "bitand", "bitor", "bitxor", "shl", "shr"):
         a, b = coerce(args[0], "s32").a, coerce(args[1], "s32").a
         if name == "remainder":
-            return Val("s32", np.fmod(a, b).astype(np.int32))
+            with np.errstate(divide="ignore"):  # integer fmod by 0 gives 0
+                return Val("s32", np.fmod(a, b).astype(np.int32))
         if name == "bitand":
             return Val("s32", a & b)
         if name == "bitor":
