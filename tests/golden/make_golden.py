@@ -7,6 +7,8 @@ checkout's location in the build container).  It writes:
 * ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
   ``expected.npz`` -- the reference's own golden vectors (numpy float64
   results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
+* ``fuzz_digests.json``: SHA-256 digests of the reference interpreter's
+  outputs on every case of the family fuzzer (``tests/fuzz_ir.py``);
 * ``ref_interp/<case>.npz``: outputs of the reference's golden model
   ``ptxgen/interp.py`` run here on extra inputs (every problem reseeded, plus
   IR that ``ptxgen.irgen`` generates at other shapes, plus random statement
@@ -21,6 +23,7 @@ Nothing at test time reads the reference checkout; only these files.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import importlib.util
 import json
 import shutil
@@ -184,7 +187,39 @@ def main() -> int:
                       "meta": f"generated/{name}.meta.json", "seed_offset": 0, "dist": "normal"})
     (HERE / "cases.json").write_text(json.dumps(cases, indent=1) + "\n")
     print(f"{len(cases)} reference-interpreter cases written")
+    n = record_fuzz_digests(ref_interp)
+    print(f"{n} family-fuzzer digests written")
     return 0
+
+
+FUZZ_CASES = 192
+
+
+def output_digest(arr) -> dict:
+    """dtype, shape and SHA-256 of an output's bytes (C order)."""
+    a = np.ascontiguousarray(np.asarray(arr))
+    return {"dtype": str(a.dtype), "shape": list(a.shape),
+            "sha256": hashlib.sha256(a.tobytes()).hexdigest()}
+
+
+def record_fuzz_digests(ref_interp) -> int:
+    """``fuzz_digests.json``: the reference interpreter's outputs on every
+    case of the family fuzzer (``tests/fuzz_ir.py``), as digests, so the
+    oracle can be held to them bit for bit without storing the arrays.
+    Cases in a dtype the reference lacks (bf16) are listed as skipped."""
+    from tests import fuzz_ir
+    out = []
+    for seed in range(FUZZ_CASES):
+        c = fuzz_ir.case(seed)
+        try:
+            res = ref_interp.interpret(c.spec, {k: v.copy() for k, v in c.inputs.items()})
+        except NotImplementedError as exc:
+            out.append({"seed": seed, "family": c.family, "skipped": str(exc)})
+            continue
+        out.append({"seed": seed, "family": c.family,
+                    "outputs": {k: output_digest(v) for k, v in sorted(res.items())}})
+    (HERE / "fuzz_digests.json").write_text(json.dumps(out, indent=1) + "\n")
+    return sum("outputs" in o for o in out)
 
 
 if __name__ == "__main__":

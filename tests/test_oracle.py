@@ -3,7 +3,9 @@
 * every shipped problem: oracle output vs ``expected.npz`` within the
   problem's own ``rtol``/``atol`` (``scripts/verify_semantics.py:65-97``);
 * every recorded case: oracle output vs the reference interpreter's output on
-  the same inputs, bit for bit.
+  the same inputs, bit for bit;
+* every non-bf16 case of the family fuzzer: the oracle's outputs against
+  SHA-256 digests of the reference interpreter's (``fuzz_digests.json``).
 """
 
 import json
@@ -52,3 +54,25 @@ def test_oracle_bit_exact_vs_reference_interpreter(case):
     ref = np.load(GOLDEN / "ref_interp" / f"{case['case']}.npz")
     for name in ref.files:
         assert np.array_equal(np.asarray(outs[name]), ref[name], equal_nan=True), name
+
+
+FUZZ = [d for d in json.loads((GOLDEN / "fuzz_digests.json").read_text()) if "outputs" in d]
+
+
+def test_fuzz_digests_cover_the_fuzzer():
+    from tests.golden.make_golden import FUZZ_CASES
+    from tests.test_gpu_fuzz import N_CASES
+    assert FUZZ_CASES == N_CASES and len(FUZZ) >= 170
+
+
+@pytest.mark.parametrize("rec", FUZZ, ids=[f"fuzz{d['seed']}_{d['family']}" for d in FUZZ])
+def test_oracle_bit_exact_on_fuzz_cases(rec):
+    """Every non-bf16 case of the family fuzzer (the GPU fuzz tests' checker):
+    the oracle's outputs hash to the reference interpreter's."""
+    from tests import fuzz_ir
+    from tests.golden.make_golden import output_digest
+    c = fuzz_ir.case(rec["seed"])
+    outs = interpret(c.spec, {k: v.copy() for k, v in c.inputs.items()})
+    assert sorted(outs) == sorted(rec["outputs"])
+    for name, want in rec["outputs"].items():
+        assert output_digest(outs[name]) == want, name
