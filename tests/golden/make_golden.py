@@ -7,8 +7,10 @@ checkout's location in the build container).  It writes:
 * ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
   ``expected.npz`` -- the reference's own golden vectors (numpy float64
   results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
-* ``fuzz_digests.json``: SHA-256 digests of the reference interpreter's
-  outputs on every case of the family fuzzer (``tests/fuzz_ir.py``);
+* ``fuzz_digests.json``, ``soup_digests.json``: SHA-256 digests of the
+  reference interpreter's outputs on every case of the family fuzzer
+  (``tests/fuzz_ir.py``) and of the statement-mix fuzzer
+  (``tests/fuzz_soup.py``);
 * ``ref_interp/<case>.npz``: outputs of the reference's golden model
   ``ptxgen/interp.py`` run here on extra inputs (every problem reseeded, plus
   IR that ``ptxgen.irgen`` generates at other shapes, plus random statement
@@ -189,10 +191,13 @@ def main() -> int:
     print(f"{len(cases)} reference-interpreter cases written")
     n = record_fuzz_digests(ref_interp)
     print(f"{n} family-fuzzer digests written")
+    n = record_fuzz_digests(ref_interp, "fuzz_soup", SOUP_FUZZ_CASES, "soup_digests.json")
+    print(f"{n} statement-mix digests written")
     return 0
 
 
 FUZZ_CASES = 192
+SOUP_FUZZ_CASES = 128
 
 
 def output_digest(arr) -> dict:
@@ -202,23 +207,26 @@ def output_digest(arr) -> dict:
             "sha256": hashlib.sha256(a.tobytes()).hexdigest()}
 
 
-def record_fuzz_digests(ref_interp) -> int:
-    """``fuzz_digests.json``: the reference interpreter's outputs on every
-    case of the family fuzzer (``tests/fuzz_ir.py``), as digests, so the
-    oracle can be held to them bit for bit without storing the arrays.
-    Cases in a dtype the reference lacks (bf16) are listed as skipped."""
-    from tests import fuzz_ir
+def record_fuzz_digests(ref_interp, module="fuzz_ir", n_cases=FUZZ_CASES,
+                        fname="fuzz_digests.json") -> int:
+    """``fname``: the reference interpreter's outputs on every case of a
+    fuzzer (``tests/fuzz_ir.py``, the family fuzzer, or ``tests/fuzz_soup.py``,
+    the statement mixes), as digests, so the oracle can be held to them bit
+    for bit without storing the arrays.  Cases in a dtype the reference
+    lacks (bf16) are listed as skipped."""
+    import importlib
+    fuzz = importlib.import_module(f"tests.{module}")
     out = []
-    for seed in range(FUZZ_CASES):
-        c = fuzz_ir.case(seed)
+    for seed in range(n_cases):
+        c = fuzz.case(seed)
         try:
             res = ref_interp.interpret(c.spec, {k: v.copy() for k, v in c.inputs.items()})
         except NotImplementedError as exc:
-            out.append({"seed": seed, "family": c.family, "skipped": str(exc)})
+            out.append({"seed": seed, "family": getattr(c, "family", "soup"), "skipped": str(exc)})
             continue
-        out.append({"seed": seed, "family": c.family,
+        out.append({"seed": seed, "family": getattr(c, "family", "soup"),
                     "outputs": {k: output_digest(v) for k, v in sorted(res.items())}})
-    (HERE / "fuzz_digests.json").write_text(json.dumps(out, indent=1) + "\n")
+    (HERE / fname).write_text(json.dumps(out, indent=1) + "\n")
     return sum("outputs" in o for o in out)
 
 

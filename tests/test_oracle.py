@@ -4,8 +4,9 @@
   problem's own ``rtol``/``atol`` (``scripts/verify_semantics.py:65-97``);
 * every recorded case: oracle output vs the reference interpreter's output on
   the same inputs, bit for bit;
-* every non-bf16 case of the family fuzzer: the oracle's outputs against
-  SHA-256 digests of the reference interpreter's (``fuzz_digests.json``).
+* every non-bf16 case of the family fuzzer and every statement mix of the
+  soup fuzzer: the oracle's outputs against SHA-256 digests of the reference
+  interpreter's (``fuzz_digests.json``, ``soup_digests.json``).
 """
 
 import json
@@ -56,22 +57,31 @@ def test_oracle_bit_exact_vs_reference_interpreter(case):
         assert np.array_equal(np.asarray(outs[name]), ref[name], equal_nan=True), name
 
 
-FUZZ = [d for d in json.loads((GOLDEN / "fuzz_digests.json").read_text()) if "outputs" in d]
+def _digests(fname, module):
+    return [dict(d, module=module) for d in json.loads((GOLDEN / fname).read_text())
+            if "outputs" in d]
 
 
-def test_fuzz_digests_cover_the_fuzzer():
-    from tests.golden.make_golden import FUZZ_CASES
+FUZZ = _digests("fuzz_digests.json", "fuzz_ir") + _digests("soup_digests.json", "fuzz_soup")
+
+
+def test_fuzz_digests_cover_the_fuzzers():
+    from tests.golden.make_golden import FUZZ_CASES, SOUP_FUZZ_CASES
     from tests.test_gpu_fuzz import N_CASES
-    assert FUZZ_CASES == N_CASES and len(FUZZ) >= 170
+    from tests.test_gpu_fuzz_soup import N_CASES as N_SOUP
+    assert FUZZ_CASES == N_CASES and SOUP_FUZZ_CASES == N_SOUP
+    assert sum(d["module"] == "fuzz_ir" for d in FUZZ) >= 170
+    assert sum(d["module"] == "fuzz_soup" for d in FUZZ) == N_SOUP
 
 
-@pytest.mark.parametrize("rec", FUZZ, ids=[f"fuzz{d['seed']}_{d['family']}" for d in FUZZ])
+@pytest.mark.parametrize("rec", FUZZ, ids=[f"{d['module']}{d['seed']}_{d['family']}" for d in FUZZ])
 def test_oracle_bit_exact_on_fuzz_cases(rec):
-    """Every non-bf16 case of the family fuzzer (the GPU fuzz tests' checker):
-    the oracle's outputs hash to the reference interpreter's."""
-    from tests import fuzz_ir
+    """Every case of the family fuzzer but the bf16 ones, and every
+    statement mix (the GPU fuzz tests' checker): the oracle's outputs hash
+    to the reference interpreter's."""
+    import importlib
     from tests.golden.make_golden import output_digest
-    c = fuzz_ir.case(rec["seed"])
+    c = importlib.import_module(f"tests.{rec['module']}").case(rec["seed"])
     outs = interpret(c.spec, {k: v.copy() for k, v in c.inputs.items()})
     assert sorted(outs) == sorted(rec["outputs"])
     for name, want in rec["outputs"].items():
