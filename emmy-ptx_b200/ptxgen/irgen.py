@@ -711,7 +711,9 @@ def attention(s: int, d: int, scale_div: float | None = None,
 
 def attention_tiled(s: int, d: int, scale_div: float | None = None,
                     entry="k_matmul_softmax_reduce_b55365", pid="attention_tiled"):
-    """softmax(q.kt / c) . v for one head (a01): the a02 online softmax with
+    """softmax(q.kt / c) . v for one head (a01,
+    ``problems/a01_attention/k_matmul_softmax_reduce_b55365.ir.json``): the
+    a02 online softmax with
     each of a CTA's 128 threads holding a 4 x 2 register tile of the output
     (8 x 16 threads over a 32 x 32 block), one q.kt dot product per tile row,
     one paired ``v`` load per key and the key loop unrolled."""
