@@ -1,0 +1,60 @@
+"""Every form of the attention template assembles for sm_100a and fits its
+launch, on the CPU: f32 and bf16, head dims 32-256, split O on and off, and
+the exp2 polynomial share at 0, 1 and 4 pairs of four.
+
+"Fits" means the main kernel's registers (allocated per thread in multiples
+of 8) fit both the SM's 64K-register file for the whole block and each
+sub-partition's 16K registers for the warps it hosts (warp w runs on
+sub-partition w % 4).  A launch over either limit fails with "too many
+resources requested", which ptxas alone does not report."""
+
+import json
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from ptxgen import irgen
+from ptxgen.emit import compile_kernel
+from ptxgen.loader import load_kernel_data
+
+VARIANTS = ([("f32", d, "1", None) for d in (32, 64, 128)]
+            + [("bf16", d, so, None) for d in (32, 64, 128, 256) for so in ("1", "0")]
+            + [("bf16", 128, "1", poly) for poly in ("0", "4")])
+
+
+def _main_registers(ptxas_log: str, entry: str) -> int:
+    """Registers of ``entry`` from ``ptxas -v`` output."""
+    cur = None
+    for line in ptxas_log.splitlines():
+        m = re.search(r"Compiling entry function '(\w+)'", line)
+        if m:
+            cur = m.group(1)
+        m = re.search(r"Used (\d+) registers", line)
+        if m and cur == entry:
+            return int(m.group(1))
+    raise AssertionError(f"no register count for {entry}")
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+@pytest.mark.parametrize("dtype,d,split_o,poly", VARIANTS,
+                         ids=[f"{t}-d{d}-so{s}-poly{p}" for t, d, s, p in VARIANTS])
+def test_attention_form_assembles_and_fits(dtype, d, split_o, poly, tmp_path, monkeypatch):
+    monkeypatch.setenv("EMMY_ATTN_SPLIT_O", split_o)
+    if poly is not None:
+        monkeypatch.setenv("EMMY_ATTN_EXP_POLY", poly)
+    spec = load_kernel_data(*irgen.attention_bhsd(1, 2, 512, d, dtype), "av")
+    ptx = compile_kernel(spec)
+    plan = json.loads(re.search(r"// @emmy-plan (\{.*\})", ptx).group(1))
+    assert plan["template"] == "attention"
+    f = tmp_path / "k.ptx"
+    f.write_text(ptx)
+    r = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", "/dev/null", str(f)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    regs = -(-_main_registers(r.stderr, plan["entry"]) // 8) * 8
+    threads = plan["block"]
+    assert threads * regs <= 65536, (threads, regs)
+    warps_per_subpartition = -(-(threads // 32) // 4)
+    assert warps_per_subpartition * 32 * regs <= 16384, (threads, regs)
