@@ -1,6 +1,7 @@
 """Every form of the attention template assembles for sm_100a and fits its
 launch, on the CPU: f32 and bf16, head dims 32-256, split O on and off, and
-the exp2 polynomial share at 0, 1 and 4 pairs of four.
+the exp2 polynomial share at 0, 1 and 4 pairs of four.  So do the benchmark
+kernels of every template, pre-pass kernels included.
 
 "Fits" means the main kernel's registers (allocated per thread in multiples
 of 8) fit both the SM's 64K-register file for the whole block and each
@@ -58,3 +59,25 @@ def test_attention_form_assembles_and_fits(dtype, d, split_o, poly, tmp_path, mo
     assert threads * regs <= 65536, (threads, regs)
     warps_per_subpartition = -(-(threads // 32) // 4)
     assert warps_per_subpartition * 32 * regs <= 16384, (threads, regs)
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+@pytest.mark.parametrize("name", sorted(irgen.bench_kernels()))
+def test_bench_kernel_fits(name, tmp_path):
+    """Every benchmark kernel and its pre-pass kernels fit their launches."""
+    spec = load_kernel_data(*irgen.bench_kernels()[name](), name)
+    ptx = compile_kernel(spec)
+    m = re.search(r"// @emmy-plan (\{.*\})", ptx)
+    plan = json.loads(m.group(1)) if m else None
+    f = tmp_path / "k.ptx"
+    f.write_text(ptx)
+    r = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", "/dev/null", str(f)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    launches = ([(plan["entry"], plan["block"])] + [(p["entry"], p["block"])
+                                                    for p in plan.get("pre", [])]
+                if plan else [(spec.entry, spec.block[0] * spec.block[1] * spec.block[2])])
+    for entry, threads in launches:
+        regs = -(-_main_registers(r.stderr, entry) // 8) * 8
+        assert threads * regs <= 65536, (entry, threads, regs)
+        assert -(-(threads // 32) // 4) * 32 * regs <= 16384, (entry, threads, regs)
