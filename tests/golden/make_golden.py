@@ -7,6 +7,9 @@ checkout's location in the build container).  It writes:
 * ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
   ``expected.npz`` -- the reference's own golden vectors (numpy float64
   results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
+* ``special_digests.json``: digests of the reference interpreter's outputs
+  on every recorded IR with NaN, infinities, signed zeros, subnormals and
+  near-overflow values mixed into its inputs (``special_inputs``);
 * ``fuzz_digests.json``, ``soup_digests.json``: SHA-256 digests of the
   reference interpreter's outputs on every case of the family fuzzer
   (``tests/fuzz_ir.py``) and of the statement-mix fuzzer
@@ -193,7 +196,55 @@ def main() -> int:
     print(f"{n} family-fuzzer digests written")
     n = record_fuzz_digests(ref_interp, "fuzz_soup", SOUP_FUZZ_CASES, "soup_digests.json")
     print(f"{n} statement-mix digests written")
+    n = record_special_digests(ref_interp, cases)
+    print(f"{n} special-value digests written")
     return 0
+
+
+SPECIAL_VALUES = (np.nan, np.inf, -np.inf, -0.0, 1e-40, -1e-40, 3e38, -3e38, 0.0, 1.0)
+
+
+def special_inputs(spec) -> dict[str, np.ndarray]:
+    """``rebuild_inputs(spec, 5000, "normal")`` with one element in 50 of
+    every floating input of 8 or more elements replaced by a special value:
+    NaN, +-inf, -0.0, an f32 subnormal, +-3e38 or 0 and 1 (as stored in the
+    argument's dtype)."""
+    inputs = rebuild_inputs(spec, 5000, "normal")
+    rng = np.random.default_rng(1)
+    special = np.array(SPECIAL_VALUES, np.float64)
+    for name, a in inputs.items():
+        if spec.args[name].output or a.dtype.kind != "f" or a.size < 8:
+            continue
+        flat = a.reshape(-1)
+        idx = rng.choice(flat.size, size=max(1, flat.size // 50), replace=False)
+        with np.errstate(over="ignore"):
+            flat[idx] = rng.choice(special, size=idx.size).astype(a.dtype)
+    return inputs
+
+
+def record_special_digests(ref_interp, cases) -> int:
+    """``special_digests.json``: the reference interpreter's outputs, as
+    digests, on every recorded IR (shipped and generated) with
+    ``special_inputs``."""
+    out, seen = [], set()
+    for c in cases:
+        if c["ir"] in seen:
+            continue
+        seen.add(c["ir"])
+        spec = _case_spec(c)
+        with np.errstate(all="ignore"):
+            res = ref_interp.interpret(spec, special_inputs(spec))
+        out.append({"case": c["case"], "ir": c["ir"], **({"meta": c["meta"]} if "meta" in c else {}),
+                    "outputs": {k: output_digest(v) for k, v in sorted(res.items())}})
+    (HERE / "special_digests.json").write_text(json.dumps(out, indent=1) + "\n")
+    return len(out)
+
+
+def _case_spec(c):
+    if "meta" in c:
+        return load_kernel_data(json.loads((HERE / c["ir"]).read_text()),
+                                json.loads((HERE / c["meta"]).read_text()), c["case"])
+    return load_kernel(HERE / c["ir"])
 
 
 FUZZ_CASES = 192

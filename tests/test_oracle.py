@@ -6,7 +6,10 @@
   the same inputs, bit for bit;
 * every non-bf16 case of the family fuzzer and every statement mix of the
   soup fuzzer: the oracle's outputs against SHA-256 digests of the reference
-  interpreter's (``fuzz_digests.json``, ``soup_digests.json``).
+  interpreter's (``fuzz_digests.json``, ``soup_digests.json``);
+* every recorded IR with special values (NaN, infinities, signed zeros,
+  subnormals, near-overflow) in its inputs, against digests of the
+  reference interpreter's outputs (``special_digests.json``).
 """
 
 import json
@@ -83,6 +86,27 @@ def test_oracle_bit_exact_on_fuzz_cases(rec):
     from tests.golden.make_golden import output_digest
     c = importlib.import_module(f"tests.{rec['module']}").case(rec["seed"])
     outs = interpret(c.spec, {k: v.copy() for k, v in c.inputs.items()})
+    assert sorted(outs) == sorted(rec["outputs"])
+    for name, want in rec["outputs"].items():
+        assert output_digest(outs[name]) == want, name
+
+
+SPECIAL = json.loads((GOLDEN / "special_digests.json").read_text())
+
+
+def test_special_digests_cover_every_recorded_ir():
+    assert len(SPECIAL) == len({c["ir"] for c in CASES})
+
+
+@pytest.mark.parametrize("rec", SPECIAL, ids=[d["case"] for d in SPECIAL])
+def test_oracle_bit_exact_on_special_values(rec):
+    """NaN, infinities, signed zeros, subnormals and near-overflow values in
+    the inputs of every recorded IR: the oracle's outputs, NaN payloads
+    included, hash to the reference interpreter's."""
+    from tests.golden.make_golden import _case_spec, output_digest, special_inputs
+    spec = _case_spec(rec)
+    with np.errstate(all="ignore"):
+        outs = interpret(spec, special_inputs(spec))
     assert sorted(outs) == sorted(rec["outputs"])
     for name, want in rec["outputs"].items():
         assert output_digest(outs[name]) == want, name
