@@ -1,7 +1,8 @@
 """Every form of the attention template assembles for sm_100a and fits its
 launch, on the CPU: f32 and bf16, head dims 32-256, split O on and off, and
 the exp2 polynomial share at 0, 1 and 4 pairs of four.  So do the benchmark
-kernels of every template, pre-pass kernels included.
+kernels of every template, pre-pass kernels included, and a quarter of the
+family fuzzer's cases, template and range-checked generic.
 
 "Fits" means the main kernel's registers (allocated per thread in multiples
 of 8) fit both the SM's 64K-register file for the whole block and each
@@ -49,24 +50,12 @@ def test_attention_form_assembles_and_fits(dtype, d, split_o, poly, tmp_path, mo
     ptx = compile_kernel(spec)
     plan = json.loads(re.search(r"// @emmy-plan (\{.*\})", ptx).group(1))
     assert plan["template"] == "attention"
-    f = tmp_path / "k.ptx"
-    f.write_text(ptx)
-    r = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", "/dev/null", str(f)],
-                       capture_output=True, text=True)
-    assert r.returncode == 0, r.stderr[-2000:]
-    regs = -(-_main_registers(r.stderr, plan["entry"]) // 8) * 8
-    threads = plan["block"]
-    assert threads * regs <= 65536, (threads, regs)
-    warps_per_subpartition = -(-(threads // 32) // 4)
-    assert warps_per_subpartition * 32 * regs <= 16384, (threads, regs)
+    _assert_fits(spec, ptx, tmp_path)
 
 
-@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
-@pytest.mark.parametrize("name", sorted(irgen.bench_kernels()))
-def test_bench_kernel_fits(name, tmp_path):
-    """Every benchmark kernel and its pre-pass kernels fit their launches."""
-    spec = load_kernel_data(*irgen.bench_kernels()[name](), name)
-    ptx = compile_kernel(spec)
+def _assert_fits(spec, ptx, tmp_path):
+    """Assemble ``ptx`` and check every launch it plans (the plan's main and
+    pre-pass kernels, or meta.json's block for a kernel without a plan)."""
     m = re.search(r"// @emmy-plan (\{.*\})", ptx)
     plan = json.loads(m.group(1)) if m else None
     f = tmp_path / "k.ptx"
@@ -81,3 +70,22 @@ def test_bench_kernel_fits(name, tmp_path):
         regs = -(-_main_registers(r.stderr, entry) // 8) * 8
         assert threads * regs <= 65536, (entry, threads, regs)
         assert -(-(threads // 32) // 4) * 32 * regs <= 16384, (entry, threads, regs)
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+@pytest.mark.parametrize("name", sorted(irgen.bench_kernels()))
+def test_bench_kernel_fits(name, tmp_path):
+    """Every benchmark kernel and its pre-pass kernels fit their launches."""
+    spec = load_kernel_data(*irgen.bench_kernels()[name](), name)
+    _assert_fits(spec, compile_kernel(spec), tmp_path)
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+@pytest.mark.parametrize("seed", range(0, 192, 4))
+def test_fuzz_kernel_fits(seed, tmp_path):
+    """A quarter of the family fuzzer's cases, through their template and
+    through the range-checked generic lowering under meta.json's block."""
+    from tests import fuzz_ir
+    c = fuzz_ir.case(seed)
+    for checked in (False, True):
+        _assert_fits(c.spec, compile_kernel(c.spec, checked=checked), tmp_path)
