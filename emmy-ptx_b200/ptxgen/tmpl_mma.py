@@ -25,7 +25,10 @@ K-major) into a launcher-owned workspace.  Kernel (one persistent CTA per SM,
   shared-memory staging buffers (128-byte swizzle) and stored by one thread
   with a TMA tensor store (``cp.reduce.async.bulk.tensor .add`` for split-K
   into the launcher-zeroed C), then the accumulator is handed back --
-  overlapping the next tile's main loop.
+  overlapping the next tile's main loop.  An output the 3xTF32 sum leaves
+  infinite or NaN is recomputed there in plain f32 in K order, so
+  infinities and NaNs come out as the IR's f32 arithmetic gives them
+  (``_emit_nonfinite_fix``).
 
 Every wait is an ``mbarrier.try_wait`` loop bounded by ``%globaltimer``; on
 expiry the kernel raises a shared abort flag and writes ``emmy_err``, every
@@ -47,7 +50,7 @@ import math
 from . import ir
 from .analysis import NoMatch, flat_affine, numel
 from .model import KernelSpec, dtype_info
-from .ptx import Kernel, Module
+from .ptx import Kernel, Module, Reg
 
 PLAN_MAGIC = 0x454D4D59          # "EMMY"
 ERR_WAIT_TIMEOUT = 0x201
@@ -289,8 +292,8 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
         k(f"mov.u32 {dsz}, %dynamic_smem_size")
         k(f"setp.lt.u32 {p}, {dsz}, {dyn_smem}")
         k(f"@{p} bra {simt}")
-        _emit_tc(k, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes, tcols, mt, nt,
-                 units, kblocks)
+        _emit_tc(k, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes, tcols,
+                 mt, nt, units, kblocks)
         k("ret")
     k.place(simt)
     _emit_simt(k, plan, A, B, C, tid, ntid, cta, ncta)
@@ -484,8 +487,103 @@ def _emit_simt(k: Kernel, plan, A, B, C, tid, ntid, cta, ncta):
     k.place(end)
 
 
-def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes, tcols,
-             mt, nt, units, kblocks):
+def _any_nonfinite(k: Kernel, regs: list) -> Reg:
+    """Predicate: some value in ``regs`` is an infinity or a NaN (all
+    exponent bits set)."""
+    m = k.reg("u32")
+    k(f"mov.u32 {m}, 0")
+    for r in regs:
+        t = k.reg("u32")
+        k(f"mov.b32 {t}, {r}")
+        k(f"and.b32 {t}, {t}, 0x7F800000")
+        k(f"max.u32 {m}, {m}, {t}")
+    p = k.reg("pred")
+    k(f"setp.eq.u32 {p}, {m}, 0x7F800000")
+    return p
+
+
+def _emit_nonfinite_fix(k: Kernel, plan, A, B, special, sbuf, rowq, r7, row0, col0, c0, kb):
+    """Outputs the 3xTF32 product leaves non-finite are recomputed as the IR
+    computes them: ``acc = acc + b*a`` over this unit's K range in K order,
+    one rounding per op (``ptxgen/interp.py:196-206``, the m01/m02 loop).
+
+    The split cannot carry an infinity: ``lo = inf - inf`` is NaN, and a
+    zero ``lo`` meets an infinite ``hi`` in a cross term (``inf * 0``), so
+    an output the f32 arithmetic makes +-inf would come out NaN.  Every
+    output an infinite or NaN operand reaches is non-finite after the
+    tensor-core pass (its ``hi.hi`` term already is), so recomputing exactly
+    the non-finite outputs gives the f32 result wherever an operand is not
+    finite; all-finite operands never take this path unless a sum
+    overflows, and then the K-order sum is the IR's own.  A NaN
+    accumulator stops the loop early (it stays NaN).
+
+    The values sit in this thread's row of the staging buffer (16-byte
+    chunk j/4 at (j/4) ^ (row % 8)); the fix rewrites them there before the
+    buffer is stored."""
+    N, K = plan.n, plan.k
+    skip = k.label("nf_skip")
+    k(f"@!{special} bra {skip}")
+    j, off, t, v = k.reg("u32"), k.reg("u32"), k.reg("u32"), k.reg("b32")
+    sa = k.reg("u32")
+    p = k.reg("pred")
+    row, col = k.reg("u32"), k.reg("u32")
+    k(f"add.u32 {row}, {row0}, {rowq}")
+    jl, jn = k.label("nf_j"), k.label("nf_next")
+    k(f"mov.u32 {j}, 0")
+    k.place(jl)
+    k(f"shr.u32 {off}, {j}, 2")
+    k(f"xor.b32 {off}, {off}, {r7}")
+    k(f"shl.b32 {off}, {off}, 4")
+    k(f"and.b32 {t}, {j}, 3")
+    k(f"mad.lo.u32 {off}, {t}, 4, {off}")
+    k(f"mad.lo.u32 {off}, {rowq}, {EPI_COLS * 4}, {off}")
+    k(f"add.u32 {sa}, {sbuf}, {off}")
+    k(f"ld.shared.b32 {v}, [{sa}]")
+    k(f"and.b32 {t}, {v}, 0x7F800000")
+    k(f"setp.ne.u32 {p}, {t}, 0x7F800000")
+    k(f"@{p} bra {jn}")
+    # C[row, col] over K rows kb .. kb + slice_k of this unit
+    k(f"add.u32 {col}, {col0}, {c0}")
+    k(f"add.u32 {col}, {col}, {j}")
+    ia, ib = k.reg("u32"), k.reg("u32")
+    pa, pb = k.reg("u64"), k.reg("u64")
+    k(f"mad.lo.u32 {ia}, {row}, {K}, {kb}")
+    k(f"mad.lo.u32 {ib}, {kb}, {N}, {col}")
+    k(f"mad.wide.u32 {pa}, {ia}, 4, {A}")
+    k(f"mad.wide.u32 {pb}, {ib}, 4, {B}")
+    acc = k.reg("f32")
+    k(f"mov.f32 {acc}, 0f00000000")
+    cnt = k.reg("u32")
+    k(f"mov.u32 {cnt}, 0")
+    kl, kd = k.label("nf_k"), k.label("nf_kdone")
+    k.place(kl)
+    # four products per trip (slice_k is a multiple of 16), loads issued first
+    av, bv = k.regs("f32", 4), k.regs("f32", 4)
+    for e in range(4):
+        k(f"ld.global.nc.f32 {av[e]}, [{pa}+{4 * e}]")
+        k(f"ld.global.nc.f32 {bv[e]}, [{pb}+{4 * N * e}]")
+    pr = k.reg("f32")
+    for e in range(4):
+        k(f"mul.rn.f32 {pr}, {bv[e]}, {av[e]}")
+        k(f"add.rn.f32 {acc}, {acc}, {pr}")
+    k(f"add.u64 {pa}, {pa}, 16")
+    k(f"add.u64 {pb}, {pb}, {16 * N}")
+    k(f"add.u32 {cnt}, {cnt}, 4")
+    k(f"testp.notanumber.f32 {p}, {acc}")
+    k(f"@{p} bra {kd}")
+    k(f"setp.lt.u32 {p}, {cnt}, {plan.slice_k}")
+    k(f"@{p} bra {kl}")
+    k.place(kd)
+    k(f"st.shared.f32 [{sa}], {acc}")
+    k.place(jn)
+    k(f"add.u32 {j}, {j}, 1")
+    k(f"setp.lt.u32 {p}, {j}, {EPI_COLS}")
+    k(f"@{p} bra {jl}")
+    k.place(skip)
+
+
+def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes,
+             tcols, mt, nt, units, kblocks):
     M, N, K = plan.m, plan.n, plan.k
     cx = _Ctx(k)
     k.shared(f"\t.shared .align 8 .b64 bar_full[{STAGES}];")
@@ -695,7 +793,7 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
     k.place(el)
     k(f"setp.ge.u32 {p}, {u4}, {units}")
     k(f"@{p} bra {ee}")
-    tm4, tn4, _ = _decode_unit(k, u4, plan, mt, nt)
+    tm4, tn4, kb4 = _decode_unit(k, u4, plan, mt, nt)
     a4, aph4 = k.reg("u32"), k.reg("u32")
     k(f"and.b32 {a4}, {acc_e}, 1")
     k(f"shr.u32 {aph4}, {acc_e}, 1")
@@ -723,6 +821,7 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
         k(f"add.u32 {tad}, {tbase}, {c * EPI_COLS}")
         k(f"tcgen05.ld.sync.aligned.32x32b.x{EPI_COLS}.b32 {{{', '.join(regs)}}}, [{tad}]")
         k("tcgen05.wait::ld.sync.aligned")
+        special = _any_nonfinite(k, regs)
         # the buffer is free once the store that used it two chunks ago read it
         k(f"@{is_iss} cp.async.bulk.wait_group.read 1")
         k(f"bar.sync 1, {EPI_THREADS}")
@@ -733,6 +832,8 @@ def _emit_tc(k: Kernel, plan, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_byt
             sa = k.reg("u32")
             k(f"add.u32 {sa}, {sbuf}, {swz_off[j]}")
             k(f"st.shared.v4.f32 [{sa}], {{{', '.join(regs[4 * j:4 * j + 4])}}}")
+        _emit_nonfinite_fix(k, plan, A, B, special, sbuf, rowq, r7, row0, col0, c * EPI_COLS,
+                            kb4)
         k("fence.proxy.async.shared::cta")
         k(f"bar.sync 1, {EPI_THREADS}")
         cc = k.reg("u32")
