@@ -1,15 +1,16 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures under ``tests/golden/`` from the reference.
 
-Run where the reference checkout exists (``--ref PATH``; the default is the
-checkout's location in the build container).  It writes:
+Run where the reference checkout exists (``--ref PATH``, required).  It
+writes:
 
 * ``problems/<id>/``: each shipped problem's ``*.ir.json``, ``meta.json`` and
   ``expected.npz`` -- the reference's own golden vectors (numpy float64
   results cast to f32, ``tools/expressions_open.py:52-104``), copied as data;
-* ``special_digests.json``: digests of the reference interpreter's outputs
-  on every recorded IR with NaN, infinities, signed zeros, subnormals and
-  near-overflow values mixed into its inputs (``special_inputs``);
+* ``special_digests.json``, ``special_nonfinite_digests.json``: digests of
+  the reference interpreter's outputs on every recorded IR with NaN,
+  infinities, signed zeros, subnormals and (in the first) near-overflow
+  values mixed into its inputs (``special_inputs``);
 * ``fuzz_digests.json``, ``soup_digests.json``: SHA-256 digests of the
   reference interpreter's outputs on every case of the family fuzzer
   (``tests/fuzz_ir.py``) and of the statement-mix fuzzer
@@ -127,12 +128,22 @@ def generated_cases():
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", choices=["special"],
+                    help="re-record only the special-value digests (every variant) of the "
+                         "recorded IRs in cases.json")
     args = ap.parse_args()
     ref = Path(args.ref)
     if not (ref / "ptxgen" / "interp.py").exists():
         print(f"no reference checkout at {ref}", file=sys.stderr)
         return 2
+    if args.only == "special":
+        ref_interp = import_reference(ref)
+        cases = json.loads((HERE / "cases.json").read_text())
+        for variant in SPECIAL_VARIANTS:
+            n = record_special_digests(ref_interp, cases, variant)
+            print(f"{n} special-value digests written ({variant})")
+        return 0
 
     # 1. copy the shipped problems
     pdst = HERE / "problems"
@@ -196,36 +207,50 @@ def main() -> int:
     print(f"{n} family-fuzzer digests written")
     n = record_fuzz_digests(ref_interp, "fuzz_soup", SOUP_FUZZ_CASES, "soup_digests.json")
     print(f"{n} statement-mix digests written")
-    n = record_special_digests(ref_interp, cases)
-    print(f"{n} special-value digests written")
+    for variant in SPECIAL_VARIANTS:
+        n = record_special_digests(ref_interp, cases, variant)
+        print(f"{n} special-value digests written ({variant})")
     return 0
 
 
 SPECIAL_VALUES = (np.nan, np.inf, -np.inf, -0.0, 1e-40, -1e-40, 3e38, -3e38, 0.0, 1.0)
+# no near-overflow values: no sum of these inputs can overflow, so every
+# output's NaN / +-inf / finite class is fixed by the inputs alone
+NONFINITE_VALUES = (np.nan, np.inf, -np.inf, -0.0, 1e-40, -1e-40, 0.0, 1.0)
+
+# variant -> (values, one element in ``every`` replaced, generator seed)
+SPECIAL_VARIANTS = {"all": (SPECIAL_VALUES, 50, 1), "nonfinite": (NONFINITE_VALUES, 400, 2)}
 
 
-def special_inputs(spec) -> dict[str, np.ndarray]:
-    """``rebuild_inputs(spec, 5000, "normal")`` with one element in 50 of
-    every floating input of 8 or more elements replaced by a special value:
-    NaN, +-inf, -0.0, an f32 subnormal, +-3e38 or 0 and 1 (as stored in the
-    argument's dtype)."""
+def special_inputs(spec, variant: str = "all") -> dict[str, np.ndarray]:
+    """``rebuild_inputs(spec, 5000, "normal")`` with special values mixed
+    into every floating input of 8 or more elements (as stored in the
+    argument's dtype).  Variant ``all``: one element in 50 replaced by NaN,
+    +-inf, -0.0, an f32 subnormal, +-3e38, 0 or 1.  Variant ``nonfinite``:
+    one in 400 replaced by the same values without +-3e38, sparse enough
+    that finite, infinite and NaN outputs all occur in a contraction."""
+    values, every, seed = SPECIAL_VARIANTS[variant]
     inputs = rebuild_inputs(spec, 5000, "normal")
-    rng = np.random.default_rng(1)
-    special = np.array(SPECIAL_VALUES, np.float64)
+    rng = np.random.default_rng(seed)
+    special = np.array(values, np.float64)
     for name, a in inputs.items():
         if spec.args[name].output or a.dtype.kind != "f" or a.size < 8:
             continue
         flat = a.reshape(-1)
-        idx = rng.choice(flat.size, size=max(1, flat.size // 50), replace=False)
+        idx = rng.choice(flat.size, size=max(1, flat.size // every), replace=False)
         with np.errstate(over="ignore"):
             flat[idx] = rng.choice(special, size=idx.size).astype(a.dtype)
     return inputs
 
 
-def record_special_digests(ref_interp, cases) -> int:
-    """``special_digests.json``: the reference interpreter's outputs, as
-    digests, on every recorded IR (shipped and generated) with
-    ``special_inputs``."""
+SPECIAL_FILES = {"all": "special_digests.json", "nonfinite": "special_nonfinite_digests.json"}
+
+
+def record_special_digests(ref_interp, cases, variant: str = "all") -> int:
+    """``special_digests.json`` (variant ``all``) or
+    ``special_nonfinite_digests.json``: the reference interpreter's outputs,
+    as digests, on every recorded IR (shipped and generated) with
+    ``special_inputs(spec, variant)``."""
     out, seen = [], set()
     for c in cases:
         if c["ir"] in seen:
@@ -233,10 +258,10 @@ def record_special_digests(ref_interp, cases) -> int:
         seen.add(c["ir"])
         spec = _case_spec(c)
         with np.errstate(all="ignore"):
-            res = ref_interp.interpret(spec, special_inputs(spec))
+            res = ref_interp.interpret(spec, special_inputs(spec, variant))
         out.append({"case": c["case"], "ir": c["ir"], **({"meta": c["meta"]} if "meta" in c else {}),
                     "outputs": {k: output_digest(v) for k, v in sorted(res.items())}})
-    (HERE / "special_digests.json").write_text(json.dumps(out, indent=1) + "\n")
+    (HERE / SPECIAL_FILES[variant]).write_text(json.dumps(out, indent=1) + "\n")
     return len(out)
 
 

@@ -9,7 +9,9 @@
   interpreter's (``fuzz_digests.json``, ``soup_digests.json``);
 * every recorded IR with special values (NaN, infinities, signed zeros,
   subnormals, near-overflow) in its inputs, against digests of the
-  reference interpreter's outputs (``special_digests.json``).
+  reference interpreter's outputs (``special_digests.json``), and again
+  with a sparser mix without near-overflow values
+  (``special_nonfinite_digests.json``).
 """
 
 import json
@@ -91,22 +93,25 @@ def test_oracle_bit_exact_on_fuzz_cases(rec):
         assert output_digest(outs[name]) == want, name
 
 
-SPECIAL = json.loads((GOLDEN / "special_digests.json").read_text())
+SPECIAL = [dict(d, variant=v) for v, f in (("all", "special_digests.json"),
+                                             ("nonfinite", "special_nonfinite_digests.json"))
+           for d in json.loads((GOLDEN / f).read_text())]
 
 
 def test_special_digests_cover_every_recorded_ir():
-    assert len(SPECIAL) == len({c["ir"] for c in CASES})
+    for v in ("all", "nonfinite"):
+        assert len([d for d in SPECIAL if d["variant"] == v]) == len({c["ir"] for c in CASES})
 
 
-@pytest.mark.parametrize("rec", SPECIAL, ids=[d["case"] for d in SPECIAL])
+@pytest.mark.parametrize("rec", SPECIAL, ids=[f"{d['variant']}-{d['case']}" for d in SPECIAL])
 def test_oracle_bit_exact_on_special_values(rec):
-    """NaN, infinities, signed zeros, subnormals and near-overflow values in
-    the inputs of every recorded IR: the oracle's outputs, NaN payloads
-    included, hash to the reference interpreter's."""
+    """NaN, infinities, signed zeros, subnormals and (variant ``all``)
+    near-overflow values in the inputs of every recorded IR: the oracle's
+    outputs, NaN payloads included, hash to the reference interpreter's."""
     from tests.golden.make_golden import _case_spec, output_digest, special_inputs
     spec = _case_spec(rec)
     with np.errstate(all="ignore"):
-        outs = interpret(spec, special_inputs(spec))
+        outs = interpret(spec, special_inputs(spec, rec["variant"]))
     assert sorted(outs) == sorted(rec["outputs"])
     for name, want in rec["outputs"].items():
         assert output_digest(outs[name]) == want, name
