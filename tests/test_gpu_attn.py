@@ -3,9 +3,10 @@
 * shipped problems against the oracle and ``expected.npz`` under the plan
   launch (tensor cores where the shape tiles, a02) and meta.json's launch
   (the SIMT path that follows the IR per key);
-* generated [B, H, S, D] shapes, f32 (3xTF32, |err| <= 1e-4 of the output
-  scale) and bf16 (bf16 output, |err| <= 2e-2 of the scale), against float64
-  numpy;
+* generated [B, H, S, D] shapes, f32 (3xTF32: per query row max|err| <=
+  1e-4 of the row's max|ref|, ``tests/contraction.py``, which a one-pass
+  TF32 kernel fails) and bf16 (bf16 output, |err| <= 2e-2 of the scale),
+  against float64 numpy;
 * the BASELINE shape [16, 32, 4096, 128] on sampled (batch, head) pairs.
 """
 
@@ -19,8 +20,18 @@ from oracle.interp import interpret, make_inputs
 from ptxgen import irgen
 from ptxgen.loader import load_kernel, load_kernel_data
 
+from tests.contraction import attention_check
+
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).parent / "golden" / "problems"
+
+
+def _close(out, ref, dtype):
+    """f32: the per-row 3xTF32 bound; bf16: 2e-2 of the output scale."""
+    if dtype == "f32":
+        return attention_check(out, ref)
+    worst = float(np.abs(out - ref).max() / np.abs(ref).max())
+    return worst <= 2e-2, worst
 
 
 def _run(spec, inputs, geometry="plan"):
@@ -71,10 +82,8 @@ def test_generated(dtype, shape):
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "att")
     q, k, v = _bhsd(b, h, s, d, dtype)
     out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
-    ref = _ref(q, k, v)
-    scale = np.abs(ref).max()
-    tol = 1e-4 if dtype == "f32" else 2e-2
-    assert np.abs(out - ref).max() <= tol * scale, float(np.abs(out - ref).max() / scale)
+    ok, worst = _close(out, _ref(q, k, v), dtype)
+    assert ok, worst
 
 
 @pytest.mark.parametrize("geometry", ["plan", "meta"])
@@ -90,7 +99,8 @@ def test_tiled_generated(shape, geometry):
         want = interpret(spec, {k: v.copy() for k, v in inputs.items()})["matmul_1"]
         assert np.allclose(got, want, rtol=1e-4, atol=1e-5), float(np.abs(got - want).max())
     ref = _ref(inputs["q"], np.swapaxes(inputs["kt"], 0, 1), inputs["v"])
-    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+    ok, worst = attention_check(got, ref)
+    assert ok, worst
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
@@ -104,9 +114,8 @@ def test_rescale_path(dtype):
     grow = (1.0 + 6.0 * np.arange(s) / s)[None, None, :, None]
     k = (k.astype(np.float64) * grow).astype(k.dtype)
     out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
-    ref = _ref(q, k, v)
-    tol = 1e-4 if dtype == "f32" else 2e-2
-    assert np.abs(out - ref).max() <= tol * np.abs(ref).max()
+    ok, worst = _close(out, _ref(q, k, v), dtype)
+    assert ok, worst
 
 
 def test_bf16_shared_o(monkeypatch):
@@ -140,10 +149,10 @@ def test_baseline_shape_sampled(dtype):
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, dtype), "attbig")
     q, k, v = _bhsd(b, h, s, d, dtype, seed=3)
     out = _run(spec, {"q": q, "k": k, "v": v})["out"]
-    tol = 1e-4 if dtype == "f32" else 2e-2
     for (bi, hi) in ((0, 0), (7, 19), (15, 31)):
         rows = np.arange(0, s, 97)
         qq = q[bi, hi, rows]
         ref = _ref(qq, k[bi, hi], v[bi, hi])
         got = out[bi, hi, rows].astype(np.float64)
-        assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
+        ok, worst = _close(got, ref, dtype)
+        assert ok, (bi, hi, worst)

@@ -120,3 +120,57 @@ def test_reduce_twice_reuses_ticket():
         pk.close()
     assert res[0] == res[1] == res[2]
     assert abs(res[0] - x.astype(np.float64).sum()) <= 1e-5 * x.sum()
+
+
+def test_vector_add_2p28_all_outputs():
+    """BASELINE configs[0] at the bench size: c = a + b over 2**28 f32
+    ~ U[-1,1]; every output bit for bit equal to IEEE f32 a + b (the
+    oracle's own arithmetic for ``add``, bit-exact with it at 2**20)."""
+    n = 1 << 28
+    spec = _spec(irgen.pointwise(n, 4, "add"), "add2p28")
+    rng = np.random.default_rng(0)
+    a = rng.uniform(-1, 1, n).astype(np.float32)
+    b = rng.uniform(-1, 1, n).astype(np.float32)
+    got = _run(spec, {"x0": a, "x1": b})["add"]
+    assert np.array_equal(got, a + b)
+
+
+def _rows_f64(fam, x, g=None, eps=1e-6):
+    x = x.astype(np.float64)
+    if fam == "rmsnorm":
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * g.astype(np.float64)
+    if fam == "l2norm":
+        return x / np.sqrt((x * x).sum(-1, keepdims=True))
+    e = np.exp(x - x.max(-1, keepdims=True))
+    return e / e.sum(-1, keepdims=True)
+
+
+@pytest.mark.parametrize("fam", ["rmsnorm", "softmax", "l2norm"])
+def test_rows_baseline_shape(fam):
+    """BASELINE configs[2] at its full shape, x[65536 x 4096] ~ N(0,1),
+    g ~ N(1, 0.1): every row against float64 numpy (|err| <= 1e-5 |ref| +
+    1e-6 max|ref row|), and 256 rows spread over the matrix against the
+    oracle running the same IR on them (rows are independent)."""
+    rows, cols = 65536, 4096
+    gen = {"rmsnorm": lambda r: irgen.rmsnorm(r, cols, eps=1e-6), "softmax":
+           lambda r: irgen.softmax(r, cols), "l2norm": lambda r: irgen.l2norm(r, cols)}[fam]
+    spec = _spec(gen(rows), fam)
+    rng = np.random.default_rng(3000)
+    x = rng.standard_normal((rows, cols), dtype=np.float32)
+    ins = {"x": x}
+    if fam == "rmsnorm":
+        ins["w"] = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    out = spec.outputs[0]
+    got = _run(spec, ins)[out]
+    for r0 in range(0, rows, 4096):
+        ref = _rows_f64(fam, x[r0:r0 + 4096], ins.get("w"))
+        bound = 1e-5 * np.abs(ref) + 1e-6 * np.abs(ref).max(-1, keepdims=True)
+        assert np.all(np.abs(got[r0:r0 + 4096] - ref) <= bound), r0
+    sel = np.linspace(0, rows - 1, 256).astype(np.int64)
+    sub = _spec(gen(len(sel)), fam + "_rows")
+    sins = make_inputs(sub)
+    sins["x"] = np.ascontiguousarray(x[sel])
+    if fam == "rmsnorm":
+        sins["w"] = ins["w"]
+    want = interpret(sub, sins)[out]
+    assert np.allclose(got[sel], want, rtol=1e-5, atol=1e-7)
