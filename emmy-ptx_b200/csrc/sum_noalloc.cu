@@ -22,10 +22,17 @@
 //     cudaMemsetAsync) before its kernel; calls that overlap on the GPU
 //     (for example on two streams at once) race on the scratch and must be
 //     serialised by the caller;
-//   - the first call on each device performs the set-up: with that device
-//     current it resolves the device address of the array with
-//     cudaGetSymbolAddress (checked) and caches it; make that first call
-//     before any stream capture.
+//   - the first call in each CUDA context performs the set-up: with that
+//     context's device current it resolves the device address of the array
+//     with cudaGetSymbolAddress (checked) and caches it under the context
+//     (the runtime's primary context, or a context the caller created with
+//     the driver API and made current); make that first call before any
+//     stream capture.  The cache is not refreshed after cudaDeviceReset (a
+//     new primary context may reuse the old handle): a process that resets
+//     a device must not call this entry point afterwards;
+//   - failures of CUDA runtime calls return EMMY_ECUDART, with the runtime's
+//     own message in emmy_last_error().
+#include <cuda.h>  // CUcontext and the cuCtxGetCurrent signature only (no libcuda link)
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -46,13 +53,20 @@ constexpr int NOALLOC_PARTIAL_WORD = 64;      // partials start on their own 256
 constexpr int NOALLOC_WORDS = NOALLOC_PARTIAL_WORD + NOALLOC_SLOTS;
 constexpr size_t NOALLOC_MAX_ELEMS = 0x7fffffffu;
 constexpr int NOALLOC_THREADS = 512;
-constexpr int NOALLOC_MAX_DEVICES = 64;
+constexpr int NOALLOC_MAX_CONTEXTS = 64;
 
 // The only memory this entry point uses beyond the caller's buffers.
 static __device__ __align__(256) unsigned int g_noalloc_scratch[NOALLOC_WORDS];
 
+// The array's device address per CUDA context: each context that loads this
+// library's kernels holds its own copy of the array.
+struct ScratchEntry {
+  CUcontext ctx;
+  unsigned int *addr;
+};
 std::mutex g_setup_mu;
-unsigned int *g_scratch_addr[NOALLOC_MAX_DEVICES] = {};
+ScratchEntry g_scratch[NOALLOC_MAX_CONTEXTS] = {};
+int g_scratch_used = 0;
 
 __device__ __forceinline__ float warp_sum(float v) {
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -125,21 +139,54 @@ int set_error(int code, const char *msg) {
   return code;
 }
 
-// Device address of the scratch array for the current device (set-up on the
-// first call per device).
-int scratch_for_current_device(unsigned int **out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
-  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return set_error(EMMY_EINVAL, "device index out of range");
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
-    g_scratch_addr[dev] = static_cast<unsigned int *>(p);
+int runtime_error(cudaError_t e) { return set_error(EMMY_ECUDART, cudaGetErrorString(e)); }
+
+// The context current on this thread, through the runtime's driver entry
+// point (the library does not link libcuda).
+int current_context(CUcontext *ctx) {
+  static CUresult (*get_current)(CUcontext *) = nullptr;
+  if (get_current == nullptr) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000,
+                                                     cudaEnableDefault, &q);
+    if (e != cudaSuccess) return runtime_error(e);
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(EMMY_ECUDART, "cuCtxGetCurrent is not available from the driver");
+    get_current = reinterpret_cast<CUresult (*)(CUcontext *)>(fn);
   }
-  *out = g_scratch_addr[dev];
+  *ctx = nullptr;
+  if (get_current(ctx) != CUDA_SUCCESS)
+    return set_error(EMMY_ECUDART, "cuCtxGetCurrent failed");
+  return EMMY_OK;
+}
+
+// Device address of the scratch array in the current context (set-up on the
+// first call in each context).
+int scratch_for_current_context(unsigned int **out) {
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  CUcontext ctx = nullptr;
+  int rc = current_context(&ctx);
+  if (rc != EMMY_OK) return rc;
+  for (int i = 0; ctx != nullptr && i < g_scratch_used; ++i) {
+    if (g_scratch[i].ctx == ctx) {
+      *out = g_scratch[i].addr;
+      return EMMY_OK;
+    }
+  }
+  // Set-up: resolve the array in the current context.  With no context
+  // current, the runtime makes the current device's primary context current
+  // here, and the entry is kept under that context.
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return runtime_error(e);
+  if (ctx == nullptr) {
+    rc = current_context(&ctx);
+    if (rc != EMMY_OK) return rc;
+  }
+  if (ctx != nullptr && g_scratch_used < NOALLOC_MAX_CONTEXTS)
+    g_scratch[g_scratch_used++] = ScratchEntry{ctx, static_cast<unsigned int *>(p)};
+  *out = static_cast<unsigned int *>(p);
   return EMMY_OK;
 }
 
@@ -150,13 +197,14 @@ extern "C" int emmy_sum_f32_noalloc(emmy_dptr x, size_t n, emmy_dptr out, emmy_s
   if (n == 0 || n > NOALLOC_MAX_ELEMS)
     return set_error(EMMY_EINVAL, "n must be between 1 and 2^31 - 1 elements");
   if (x % 16 != 0) return set_error(EMMY_EINVAL, "x must be 16-byte aligned");
+  if (out % 4 != 0) return set_error(EMMY_EINVAL, "out must be 4-byte aligned");
   unsigned int *scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  int rc = scratch_for_current_context(&scratch);
   if (rc != EMMY_OK) return rc;
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  if (e != cudaSuccess) return runtime_error(e);
   const size_t nvec = (n + 3) / 4;
   size_t grid = (nvec + NOALLOC_THREADS * 8 - 1) / (NOALLOC_THREADS * 8);
   if (grid > size_t(sms) * 4) grid = size_t(sms) * 4;
@@ -165,10 +213,10 @@ extern "C" int emmy_sum_f32_noalloc(emmy_dptr x, size_t n, emmy_dptr out, emmy_s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the ticket must start at zero; the partials are overwritten before use
   e = cudaMemsetAsync(scratch + NOALLOC_TICKET_WORD, 0, sizeof(unsigned int), s);
-  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  if (e != cudaSuccess) return runtime_error(e);
   sum_noalloc_kernel<<<unsigned(grid), NOALLOC_THREADS, 0, s>>>(
       reinterpret_cast<const float *>(x), uint32_t(n), reinterpret_cast<float *>(out), scratch);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(int(e), cudaGetErrorString(e));
+  if (e != cudaSuccess) return runtime_error(e);
   return EMMY_OK;
 }

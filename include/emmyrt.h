@@ -44,7 +44,8 @@ enum {
   EMMY_EINVAL = -3,     /* bad argument */
   EMMY_ENOENTRY = -4,   /* entry point not in module (runner stage "lookup") */
   EMMY_EKERNEL = -5,    /* a kernel reported an error in its error word */
-  EMMY_ESYMBOL = -6     /* module global not found */
+  EMMY_ESYMBOL = -6,    /* module global not found */
+  EMMY_ECUDART = -7     /* a CUDA runtime call failed (emmy_sum_f32_noalloc) */
 };
 
 /* Library identity and the last error message of the calling thread. */
@@ -162,14 +163,18 @@ int emmy_nccl_destroy(emmy_comm *comm);
  * not allocate because the host framework owns all device memory, and
  * latency-critical loops where cudaMalloc's implicit device-wide
  * synchronisation would stall other streams.  *out = sum of the n f32 at x
- * (x 16-byte aligned, 1 <= n <= 2^31 - 1, else EMMY_EINVAL), on `stream`
- * (the CUDA runtime's current device).  It allocates nothing: its scratch is
- * a 4.25 KiB file-scope device array (1024 per-CTA partials + a ticket) held
- * by every GPU that loads this library until exit.  The first call on a
- * device resolves that array's address (cudaGetSymbolAddress) -- make it
- * before any stream capture.  All calls on a device share the array and
- * each clears the ticket first; calls that overlap on the GPU race and must
- * be serialised by the caller. */
+ * (x 16-byte aligned, out 4-byte aligned, 1 <= n <= 2^31 - 1, else
+ * EMMY_EINVAL), on `stream` (the CUDA runtime's current device, in the
+ * context current on the calling thread).  It allocates nothing: its
+ * scratch is a 4.25 KiB file-scope device array (1024 per-CTA partials + a
+ * ticket) held by every GPU that loads this library until exit.  The first
+ * call in each context resolves that array's address (cudaGetSymbolAddress)
+ * -- make it before any stream capture; the resolved address is not
+ * refreshed after cudaDeviceReset, so do not call this after resetting the
+ * device.  All calls on a device share the array and each clears the ticket
+ * first; calls that overlap on the GPU race and must be serialised by the
+ * caller.  A failing CUDA runtime call returns EMMY_ECUDART (its message in
+ * emmy_last_error()), never a raw cudaError_t. */
 int emmy_sum_f32_noalloc(emmy_dptr x, size_t n, emmy_dptr out, emmy_stream stream);
 
 #ifdef __cplusplus
