@@ -1,5 +1,7 @@
 """bench.py's reference arm (the oracle port on every host core, no GPU):
-one JSON line with the contract's keys, ``cores`` the workers it used."""
+one JSON line with the contract's keys, ``cores`` the workers it used.  For
+the default configuration it runs the whole workload (same_config), for
+another workload a bounded sample."""
 
 import json
 import subprocess
@@ -38,3 +40,16 @@ def test_reference_arm_under_torchrun_prints_once():
     assert len(lines) == 1, r.stdout
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
+
+
+def test_reference_arm_full_default_configuration():
+    """The driver's reference arm: the full configs[1] workload split over
+    the host cores, its folded result checked against float64 in-run."""
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                        "--steps", "1", "--warmup", "3"],
+                       capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
+    assert line["config"]["same_config"] is True
+    assert "2^26" in line["config"]["workload"] and line["cpu_baseline"]["kind"] == "port"
