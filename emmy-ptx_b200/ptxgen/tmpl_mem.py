@@ -144,6 +144,43 @@ def grid_stride(k: Kernel, start: str, stride: str, count: int, process, unroll:
     k.place(done)
 
 
+def grid_blocked(k: Kernel, tid: str, ntid: str, cta: str, ncta: str, count: int, process,
+                 unroll: int = 4):
+    """Indices ``0 .. count-1`` in blocks of ``ntid * unroll`` contiguous
+    indices, block b handled by CTA ``b % nctaid`` (a grid-stride loop over
+    blocks): in one trip a thread takes ``b*ntid*unroll + u*ntid + tid`` for
+    every u, so a CTA's loads in flight cover one contiguous block and the
+    grid's cover consecutive blocks.  The partial last block goes one index
+    at a time."""
+    blk, bs, base, last, i = (k.reg("u32") for _ in range(5))
+    p = k.reg("pred")
+    k(f"mul.lo.u32 {bs}, {ntid}, {unroll}")
+    k(f"mov.u32 {blk}, {cta}")
+    lu, tail, tl, done = k.label("gbu"), k.label("gbt"), k.label("gbtl"), k.label("gbdone")
+    k.place(lu)
+    k(f"mad.lo.u32 {base}, {blk}, {bs}, {tid}")
+    k(f"mad.lo.u32 {last}, {ntid}, {unroll - 1}, {base}")
+    k(f"setp.ge.u32 {p}, {last}, {count}")
+    k(f"@{p} bra {tail}")
+    idx = [base]
+    for u in range(1, unroll):
+        r = k.reg("u32")
+        k(f"mad.lo.u32 {r}, {ntid}, {u}, {base}")
+        idx.append(r)
+    process(idx)
+    k(f"add.u32 {blk}, {blk}, {ncta}")
+    k(f"bra.uni {lu}")
+    k.place(tail)
+    k(f"mov.u32 {i}, {base}")
+    k.place(tl)
+    k(f"setp.ge.u32 {p}, {i}, {count}")
+    k(f"@{p} bra {done}")
+    process([i])
+    k(f"add.u32 {i}, {i}, {ntid}")
+    k(f"bra.uni {tl}")
+    k.place(done)
+
+
 # ---------------------------------------------------------------------------
 # pointwise
 # ---------------------------------------------------------------------------
@@ -771,6 +808,10 @@ def _scalar_write_hook(lo: Lowerer, spec, base, row_reg=None, row_stride=None):
 # 45.0 us.  Giving each CTA one contiguous range instead of striding the grid
 # measured 45.3-51.4 us over the same launch shapes.
 FULL_REDUCE_UNROLL = 4
+# "strided": the loads in flight of one thread lie a grid width apart;
+# "blocked": a CTA's loads in flight cover one contiguous block (grid_blocked)
+FULL_REDUCE_LAYOUT = "strided"
+FULL_REDUCE_BLOCK, FULL_REDUCE_PER_SM = 512, 2
 
 
 def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
@@ -854,7 +895,10 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
                 lo.run(lb.loop.body)
                 lo.load_hook = saved
 
-    grid_stride(k, gid, stride, nvec, run_elements, unroll=FULL_REDUCE_UNROLL)
+    if FULL_REDUCE_LAYOUT == "blocked":
+        grid_blocked(k, tid, ntid, cta, ncta, nvec, run_elements, unroll=FULL_REDUCE_UNROLL)
+    else:
+        grid_stride(k, gid, stride, nvec, run_elements, unroll=FULL_REDUCE_UNROLL)
 
     _block_combine(lo, k, ws, "red_slots", None, ident)
 
@@ -929,8 +973,10 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     mod.kernels.append(k)
     # 512 threads x 2 CTAs per SM: measured fastest on B200 for 2^26 f32
     # (43.8 us back to back, against 45.5 with 4 CTAs per SM)
-    mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": 512, "grid_per_sm": 2,
-                "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / 512))), "smem": 0,
+    mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": FULL_REDUCE_BLOCK,
+                "grid_per_sm": FULL_REDUCE_PER_SM,
+                "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / FULL_REDUCE_BLOCK))),
+                "smem": 0,
                 "scratch": {"emmy_part": MAX_PARTIALS * 4, "emmy_ticket": 4}}
     if xg is not None:
         mod.plan["xgpu"] = xg

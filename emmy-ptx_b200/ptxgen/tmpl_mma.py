@@ -176,9 +176,14 @@ def match_matmul(spec: KernelSpec) -> MatmulPlan:
 
 
 class _Ctx:
-    def __init__(self, k: Kernel):
+    """Bounded mbarrier waits.  ``limit``: a register holding the limit in
+    ns (read from a module global the launcher may lower), or None for the
+    fixed ``WAIT_LIMIT_NS``."""
+
+    def __init__(self, k: Kernel, limit: str | None = None):
         self.k = k
         self.abort_label = None
+        self.limit = limit if limit is not None else str(WAIT_LIMIT_NS)
 
     def wait(self, bar_addr: str, parity: str, abort_label: str, code: int = ERR_WAIT_TIMEOUT):
         """Bounded wait for the phase of parity ``parity`` of an mbarrier."""
@@ -201,7 +206,7 @@ class _Ctx:
         k(f"@{p} bra {abort_label}")
         k(f"mov.u64 {t1}, %globaltimer")
         k(f"sub.u64 {t1}, {t1}, {t0}")
-        k(f"setp.gt.u64 {p}, {t1}, {WAIT_LIMIT_NS}")
+        k(f"setp.gt.u64 {p}, {t1}, {self.limit}")
         k(f"@!{p} bra {loop}")
         k(f"st.volatile.shared.u32 [abort_flag], 1")
         k(f"st.global.u32 [emmy_err], {code}")
@@ -263,6 +268,12 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
     mod.add_global(".visible .global .align 8 .u64 emmy_ws;")
     for t in ("ahi", "alo", "bhi", "blo", "c"):
         mod.add_global(f".visible .global .align 64 .b8 tmap_{t}[128];")
+    # the mbarrier wait limit, and a test hook: with emmy_test_stall set, the
+    # MMA issuer first waits on a barrier nothing arrives on, so a test can
+    # make the bounded wait run out (emmy_err 0x201) and check that the
+    # kernel drains, frees TMEM and returns
+    mod.add_global(f".visible .global .align 8 .u64 emmy_wait_ns = {WAIT_LIMIT_NS};")
+    mod.add_global(".visible .global .align 4 .u32 emmy_test_stall;")
     M, N, K = plan.m, plan.n, plan.k
     BN = plan.bn or 32
     a_bytes = BM * BK * 4
@@ -585,12 +596,15 @@ def _emit_nonfinite_fix(k: Kernel, plan, A, B, special, sbuf, rowq, r7, row0, co
 def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes,
              tcols, mt, nt, units, kblocks):
     M, N, K = plan.m, plan.n, plan.k
-    cx = _Ctx(k)
+    wlim = k.reg("u64")
+    k(f"ld.global.u64 {wlim}, [emmy_wait_ns]")
+    cx = _Ctx(k, wlim)
     k.shared(f"\t.shared .align 8 .b64 bar_full[{STAGES}];")
     k.shared(f"\t.shared .align 8 .b64 bar_empty[{STAGES}];")
     k.shared("\t.shared .align 8 .b64 bar_tfull[2];")
     k.shared("\t.shared .align 8 .b64 bar_tempty[2];")
     k.shared("\t.shared .align 8 .b64 bar_drain;")
+    k.shared("\t.shared .align 8 .b64 bar_stall;")
     k.shared("\t.shared .align 4 .u32 tmem_slot;")
     k.shared("\t.shared .align 4 .u32 abort_flag;")
     warp, lane = k.reg("u32"), k.reg("u32")
@@ -625,6 +639,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
         k(f"mbarrier.init.shared::cta.b64 [bar_tfull+{8 * a}], 1")
         k(f"mbarrier.init.shared::cta.b64 [bar_tempty+{8 * a}], {EPI_THREADS}")
     k("mbarrier.init.shared::cta.b64 [bar_drain], 1")
+    k("mbarrier.init.shared::cta.b64 [bar_stall], 1")
     k("st.shared.u32 [abort_flag], 0")
     for t in tmaps.values():
         k(f"prefetch.tensormap [{t}]")
@@ -700,6 +715,14 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     k(f"@{p} bra {role_epi}")
     k(f"setp.ne.u32 {p}, {lane}, 0")
     k(f"@{p} bra {teardown}")
+    stall, nostall = k.reg("u32"), k.label("nostall")
+    k(f"ld.global.u32 {stall}, [emmy_test_stall]")
+    k(f"setp.eq.u32 {p}, {stall}, 0")
+    k(f"@{p} bra {nostall}")
+    sb0 = k.reg("u32")
+    k(f"mov.u32 {sb0}, bar_stall")
+    cx.wait(sb0, "0", abort_l)
+    k.place(nostall)
     kmaj = _desc_const(16, 512, 4)   # K-major, 64-byte swizzle, 8-row groups 512 B apart
     idr = k.reg("u32")
     k(f"mov.u32 {idr}, {_idesc_tf32(BM, BN)}")
