@@ -803,15 +803,22 @@ def _scalar_write_hook(lo: Lowerer, spec, base, row_reg=None, row_stride=None):
     return hook
 
 
-# 16-byte loads in flight per thread in the full reduction's grid-stride loop.
-# Measured on B200 for 2^26 f32 (512 x 2 CTAs per SM): 4 -> 43.4 us; 8 ->
-# 45.0 us.  Giving each CTA one contiguous range instead of striding the grid
-# measured 45.3-51.4 us over the same launch shapes.
+# The full reduction's main loop: 16-byte loads in flight per thread, the
+# layout of a CTA's loads, threads per CTA and CTAs per SM.  Measured on B200
+# for 2^26 f32, back-to-back launches (mean of 100, three passes):
+#   blocked, 4 loads, 512 x 3 CTAs per SM  41.9-42.4 us  (kept)
+#   strided, 4 loads, 512 x 3              42.1-42.6
+#   strided, 4 loads, 512 x 2              43.0-43.2
+#   blocked, 8 loads, 512 x 2 / 256 x 4    42.8-43.1
+#   strided, 4 loads, 512 x 4 / 256 x 8    43.2-44.6
+# One contiguous range per CTA measured 45.3-51.4 us.  Dropping the fence
+# before the last CTA's fold saved at most 0.1 us; it stays.
 FULL_REDUCE_UNROLL = 4
 # "strided": the loads in flight of one thread lie a grid width apart;
 # "blocked": a CTA's loads in flight cover one contiguous block (grid_blocked)
-FULL_REDUCE_LAYOUT = "strided"
-FULL_REDUCE_BLOCK, FULL_REDUCE_PER_SM = 512, 2
+FULL_REDUCE_LAYOUT = "blocked"
+FULL_REDUCE_BLOCK, FULL_REDUCE_PER_SM = 512, 3
+FULL_REDUCE_FENCE = True
 
 
 def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
@@ -937,7 +944,8 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     k(f"@{p} bra {exit_l}")
     # thread 0's ticket acquired every CTA's partial; the barrier and this
     # fence carry that to the threads that read them
-    k("fence.acq_rel.gpu")
+    if FULL_REDUCE_FENCE:
+        k("fence.acq_rel.gpu")
     # the last CTA folds all partials with the IR's combine
     for j, s in enumerate(states):
         lo.bind(s, ident[j])
@@ -971,8 +979,7 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     lo.run(plan.post)
     k.place(exit_l)
     mod.kernels.append(k)
-    # 512 threads x 2 CTAs per SM: measured fastest on B200 for 2^26 f32
-    # (43.8 us back to back, against 45.5 with 4 CTAs per SM)
+    # launch shape: FULL_REDUCE_BLOCK threads x FULL_REDUCE_PER_SM CTAs per SM
     mod.plan = {"entry": spec.entry, "kind": "reduce_full", "block": FULL_REDUCE_BLOCK,
                 "grid_per_sm": FULL_REDUCE_PER_SM,
                 "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / FULL_REDUCE_BLOCK))),
