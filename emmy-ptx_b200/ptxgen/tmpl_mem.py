@@ -544,6 +544,12 @@ XG_MAX_STATES = 4
 XG_FLAGS = 2 * XG_MAX_RANKS * 16
 XG_WAIT_NS = 2_000_000_000
 ERR_PEER_TIMEOUT = 0x203
+# flags: "release" -- one st.release.sys per rank; "fence" -- one
+# fence.acq_rel.sys after the partials, then relaxed system-scope flag stores
+XG_PUBLISH = "release"
+# polling: "acquire" -- ld.acquire.sys per poll; "relaxed" -- ld.relaxed.sys
+# per poll and one fence.acq_rel.sys once every flag has been seen
+XG_POLL = "acquire"
 
 
 def _xgpu_globals(mod: Module) -> dict:
@@ -609,10 +615,16 @@ def _emit_xgpu_exchange(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, ident: list[
                 k(f"st.global.{tt[j]} [{a}+{4 * j}], {lo.env[s].reg}")
         else:
             k(f"add.u64 {a}, {pa}, {foff}")
-            k(f"st.global.release.sys.u32 [{a}], {ep}")
+            if XG_PUBLISH == "fence":
+                k(f"st.global.relaxed.sys.u32 [{a}], {ep}")
+            else:
+                k(f"st.global.release.sys.u32 [{a}], {ep}")
         k(f"add.u32 {i}, {i}, 1")
         k(f"bra.uni {lp}")
         k.place(end)
+        if phase == "val" and XG_PUBLISH == "fence":
+            # one system-scope fence orders every partial before every flag
+            k("fence.acq_rel.sys")
     # wait for every rank's flag of this epoch in the own inbox
     own = k.reg("u64")
     k(f"mad.wide.u32 {own}, {rank}, 8, {peers}")
@@ -630,7 +642,7 @@ def _emit_xgpu_exchange(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, ident: list[
     k(f"add.u64 {a}, {a}, {XG_FLAGS}")
     spin = k.label("xspin")
     k.place(spin)
-    k(f"ld.global.acquire.sys.u32 {f}, [{a}]")
+    k(f"ld.global.{'relaxed' if XG_POLL == 'relaxed' else 'acquire'}.sys.u32 {f}, [{a}]")
     k(f"setp.eq.u32 {p}, {f}, {ep}")
     k(f"@{p} bra {wnext}")
     k(f"mov.u64 {t1}, %globaltimer")
@@ -644,6 +656,8 @@ def _emit_xgpu_exchange(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, ident: list[
     k.place(tout)
     k(f"st.global.u32 [emmy_err], {ERR_PEER_TIMEOUT}")
     k.place(wend)
+    if XG_POLL == "relaxed":
+        k("fence.acq_rel.sys")           # the flags seen order the partials' reads
     # fold the ranks' partials in rank order (a rank that timed out adds
     # whatever its slot holds; the error word reports it)
     for j, s in enumerate(states):
