@@ -740,6 +740,7 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
     }
     for j in jobs:
         if j.inbox is not None:
+            j.pk.detach_peers()       # the module forgets the inbox before it goes
             j.inbox.close()
         for copy in j.rot:
             for p in copy.values():

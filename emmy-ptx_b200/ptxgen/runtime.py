@@ -444,6 +444,23 @@ class PreparedKernel:
             ptr, _ = self.mod.global_ptr(sym)
             self.dev.htod(ptr, arr)
         self.dev.sync()
+        self.peers_attached = True
+
+    def detach_peers(self) -> None:
+        """Leave the multi-GPU exchange: world 0 and no peer addresses in the
+        module.  Modules are shared by every PreparedKernel of the same PTX,
+        so an inbox's addresses must not outlive it there: a later kernel of
+        this PTX would otherwise store into freed or unmapped memory."""
+        x = self.plan.get("xgpu")
+        if not x or not getattr(self, "peers_attached", False):
+            return
+        self.dev.sync()
+        for sym, arr in ((x["world"], np.array([0], np.uint32)),
+                         (x["peers"], np.zeros(int(x["max_ranks"]), dtype=np.uint64))):
+            ptr, _ = self.mod.global_ptr(sym)
+            self.dev.htod(ptr, arr)
+        self.dev.sync()
+        self.peers_attached = False
 
     def upload(self, inputs: dict[str, np.ndarray], stream=None) -> int:
         nbytes = 0
@@ -529,6 +546,7 @@ class PreparedKernel:
         raise EmmyError(msg)
 
     def close(self) -> None:
+        self.detach_peers()
         for p in self.bufs.values():
             self.dev.free(p)
         self.bufs = {}

@@ -102,3 +102,38 @@ def test_matmul_mbarrier_wait_runs_out():
         assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
     finally:
         pk.close()
+
+
+def test_closed_kernel_leaves_no_peer_state():
+    """Modules are shared by every prepared kernel of the same PTX: closing a
+    kernel that joined an exchange resets the module's world and peer
+    addresses, so the next kernel of that PTX runs alone instead of storing
+    into a freed inbox."""
+    from ptxgen.runtime import Device, PreparedKernel
+    dev = Device.get(0)
+    n = 1 << 16
+    spec = load_kernel_data(*irgen.reduce_full(n, pid="xdetach"), "sum_xdetach")
+    x = np.random.default_rng(3).random(n, dtype=np.float32)
+    own, other = dev.alloc(4096), dev.alloc(4096)
+    pk = PreparedKernel(spec, dev=dev)
+    xg = pk.plan["xgpu"]
+    pk.attach_peers(_Inbox([own, other]))
+    pk.close()
+    dev.free(own)
+    dev.free(other)
+    pk2 = PreparedKernel(spec, dev=dev)
+    try:
+        assert pk2.mod is pk.mod
+        world = np.zeros(1, np.uint32)
+        peers = np.ones(int(xg["max_ranks"]), np.uint64)
+        dev.dtoh(world, pk2.mod.global_ptr(xg["world"])[0])
+        dev.dtoh(peers, pk2.mod.global_ptr(xg["peers"])[0])
+        dev.sync()
+        assert world[0] == 0 and not peers.any()
+        pk2.upload({"x": x})
+        pk2.launch()
+        pk2.check_errors()
+        got = float(pk2.download()["sum_1"][0])
+        assert abs(got - float(x.astype(np.float64).sum())) <= 1e-5 * float(x.sum())
+    finally:
+        pk2.close()
