@@ -563,122 +563,115 @@ def _xgpu_globals(mod: Module) -> dict:
 
 def _emit_xgpu_exchange(lo: Lowerer, k: Kernel, ws: ir.WarpShuffle, ident: list[Val],
                         slots: str, world: str | None = None) -> None:
-    """With ``emmy_xworld`` > 1: thread 0 of the CTA holding this rank's
-    total stores it into every rank's inbox over NVLink, raises its flag
-    there (release, system scope) with the launch epoch, waits -- bounded by
-    %globaltimer -- for every rank's flag in its own inbox (acquire), folds
-    the ranks' partials in rank order with the IR's combine (the same result
-    on every rank) and shares it with the CTA through shared memory.
-    ``world``: a register that already holds ``emmy_xworld`` (loaded at the
-    kernel's start, off the critical path)."""
+    """With ``emmy_xworld`` > 1, warp 0 of the CTA holding this rank's total
+    exchanges it with the other ranks, one lane per rank, all in parallel:
+    lane i stores the total into rank i's inbox over NVLink and raises its
+    flag there (release, system scope) with the launch epoch, then waits --
+    bounded by %globaltimer -- for rank i's flag in its own inbox (acquire)
+    and loads rank i's partial.  The warp then folds the ranks' partials in
+    rank order with the IR's combine, passing them along with shuffles (the
+    same result on every rank), and lane 0 shares it with the CTA through
+    shared memory.  ``world``: a register that already holds
+    ``emmy_xworld`` (loaded at the kernel's start, off the critical path).
+
+    One lane per rank keeps the exchange's latency flat in the number of
+    ranks: a single thread publishing and polling rank after rank paid one
+    system-scope release per rank in series."""
     states = list(ws.state)
-    ns = len(states)
     kinds = [lo.env[s].kind for s in states]
     tt = ["f32" if kd == "f32" else "b32" for kd in kinds]
     tid = k.sreg("%tid.x")
     p, q = k.reg("pred"), k.reg("pred")
-    done, bcast = k.label("xdone"), k.label("xbcast")
+    done, bcast, join = k.label("xdone"), k.label("xbcast"), k.label("xjoin")
     if world is None:
         world = k.reg("u32")
         k(f"ld.global.u32 {world}, [emmy_xworld]")
     k(f"setp.le.u32 {p}, {world}, 1")
     k(f"@{p} bra {done}")
     k("bar.sync 0")                           # the CTA's combine reads of the slots are done
-    k(f"setp.ne.u32 {q}, {tid}, 0")
+    k(f"setp.ge.u32 {q}, {tid}, 32")
     k(f"@{q} bra {bcast}")
     rank, ep, par, slot = (k.reg("u32") for _ in range(4))
     k(f"ld.global.u32 {rank}, [emmy_xrank]")
     k(f"ld.global.u32 {ep}, [emmy_xepoch]")
     k(f"add.u32 {ep}, {ep}, 1")
-    k(f"st.global.u32 [emmy_xepoch], {ep}")
+    k("bar.warp.sync -1")                     # every lane has read the old epoch
+    k(f"setp.eq.u32 {p}, {tid}, 0")
+    k(f"@{p} st.global.u32 [emmy_xepoch], {ep}")
     k(f"and.b32 {par}, {ep}, 1")
     k(f"mad.lo.u32 {slot}, {par}, {XG_MAX_RANKS}, {rank}")
-    voff, foff = k.reg("u64"), k.reg("u64")
-    k(f"mul.wide.u32 {voff}, {slot}, 16")
-    k(f"mul.wide.u32 {foff}, {slot}, 4")
-    k(f"add.u64 {foff}, {foff}, {XG_FLAGS}")
-    peers = k.reg("u64")
+    peers, own, pa, a = (k.reg("u64") for _ in range(4))
     k(f"mov.u64 {peers}, emmy_xpeer")
-    # publish the partial states, then the flags
-    i, pa, a = k.reg("u32"), k.reg("u64"), k.reg("u64")
-    for phase in ("val", "flag"):
-        lp, end = k.label(f"x{phase}"), k.label(f"x{phase}end")
-        k(f"mov.u32 {i}, 0")
-        k.place(lp)
-        k(f"setp.ge.u32 {p}, {i}, {world}")
-        k(f"@{p} bra {end}")
-        k(f"mad.wide.u32 {pa}, {i}, 8, {peers}")
-        k(f"ld.global.u64 {pa}, [{pa}]")
-        if phase == "val":
-            k(f"add.u64 {a}, {pa}, {voff}")
-            for j, s in enumerate(states):
-                k(f"st.global.{tt[j]} [{a}+{4 * j}], {lo.env[s].reg}")
-        else:
-            k(f"add.u64 {a}, {pa}, {foff}")
-            if XG_PUBLISH == "fence":
-                k(f"st.global.relaxed.sys.u32 [{a}], {ep}")
-            else:
-                k(f"st.global.release.sys.u32 [{a}], {ep}")
-        k(f"add.u32 {i}, {i}, 1")
-        k(f"bra.uni {lp}")
-        k.place(end)
-        if phase == "val" and XG_PUBLISH == "fence":
-            # one system-scope fence orders every partial before every flag
-            k("fence.acq_rel.sys")
-    # wait for every rank's flag of this epoch in the own inbox
-    own = k.reg("u64")
     k(f"mad.wide.u32 {own}, {rank}, 8, {peers}")
     k(f"ld.global.u64 {own}, [{own}]")
+    vals = [k.reg(kd) for kd in kinds]
+    k(f"setp.ge.u32 {p}, {tid}, {world}")
+    k(f"@{p} bra {join}")
+    # lane i: publish this rank's partial states, then the flag, to rank i
+    k(f"mad.wide.u32 {pa}, {tid}, 8, {peers}")
+    k(f"ld.global.u64 {pa}, [{pa}]")
+    off = k.reg("u64")
+    k(f"mul.wide.u32 {off}, {slot}, 16")
+    k(f"add.u64 {a}, {pa}, {off}")
+    for j, s in enumerate(states):
+        k(f"st.global.{tt[j]} [{a}+{4 * j}], {lo.env[s].reg}")
+    k(f"mul.wide.u32 {off}, {slot}, 4")
+    k(f"add.u64 {a}, {pa}, {off}")
+    if XG_PUBLISH == "fence":
+        k("fence.acq_rel.sys")
+        k(f"st.global.relaxed.sys.u32 [{a}+{XG_FLAGS}], {ep}")
+    else:
+        k(f"st.global.release.sys.u32 [{a}+{XG_FLAGS}], {ep}")
+    # lane i: wait for rank i's flag of this epoch in the own inbox
+    row, f = k.reg("u32"), k.reg("u32")
+    k(f"mad.lo.u32 {row}, {par}, {XG_MAX_RANKS}, {tid}")
+    fa = k.reg("u64")
+    k(f"mad.wide.u32 {fa}, {row}, 4, {own}")
     t0, t1 = k.reg("u64"), k.reg("u64")
     k(f"mov.u64 {t0}, %globaltimer")
-    f, row = k.reg("u32"), k.reg("u32")
-    wl, wnext, wend, tout = k.label("xwait"), k.label("xwnext"), k.label("xwend"), k.label("xtout")
-    k(f"mov.u32 {i}, 0")
-    k.place(wl)
-    k(f"setp.ge.u32 {p}, {i}, {world}")
-    k(f"@{p} bra {wend}")
-    k(f"mad.lo.u32 {row}, {par}, {XG_MAX_RANKS}, {i}")
-    k(f"mad.wide.u32 {a}, {row}, 4, {own}")
-    k(f"add.u64 {a}, {a}, {XG_FLAGS}")
-    spin = k.label("xspin")
+    spin, got, tout = k.label("xspin"), k.label("xgot"), k.label("xtout")
     k.place(spin)
-    k(f"ld.global.{'relaxed' if XG_POLL == 'relaxed' else 'acquire'}.sys.u32 {f}, [{a}]")
+    k(f"ld.global.{'relaxed' if XG_POLL == 'relaxed' else 'acquire'}.sys.u32 {f}, [{fa}+{XG_FLAGS}]")
     k(f"setp.eq.u32 {p}, {f}, {ep}")
-    k(f"@{p} bra {wnext}")
+    k(f"@{p} bra {got}")
     k(f"mov.u64 {t1}, %globaltimer")
     k(f"sub.u64 {t1}, {t1}, {t0}")
     k(f"setp.gt.u64 {p}, {t1}, {XG_WAIT_NS}")
     k(f"@{p} bra {tout}")
     k(f"bra.uni {spin}")
-    k.place(wnext)
-    k(f"add.u32 {i}, {i}, 1")
-    k(f"bra.uni {wl}")
     k.place(tout)
+    # a rank that timed out contributes whatever its slot holds; the error
+    # word reports it
     k(f"st.global.u32 [emmy_err], {ERR_PEER_TIMEOUT}")
-    k.place(wend)
+    k.place(got)
     if XG_POLL == "relaxed":
-        k("fence.acq_rel.sys")           # the flags seen order the partials' reads
-    # fold the ranks' partials in rank order (a rank that timed out adds
-    # whatever its slot holds; the error word reports it)
+        k("fence.acq_rel.sys")               # the flag seen orders the partial's reads
+    va = k.reg("u64")
+    k(f"mad.wide.u32 {va}, {row}, 16, {own}")
+    for j in range(len(states)):
+        k(f"ld.global.relaxed.sys.{tt[j]} {vals[j]}, [{va}+{4 * j}]")
+    k.place(join)
+    k("bar.warp.sync -1")
+    # fold the ranks' partials in rank order (every lane, the same bits)
     for j, s in enumerate(states):
         lo.bind(s, ident[j])
+    i = k.reg("u32")
     fl, fend = k.label("xfold"), k.label("xfoldend")
     k(f"mov.u32 {i}, 0")
     k.place(fl)
     k(f"setp.ge.u32 {p}, {i}, {world}")
     k(f"@{p} bra {fend}")
-    k(f"mad.lo.u32 {row}, {par}, {XG_MAX_RANKS}, {i}")
-    k(f"mad.wide.u32 {a}, {row}, 16, {own}")
     for j, (s, sb) in enumerate(zip(states, ws.state_b)):
         r = k.reg(kinds[j])
-        k(f"ld.global.relaxed.sys.{tt[j]} {r}, [{a}+{4 * j}]")
+        k(f"shfl.sync.idx.b32 {r}, {vals[j]}, {i}, 31, -1")
         lo.bind(sb, Val(r, kinds[j]))
     lo.run(ws.combine_states)
     k(f"add.u32 {i}, {i}, 1")
     k(f"bra.uni {fl}")
     k.place(fend)
+    k(f"setp.eq.u32 {p}, {tid}, 0")
     for j, s in enumerate(states):
-        k(f"st.shared.{tt[j]} [{slots}+{4 * j}], {lo.env[s].reg}")
+        k(f"@{p} st.shared.{tt[j]} [{slots}+{4 * j}], {lo.env[s].reg}")
     k.place(bcast)
     k("bar.sync 0")
     for j, s in enumerate(states):
