@@ -501,7 +501,11 @@ class PreparedKernel:
         # e.g. split-K whose slices one CTA accumulates before a plain store,
         # where 0 + x == x); under meta.json's geometry they are always cleared
         skip = set(self.plan.get("overwrites", [])) if self.geometry != "meta" else set()
-        for name in self.spec.zero_outputs:
+        # and outputs the plan's kernel accumulates into (``zero``: K slices
+        # reduce-added into C)
+        extra = [n for n in self.plan.get("zero", []) if self.geometry != "meta"
+                 and n not in self.spec.zero_outputs]
+        for name in list(self.spec.zero_outputs) + extra:
             if name in skip:
                 continue
             a = self.spec.args[name]

@@ -155,19 +155,58 @@ def match_matmul(spec: KernelSpec) -> MatmulPlan:
     while plan.slices > 1 and (slice_k % BK or slice_k < 4 * BK):
         plan.slices //= 2
         slice_k = k // plan.slices
-    # A CTA accumulates its tile's K slices in TMEM before its one atomic add
-    # (the same sum, another association): keep only as many slice groups as
-    # the SMs need -- at least two waves of units on B200's 148 SMs.
-    if plan.atomic and plan.bn and m % BM == 0:
-        tiles = (m // BM) * (n // plan.bn)
-        while (plan.slices > 1 and plan.slices % 2 == 0
-               and tiles * (plan.slices // 2) >= 2 * SM_COUNT):
-            plan.slices //= 2
-            slice_k = k // plan.slices
+    if plan.bn and m % BM == 0 and k % BK == 0:
+        plan.slices = _choose_slices(k, (m // BM) * (n // plan.bn), plan.slices,
+                                     atomic=plan.atomic)
+        slice_k = k // plan.slices
     plan.slice_k = slice_k
     plan.tc = (m % BM == 0 and plan.bn > 0 and k % 32 == 0 and slice_k % BK == 0
                and m * n < 2 ** 31 and m * k < 2 ** 31 and k * n < 2 ** 31)
     return plan
+
+
+# The longest K range one tensor-memory accumulator sums.  On B200 the
+# kind::tf32 accumulation truncates each MMA's sum, so its error grows with
+# the number of MMAs accumulated: slices of at most MAX_SLICE_K, added
+# into C with f32 TMA reduce-adds (rounded to nearest), keep a K = 8192
+# product near the accuracy of a K = 1024 one.
+MAX_SLICE_K = 1024
+# ... and the shortest K range worth a unit of its own (its epilogue, a
+# 128 x BN TMA reduce-add, must hide behind the next unit's MMAs)
+MIN_SLICE_K = 256
+
+
+def _wave_eff(units: int) -> float:
+    """Fraction of SM slots busy over the waves ``units`` take on 148 SMs."""
+    return units / (math.ceil(units / SM_COUNT) * SM_COUNT)
+
+
+def _choose_slices(k: int, tiles: int, ir_slices: int, atomic: bool) -> int:
+    """How many K slices the units of one C tile take.
+
+    Atomic (split-K) IR: a divisor of its own slice count -- a CTA
+    accumulates a group of the IR's slices in TMEM before its one add (the
+    same sum, another association).  Other IR: any power of two; with more
+    than one slice, C is cleared by the launcher and the slices reduce-add
+    into it.  Among the slice counts whose slices are at most
+    ``MAX_SLICE_K`` long (when any is), the fewest whose units fill the SMs'
+    waves to within 2 % of the best, and at least two waves where the
+    choice allows."""
+    cands = []
+    s = 1
+    limit = ir_slices if atomic else max(1, k // (4 * BK))
+    while s <= limit:
+        if (k % s == 0 and (k // s) % BK == 0 and k // s >= 4 * BK
+                and (atomic or s == 1 or k // s >= MIN_SLICE_K)):
+            cands.append(s)
+        s *= 2
+    if not cands:
+        return ir_slices if atomic else 1
+    short = [c for c in cands if k // c <= MAX_SLICE_K] or cands[-1:]
+    best = max(_wave_eff(tiles * c) for c in short)
+    good = [c for c in short if _wave_eff(tiles * c) >= best - 0.02]
+    two = [c for c in good if tiles * c >= 2 * SM_COUNT]
+    return min(two or good)
 
 
 # ---------------------------------------------------------------------------
@@ -344,6 +383,9 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
             # every C element is written once by a plain TMA store: C needs
             # no clearing before a launch even when the IR adds into it
             plan_d["overwrites"] = [plan.c]
+        elif not plan.atomic:
+            # K slices reduce-add into C: the launcher clears it first
+            plan_d["zero"] = [plan.c]
     mod.plan = plan_d
     return mod
 
@@ -861,7 +903,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
         k(f"bar.sync 1, {EPI_THREADS}")
         cc = k.reg("u32")
         k(f"add.u32 {cc}, {col0}, {c * EPI_COLS}")
-        if plan.atomic and plan.slices > 1:
+        if plan.slices > 1:
             k(f"@{is_iss} cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group "
               f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
         else:

@@ -86,13 +86,14 @@ def test_splitk_generated():
     assert ok, rel
 
 
-@pytest.mark.parametrize("mnk", [(4096, 4096, 512), (256, 256, 1024)])
+@pytest.mark.parametrize("mnk", [(4736, 2048, 512), (256, 256, 1024)])
 def test_splitk_repeated_launches(mnk):
     """Split-K IR adds into a C cleared before every launch.  With the slices
-    grouped into one CTA per tile (4096x4096x512) the kernel stores C in full
-    and the launcher skips the clearing (plan ``overwrites``); with slices
-    spread over CTAs (256x256x1024) it clears C and the kernel reduce-adds.
-    Three launches on the same buffers must each give A.B, not a sum."""
+    grouped into one CTA per tile (4736x2048x512: 296 tiles, two full waves
+    on 148 SMs) the kernel stores C in full and the launcher skips the
+    clearing (plan ``overwrites``); with slices spread over CTAs
+    (256x256x1024) it clears C and the kernel reduce-adds.  Three launches
+    on the same buffers must each give A.B, not a sum."""
     from ptxgen.runtime import PreparedKernel
     m, n, k = mnk
     spec = load_kernel_data(*irgen.matmul_splitk(m, n, k, slice_k=128), "skr")
@@ -101,7 +102,7 @@ def test_splitk_repeated_launches(mnk):
     b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
     pk = PreparedKernel(spec)
     try:
-        assert ("overwrites" in pk.plan) == (m == 4096)
+        assert ("overwrites" in pk.plan) == (m == 4736)
         pk.upload({"x0": a, "x1": b})
         for _ in range(3):
             pk.launch()
@@ -111,6 +112,32 @@ def test_splitk_repeated_launches(mnk):
         pk.close()
     rows = np.random.default_rng(5).choice(m, min(m, 64), replace=False)
     ok, rel = _bound_ok(got, a, b, rows)
+    assert ok, rel
+
+
+def test_sliced_k_repeated_launches():
+    """Non-atomic IR whose K is cut into slices (at most 1024 long, for the
+    tensor core's accumulation error, and enough of them to fill the SMs'
+    waves): the
+    launcher clears C before every launch (plan ``zero``) and the slices
+    reduce-add into it; three launches must each give A.B."""
+    from ptxgen.runtime import PreparedKernel
+    m, n, k = 512, 1024, 8192
+    spec = load_kernel_data(*irgen.matmul(m, n, k), "mmslice")
+    rng = np.random.default_rng(6)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    pk = PreparedKernel(spec)
+    try:
+        assert pk.plan["split_k"] > 1 and pk.plan.get("zero") == ["matmul"]
+        pk.upload({"x0": a, "x1": b})
+        for _ in range(3):
+            pk.launch()
+        pk.check_errors()
+        got = pk.download()["matmul"]
+    finally:
+        pk.close()
+    ok, rel = _bound_ok(got, a, b)
     assert ok, rel
 
 
