@@ -165,15 +165,22 @@ def match_matmul(spec: KernelSpec) -> MatmulPlan:
     return plan
 
 
-# The longest K range one tensor-memory accumulator sums.  On B200 the
-# kind::tf32 accumulation truncates each MMA's sum, so its error grows with
-# the number of MMAs accumulated: slices of at most MAX_SLICE_K, added
-# into C with f32 TMA reduce-adds (rounded to nearest), keep a K = 8192
-# product near the accuracy of a K = 1024 one.
-MAX_SLICE_K = 1024
-# ... and the shortest K range worth a unit of its own (its epilogue, a
-# 128 x BN TMA reduce-add, must hide behind the next unit's MMAs)
-MIN_SLICE_K = 256
+# K slices.  On B200 the kind::tf32 accumulation truncates each MMA's sum,
+# so a C tile's error grows with the number of MMAs it accumulates.  Cutting
+# K into slices of at most EMMY_MATMUL_MAX_SLICE_K (reduce-added into a
+# launcher-cleared C with f32 TMA reduce-adds, rounded to nearest) keeps a
+# K = 8192 product near a K = 1024 one.  Measured on B200, 8192^3: per-16-row
+# max|err| / max|ref| 7.1e-5 unsliced, 1.7e-5 with 4 slices, 8.7e-6 with 8;
+# but 4.18 ms unsliced against 4.79 and 5.10 ms.  Both are inside the
+# 1e-4 contraction bound, so slicing is opt-in (environment variable, read
+# when the kernel is compiled); the default favours speed.
+MIN_SLICE_K = 256     # the shortest K range worth a unit of its own
+
+
+def _max_slice_k() -> int:
+    import os
+    v = os.environ.get("EMMY_MATMUL_MAX_SLICE_K", "").strip()
+    return int(v) if v else 0
 
 
 def _wave_eff(units: int) -> float:
@@ -186,15 +193,15 @@ def _choose_slices(k: int, tiles: int, ir_slices: int, atomic: bool) -> int:
 
     Atomic (split-K) IR: a divisor of its own slice count -- a CTA
     accumulates a group of the IR's slices in TMEM before its one add (the
-    same sum, another association).  Other IR: any power of two; with more
-    than one slice, C is cleared by the launcher and the slices reduce-add
-    into it.  Among the slice counts whose slices are at most
-    ``MAX_SLICE_K`` long (when any is), the fewest whose units fill the SMs'
-    waves to within 2 % of the best, and at least two waves where the
-    choice allows."""
+    same sum, another association) -- the fewest that give every SM a unit
+    (measured: more slices than that only add reduce-add traffic; at 256
+    tiles, 2 slices took 0.088 ms against 0.074 unsliced).  Other IR: one
+    slice, or with ``EMMY_MATMUL_MAX_SLICE_K`` set, the fewest slices no
+    longer than it (C cleared by the launcher, slices reduce-added)."""
+    maxk = _max_slice_k()
     cands = []
     s = 1
-    limit = ir_slices if atomic else max(1, k // (4 * BK))
+    limit = ir_slices if atomic else max(1, k // MIN_SLICE_K)
     while s <= limit:
         if (k % s == 0 and (k // s) % BK == 0 and k // s >= 4 * BK
                 and (atomic or s == 1 or k // s >= MIN_SLICE_K)):
@@ -202,11 +209,13 @@ def _choose_slices(k: int, tiles: int, ir_slices: int, atomic: bool) -> int:
         s *= 2
     if not cands:
         return ir_slices if atomic else 1
-    short = [c for c in cands if k // c <= MAX_SLICE_K] or cands[-1:]
-    best = max(_wave_eff(tiles * c) for c in short)
-    good = [c for c in short if _wave_eff(tiles * c) >= best - 0.02]
-    two = [c for c in good if tiles * c >= 2 * SM_COUNT]
-    return min(two or good)
+    if maxk:
+        short = [c for c in cands if k // c <= maxk]
+        cands = short or cands[-1:]
+    if not atomic:
+        return cands[0] if maxk else 1
+    fill = [c for c in cands if tiles * c >= SM_COUNT]
+    return fill[0] if fill else cands[-1]
 
 
 # ---------------------------------------------------------------------------
