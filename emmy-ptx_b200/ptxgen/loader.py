@@ -62,11 +62,11 @@ def load_kernel_data(data: dict, meta: dict | None, source: str = "<memory>") ->
     graph = ir.Graph.from_dict(data)
     kernels = [n.op for n in graph.nodes.values() if isinstance(n.op, ir.KernelOp)]
     if not kernels:
-        raise ValueError(f"{source}: no KernelOp node in the graph")
+        raise ValueError(f"{source}: the graph holds no KernelOp to compile")
     op = kernels[0]
     entry = op.name or ""
     if not entry:
-        raise ValueError(f"{source}: KernelOp has no entry name")
+        raise ValueError(f"{source}: the KernelOp names no entry point")
 
     kmeta = None
     if meta is not None:
