@@ -50,6 +50,11 @@ from .model import KernelSpec, dtype_info
 from .ptx import Kernel, Module, f32_hex
 from .tmpl_mma import ERR_WAIT_TIMEOUT, PLAN_MAGIC, _Ctx, _desc_const
 
+
+def _late_import():
+    from . import tmpl_attn2q
+    return tmpl_attn2q
+
 LOG2E = 1.4426950408889634
 SMEM_MAX = 232448            # shared memory per CTA, static + dynamic
 XCH_STATIC = 4096            # static shared memory of the two-threads-per-row form
@@ -243,19 +248,26 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     cta, ncta = k.sreg("%ctaid.x"), k.sreg("%nctaid.x")
     p = k.reg("pred")
     simt = k.label("simt")
-    dyn = lay["total"] + 1024
+    # bf16 with D = 128: two query tiles per unit (tmpl_attn2q)
+    tmpl_attn2q = _late_import()
+    two_q = tmpl_attn2q.eligible(plan)
+    dyn = tmpl_attn2q.SMEM_DYN if two_q else lay["total"] + 1024
+    threads = tmpl_attn2q.THREADS if two_q else lay["threads"]
     if plan.tc and dyn <= 232448 - 1024:
         mod.add_global(".extern .shared .align 1024 .b8 dsmem[];")
         flag, dsz = k.reg("u32"), k.reg("u32")
         k(f"ld.global.u32 {flag}, [emmy_plan]")
         k(f"setp.ne.u32 {p}, {flag}, {PLAN_MAGIC}")
         k(f"@{p} bra {simt}")
-        k(f"setp.ne.u32 {p}, {ntid}, {lay['threads']}")
+        k(f"setp.ne.u32 {p}, {ntid}, {threads}")
         k(f"@{p} bra {simt}")
         k(f"mov.u32 {dsz}, %dynamic_smem_size")
         k(f"setp.lt.u32 {p}, {dsz}, {dyn}")
         k(f"@{p} bra {simt}")
-        _emit_tc(k, spec, plan, lay, base, tid, cta, ncta)
+        if two_q:
+            tmpl_attn2q.emit_tc2q(k, spec, plan, base, tid, cta, ncta)
+        else:
+            _emit_tc(k, spec, plan, lay, base, tid, cta, ncta)
         k("ret")
         tc_ok = True
     else:
@@ -271,10 +283,12 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     if tc_ok:
         pre, ws_bytes, tm = _emit_pre(mod, spec, plan, lay)
         plan_d.update({
-            "block": lay["threads"], "grid_per_sm": 1, "grid_max": BH * (S // BQ), "smem": dyn,
+            "block": threads, "grid_per_sm": 1,
+            "grid_max": BH * (S // (2 * BQ if two_q else BQ)), "smem": dyn,
             "workspace": {"sym": "emmy_ws", "bytes": ws_bytes}, "pre": pre, "tmaps": tm,
             "flags": [{"sym": "emmy_plan", "value": PLAN_MAGIC}],
-            "tile": [BQ, plan.bkv, D], "passes": plan.passes,
+            "tile": [2 * BQ if two_q else BQ, plan.bkv, D], "passes": plan.passes,
+            "schedule": "two query tiles" if two_q else "one query tile",
         })
     mod.plan = plan_d
     return mod

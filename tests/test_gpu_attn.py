@@ -86,6 +86,45 @@ def test_generated(dtype, shape):
     assert ok, worst
 
 
+@pytest.mark.parametrize("two_q", ["1", "0"])
+@pytest.mark.parametrize("shape", [(1, 2, 256, 128), (2, 3, 512, 128), (1, 1, 1024, 128)])
+def test_bf16_d128_schedules(shape, two_q, monkeypatch):
+    """bf16 with D = 128 runs the two-query-tile kernel (``tmpl_attn2q``)
+    when S is a multiple of 256, else the one-tile kernel; both forms are
+    checked here at the same shapes (``EMMY_ATTN_2Q=0`` forces one tile)."""
+    monkeypatch.setenv("EMMY_ATTN_2Q", two_q)
+    b, h, s, d = shape
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), f"att2q{two_q}")
+    q, k, v = _bhsd(b, h, s, d, "bf16", seed=21)
+    from ptxgen.runtime import PreparedKernel
+    pk = PreparedKernel(spec)
+    try:
+        want = "two query tiles" if two_q == "1" else "one query tile"
+        assert pk.plan["schedule"] == want
+        pk.upload({"q": q, "k": k, "v": v})
+        for _ in range(2):
+            pk.launch()
+        pk.check_errors()
+        out = pk.download()["out"].astype(np.float64)
+    finally:
+        pk.close()
+    ok, worst = _close(out, _ref(q, k, v), "bf16")
+    assert ok, worst
+
+
+def test_bf16_two_tile_rescale_path():
+    """Keys scaled up along the sequence: every row's max keeps growing, so
+    the two-tile kernel rescales O in TMEM block after block."""
+    b, h, s, d = 1, 2, 2048, 128
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "att2qr")
+    q, k, v = _bhsd(b, h, s, d, "bf16", seed=23)
+    grow = (1.0 + 8.0 * np.arange(s) / s)[None, None, :, None]
+    k = (k.astype(np.float64) * grow).astype(k.dtype)
+    out = _run(spec, {"q": q, "k": k, "v": v})["out"].astype(np.float64)
+    ok, worst = _close(out, _ref(q, k, v), "bf16")
+    assert ok, worst
+
+
 @pytest.mark.parametrize("geometry", ["plan", "meta"])
 @pytest.mark.parametrize("shape", [(96, 64), (128, 32), (256, 128), (512, 64)])
 def test_tiled_generated(shape, geometry):
