@@ -337,6 +337,10 @@ def record_attention(dt, rank, world, strong=True):
 
 
 _SMALL = False
+# The jobs of a record never read what another job (or the previous launch
+# of the same job) writes, so kernels whose plans allow it start while the
+# previous kernel in the stream finishes (programmatic dependent launch).
+OVERLAP = True
 
 RECORDS = {
     "reductions": lambda r, w, s: record_reductions(r, w, s),
@@ -527,6 +531,10 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
         for j in jobs:
             j.stream, j.ev_join = dev.new_stream(), dev.event()
         cfg["streams"] = "one stream per job, forked and joined every step"
+    if OVERLAP and any(j.pk.plan.get("overlap") for j in jobs):
+        cfg["launch"] = ("programmatic dependent launch: kernels whose plan allows it start "
+                         "while the previous one finishes and wait for it before their "
+                         "first write")
     counter = [0]
 
     def rotate():
@@ -543,7 +551,7 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
                 dev.wait_event(j.stream, ev_fork)
                 if j.pk.has_pre:
                     j.pk.launch_pre(j.stream)
-                j.pk.launch_main(j.stream)
+                j.pk.launch_main(j.stream, overlap=OVERLAP)
                 dev.record(j.ev_join, j.stream)
             for j in jobs:
                 dev.wait_event(dev.stream, j.ev_join)
@@ -552,7 +560,7 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
         for i, j in enumerate(jobs):
             if j.pk.has_pre:
                 j.pk.launch_pre()
-            j.pk.launch_main()
+            j.pk.launch_main(overlap=OVERLAP)
             if comm is not None and j.allreduce:
                 pending.append(j)
             if pending and i == last_ar:
@@ -617,7 +625,7 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
     dev.sync()
     for j in jobs:
         batches = ([(j.key + ".pre", j.pk.launch_pre)] if j.pk.has_pre else [])
-        batches.append((j.key, j.pk.launch_main))
+        batches.append((j.key, lambda j=j: j.pk.launch_main(overlap=OVERLAP)))
         for key, launch in batches:
             a, b = dev.event(), dev.event()
             dev.record(a)
@@ -1099,9 +1107,12 @@ def main(argv=None):
                     help="comma-separated job keys to keep in each record (default: all)")
     ap.add_argument("--small", action="store_true",
                     help="reduced shapes (attention: B=1) for profiler captures only")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch every kernel after the previous one completes")
     args = ap.parse_args(argv)
-    global _SMALL
+    global _SMALL, OVERLAP
     _SMALL = args.small
+    OVERLAP = not args.no_overlap
     if args.workload in ALIASES:
         first, *rest = ALIASES[args.workload]
         args.workload = first

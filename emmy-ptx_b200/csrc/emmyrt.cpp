@@ -77,6 +77,7 @@ struct Driver {
   EMMY_FN(cuIpcGetMemHandle)
   EMMY_FN(cuIpcOpenMemHandle)
   EMMY_FN(cuIpcCloseMemHandle)
+  EMMY_FN(cuLaunchKernelEx)  // optional: only launches that overlap their predecessor use it
 #undef EMMY_FN
 };
 
@@ -139,6 +140,8 @@ void load_driver() {
   EMMY_LOAD(cuIpcOpenMemHandle, "cuIpcOpenMemHandle_v2")
   EMMY_LOAD(cuIpcCloseMemHandle, "cuIpcCloseMemHandle")
 #undef EMMY_LOAD
+  g_drv.cuLaunchKernelEx =
+      reinterpret_cast<decltype(g_drv.cuLaunchKernelEx)>(dlsym(h, "cuLaunchKernelEx"));
   if (!all) return;
   CUresult r = g_drv.cuInit(0);
   if (r != CUDA_SUCCESS) {
@@ -422,6 +425,52 @@ int emmy_launch(emmy_mod *mod, const char *entry, const uint32_t grid[3], const 
   CU_TRY(g_drv.cuLaunchKernel(f, grid[0], grid[1], grid[2], block[0], block[1], block[2],
                               smem_bytes, static_cast<CUstream>(stream), args, nullptr),
          "cuLaunchKernel");
+  return EMMY_OK;
+}
+
+int emmy_launch_ex(emmy_mod *mod, const char *entry, const uint32_t grid[3],
+                   const uint32_t block[3], uint32_t smem_bytes, void **args, emmy_stream stream,
+                   uint32_t flags) {
+  if ((flags & ~uint32_t(EMMY_LAUNCH_OVERLAP_PREV)) != 0)
+    return fail(EMMY_EINVAL, "unknown launch flags 0x%x", flags);
+  if (!(flags & EMMY_LAUNCH_OVERLAP_PREV))
+    return emmy_launch(mod, entry, grid, block, smem_bytes, args, stream);
+  if (!mod || !entry || !grid || !block) return fail(EMMY_EINVAL, "null argument");
+  DRV_OR_FAIL();
+  if (!g_drv.cuLaunchKernelEx) return fail(EMMY_ENODRIVER, "libcuda.so.1 lacks cuLaunchKernelEx");
+  CUfunction f;
+  int rc = get_func(mod, entry, &f);
+  if (rc) return rc;
+  if (smem_bytes > 48 * 1024) {
+    auto it = mod->smem_set.find(entry);
+    if (it == mod->smem_set.end() || it->second < int(smem_bytes)) {
+      CU_TRY(g_drv.cuFuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                      int(smem_bytes)),
+             "cuFuncSetAttribute(max dynamic smem)");
+      mod->smem_set[entry] = int(smem_bytes);
+    }
+  }
+  // programmatic stream serialization: this grid may be scheduled once the
+  // previous kernel in the stream has triggered (griddepcontrol.launch_
+  // dependents) instead of once it has completed; the kernel itself waits
+  // (griddepcontrol.wait) before its first write
+  CUlaunchAttribute attr[1];
+  memset(attr, 0, sizeof attr);
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg;
+  memset(&cfg, 0, sizeof cfg);
+  cfg.gridDimX = grid[0];
+  cfg.gridDimY = grid[1];
+  cfg.gridDimZ = grid[2];
+  cfg.blockDimX = block[0];
+  cfg.blockDimY = block[1];
+  cfg.blockDimZ = block[2];
+  cfg.sharedMemBytes = smem_bytes;
+  cfg.hStream = static_cast<CUstream>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CU_TRY(g_drv.cuLaunchKernelEx(&cfg, f, args, nullptr), "cuLaunchKernelEx");
   return EMMY_OK;
 }
 

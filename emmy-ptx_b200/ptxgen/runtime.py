@@ -72,6 +72,8 @@ def load_library():
                               C.POINTER(vp), vp]),
         "emmy_launch_ptrs": (i32, [vp, C.c_char_p, C.POINTER(u32), C.POINTER(u32), u32,
                                    C.POINTER(u64), i32, vp]),
+        "emmy_launch_ex": (i32, [vp, C.c_char_p, C.POINTER(u32), C.POINTER(u32), u32,
+                                 C.POINTER(vp), vp, u32]),
         "emmy_tmap_encode": (i32, [vp, vp]),
         "emmy_tmap_fill": (i32, [vp, C.c_char_p, vp, vp]),
         "emmy_mem_alloc": (i32, [vp, sz, C.POINTER(u64)]),
@@ -309,12 +311,21 @@ class LoadedModule:
         check(self.dev.L.emmy_tmap_fill(self.h, sym.encode(), C.byref(d), self.dev.stream),
               f"tensor map {sym}")
 
-    def launch(self, entry: str, grid, block, smem: int, ptrs: list, stream=None) -> None:
+    def launch(self, entry: str, grid, block, smem: int, ptrs: list, stream=None,
+               overlap: bool = False) -> None:
         """``ptrs``: one kernel argument per parameter, in ``arg_order``: a
         buffer address (int) or a by-value scalar (a ctypes value, the
-        runner's ``"scalar": true`` argument form, ``docs/API.md:49``)."""
+        runner's ``"scalar": true`` argument form, ``docs/API.md:49``).
+        ``overlap``: programmatic dependent launch (``emmy_launch_ex``)."""
         g = (C.c_uint32 * 3)(*[int(x) for x in grid])
         b = (C.c_uint32 * 3)(*[int(x) for x in block])
+        if overlap:
+            vals = [C.c_uint64(p) if isinstance(p, int) else p for p in ptrs]
+            argv = (C.c_void_p * max(1, len(vals)))(
+                *[C.cast(C.pointer(v), C.c_void_p) for v in vals])
+            check(self.dev.L.emmy_launch_ex(self.h, entry.encode(), g, b, int(smem), argv,
+                                            stream or self.dev.stream, 1), f"launch {entry}")
+            return
         if all(isinstance(p, int) for p in ptrs):
             arr = (C.c_uint64 * max(1, len(ptrs)))(*[int(p) for p in ptrs])
             check(self.dev.L.emmy_launch_ptrs(self.h, entry.encode(), g, b, int(smem), arr,
@@ -495,7 +506,11 @@ class PreparedKernel:
         return [self.scalars[n] if n in self.scalars else self.bufs[n]
                 for n in self.spec.arg_order]
 
-    def launch_main(self, stream=None) -> None:
+    def launch_main(self, stream=None, overlap: bool = False) -> None:
+        """The main kernel.  ``overlap``: let it start while the previous
+        kernel in the stream finishes -- taken only when the plan allows it
+        (the kernel waits before its first write); the caller promises that
+        the previous kernel writes none of this kernel's inputs."""
         # zero_outputs are cleared before every launch, except outputs the
         # plan's kernel writes in full without reading them (``overwrites``:
         # e.g. split-K whose slices one CTA accumulates before a plain store,
@@ -511,7 +526,9 @@ class PreparedKernel:
             a = self.spec.args[name]
             self.dev.memset32(self.bufs[name], 0, (a.nbytes + 3) // 4, stream)
         ptrs = self.kernel_args()
-        self.mod.launch(self.spec.entry, self.grid, self.block, self.smem, ptrs, stream)
+        ov = overlap and self.geometry != "meta" and bool(self.plan.get("overlap"))
+        self.mod.launch(self.spec.entry, self.grid, self.block, self.smem, ptrs, stream,
+                        overlap=ov)
         self.launches += 1
 
     def launch(self, stream=None) -> None:

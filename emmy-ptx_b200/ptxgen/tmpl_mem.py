@@ -863,6 +863,9 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
     k("ret")
     k.place(ok)
 
+    # a launch that overlaps its predecessor (emmy_launch_ex) may be
+    # scheduled now: this grid only reads its inputs until the wait below
+    k("griddepcontrol.launch_dependents")
     lo.run(plan.pre)
     lo.seed_accums(lb.loop.body, bool(lb.loop.seed))
     ident = _state_identities(lo, lb.loop.body, states)
@@ -915,6 +918,11 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
         grid_stride(k, gid, stride, nvec, run_elements, unroll=FULL_REDUCE_UNROLL)
 
     _block_combine(lo, k, ws, "red_slots", None, ident)
+    # before the first global write (partials, ticket, exchange, output):
+    # when launched to overlap the previous kernel in the stream, that kernel
+    # -- which may be this one, with the same scratch -- has completed and
+    # its writes are visible (returns at once otherwise)
+    k("griddepcontrol.wait")
 
     # ---- grid level: partials + last-CTA ticket -------------------------
     single = k.label("single")
@@ -991,7 +999,9 @@ def emit_full_reduce(spec: KernelSpec, plan: FullReducePlan) -> Module:
                 "grid_per_sm": FULL_REDUCE_PER_SM,
                 "grid_max": max(1, min(MAX_PARTIALS // ns, math.ceil(nvec / FULL_REDUCE_BLOCK))),
                 "smem": 0,
-                "scratch": {"emmy_part": MAX_PARTIALS * 4, "emmy_ticket": 4}}
+                "scratch": {"emmy_part": MAX_PARTIALS * 4, "emmy_ticket": 4},
+                # the kernel reads only its inputs before griddepcontrol.wait
+                "overlap": True}
     if xg is not None:
         mod.plan["xgpu"] = xg
     return mod

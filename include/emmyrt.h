@@ -85,6 +85,16 @@ int emmy_launch(emmy_mod *mod, const char *entry, const uint32_t grid[3],
 int emmy_launch_ptrs(emmy_mod *mod, const char *entry, const uint32_t grid[3],
                      const uint32_t block[3], uint32_t smem_bytes, const emmy_dptr *ptrs,
                      int nptrs, emmy_stream stream);
+/* emmy_launch with flags.  EMMY_LAUNCH_OVERLAP_PREV: the grid may start
+ * while the previous kernel in `stream` finishes (programmatic dependent
+ * launch).  Only for kernels whose plan declares "overlap" (they wait for
+ * the previous kernel before their first write) and only when none of
+ * their inputs is written by that previous kernel -- the caller's promise.
+ * Replaces the same runner step as emmy_launch; the overlap is new. */
+enum { EMMY_LAUNCH_OVERLAP_PREV = 1 };
+int emmy_launch_ex(emmy_mod *mod, const char *entry, const uint32_t grid[3],
+                   const uint32_t block[3], uint32_t smem_bytes, void **args, emmy_stream stream,
+                   uint32_t flags);
 
 /* ---- TMA tensor maps kept in module globals ---- */
 /* A kernel parameter list is fixed by meta.json arg_order, so tensor maps

@@ -174,3 +174,42 @@ def test_rows_baseline_shape(fam):
         sins["w"] = ins["w"]
     want = interpret(sub, sins)[out]
     assert np.allclose(got[sel], want, rtol=1e-5, atol=1e-7)
+
+
+def test_overlapped_launches_keep_results():
+    """Full reductions launched to overlap the previous kernel in the stream
+    (programmatic dependent launch, ``overlap=True``): a launch starts
+    streaming while the previous one folds, and waits for it before its
+    first write.  Back to back on the same scratch and alternating with
+    another reduction, every result equals the one of a plain launch."""
+    from ptxgen.runtime import Device, PreparedKernel
+    dev = Device.get(0)
+    xs = [np.random.default_rng(40 + i).random(1 << 24, dtype=np.float32) for i in range(2)]
+    pks = []
+    try:
+        for i, x in enumerate(xs):
+            pk = PreparedKernel(_spec(irgen.reduce_full(1 << 24, mean=bool(i)), f"ov{i}"), dev=dev)
+            assert pk.plan.get("overlap")
+            pk.upload({"x": x})
+            pks.append(pk)
+        want = []
+        for pk in pks:
+            pk.launch_main()
+            pk.check_errors()
+            want.append(pk.download())
+        for _ in range(50):
+            for pk in pks:
+                pk.launch_main(overlap=True)
+        for pk in pks * 20:
+            pk.launch_main(overlap=True)
+        for pk in pks:
+            for _ in range(20):
+                pk.launch_main(overlap=True)
+        for pk, w in zip(pks, want):
+            pk.check_errors()
+            got = pk.download()
+            for name in w:
+                assert np.array_equal(got[name], w[name]), name
+    finally:
+        for pk in pks:
+            pk.close()
