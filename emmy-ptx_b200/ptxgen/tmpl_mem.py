@@ -1112,6 +1112,9 @@ def emit_rows(spec: KernelSpec, plan: RowsPlan) -> Module:
 
     tid, ntid, cta, ncta = (k.sreg(s) for s in ("%tid.x", "%ntid.x", "%ctaid.x", "%nctaid.x"))
     _require_whole_warps(k, ntid, mod)
+    # a launch that overlaps its predecessor (emmy_launch_ex) may be
+    # scheduled now: a row only reads until its combine is done
+    k("griddepcontrol.launch_dependents")
     lo.run(plan.pre)
     consts = _preload_consts(lo, spec, base, [lb for lb in (lb1, lb2) if lb is not None])
     row = k.reg("u32")
@@ -1266,6 +1269,9 @@ def emit_rows(spec: KernelSpec, plan: RowsPlan) -> Module:
                                         for (x, b, e) in cache if x == jj}, False)
             k.place(sk)
         _block_combine(lo, k, ws, "row_slots", parity, ident)
+        # before the row's first global write: an overlapped launch's
+        # predecessor has completed (returns at once otherwise)
+        k("griddepcontrol.wait")
         lo.run(plan.mid)
         if lb2 is not None:
             for jj in range(kmax):
@@ -1289,6 +1295,7 @@ def emit_rows(spec: KernelSpec, plan: RowsPlan) -> Module:
     l1_bufs = row_bufs1 + [b for b in col_bufs if b in {c[1] for c in lb1.loads.values()}]
     streamed(lb1, l1_bufs)
     _block_combine(lo, k, ws, "row_slots", parity, ident)
+    k("griddepcontrol.wait")
     lo.run(plan.mid)
     if lb2 is not None:
         l2_bufs = row_bufs2 + [b for b in col_bufs if b in {c[1] for c in lb2.loads.values()}]
@@ -1302,5 +1309,7 @@ def emit_rows(spec: KernelSpec, plan: RowsPlan) -> Module:
     k.place(rend)
     mod.kernels.append(k)
     mod.plan = {"entry": spec.entry, "kind": "rows", "block": blk, "grid_max": R,
-                "grid_per_sm": 0, "smem": 0}
+                "grid_per_sm": 0, "smem": 0,
+                # rows read only their inputs before griddepcontrol.wait
+                "overlap": True}
     return mod

@@ -177,11 +177,12 @@ def test_rows_baseline_shape(fam):
 
 
 def test_overlapped_launches_keep_results():
-    """Full reductions launched to overlap the previous kernel in the stream
-    (programmatic dependent launch, ``overlap=True``): a launch starts
-    streaming while the previous one folds, and waits for it before its
-    first write.  Back to back on the same scratch and alternating with
-    another reduction, every result equals the one of a plain launch."""
+    """Full reductions and row kernels launched to overlap the previous
+    kernel in the stream (programmatic dependent launch, ``overlap=True``):
+    a launch starts reading while the previous one finishes, and waits for
+    it before its first write.  Back to back on the same scratch and outputs
+    and interleaved with each other, every result equals the one of a plain
+    launch."""
     from ptxgen.runtime import Device, PreparedKernel
     dev = Device.get(0)
     xs = [np.random.default_rng(40 + i).random(1 << 24, dtype=np.float32) for i in range(2)]
@@ -191,6 +192,16 @@ def test_overlapped_launches_keep_results():
             pk = PreparedKernel(_spec(irgen.reduce_full(1 << 24, mean=bool(i)), f"ov{i}"), dev=dev)
             assert pk.plan.get("overlap")
             pk.upload({"x": x})
+            pks.append(pk)
+        # a rows kernel (row sums, then an RMSNorm writing a full output) in the mix
+        xr = np.random.default_rng(42).standard_normal((2048, 4096), dtype=np.float32)
+        for gm, nm in ((irgen.reduce_rows(2048, 4096), "ovr"), (irgen.rmsnorm(2048, 4096), "ovn")):
+            pk = PreparedKernel(_spec(gm, nm), dev=dev)
+            assert pk.plan.get("overlap")
+            ins = {"x": xr}
+            if "w" in pk.spec.args:
+                ins["w"] = np.ones(4096, np.float32)
+            pk.upload(ins)
             pks.append(pk)
         want = []
         for pk in pks:
