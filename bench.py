@@ -522,10 +522,12 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
         ev_ready, ev_done = dev.event(), dev.event()
         cfg["collective"] = "NCCL all-reduce on a second stream"
     last_ar = max((i for i, j in enumerate(jobs) if j.allreduce), default=-1)
-    # With the in-kernel exchange each job runs on its own stream (forked from
-    # and joined back to the main stream every step): a reduction's last CTA
-    # waiting for the other GPUs then overlaps the step's other kernels.
-    concurrent = any(j.inbox is not None for j in jobs)
+    # With the in-kernel exchange, a reduction's last CTA waiting for the other
+    # GPUs must overlap the step's other kernels: with overlapped launches the
+    # next kernel in the one stream streams meanwhile; without them each job
+    # runs on its own stream (forked from and joined back to the main stream
+    # every step -- the event waits would break the launches' adjacency).
+    concurrent = any(j.inbox is not None for j in jobs) and not OVERLAP
     if concurrent:
         ev_fork = dev.event()
         for j in jobs:
