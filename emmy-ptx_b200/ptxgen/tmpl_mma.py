@@ -13,12 +13,10 @@ Pre-passes write the TF32 hi/lo halves of A and of B (B transposed to
 K-major) into a launcher-owned workspace.  Kernel (one persistent CTA per SM,
 192 threads):
 
-* warp 0 -- TMA producer (converged, one elected lane issues): per K
-  block of 16, the A hi/lo boxes
+* warp 0, one lane -- TMA producer: per K block of 16, the A hi/lo boxes
   (128x16) and the B hi/lo boxes (BNx16), K-major with the 64-byte swizzle,
   into a 4-stage shared-memory ring, ``mbarrier`` complete_tx;
-* warp 1 -- allocates 2 x BN TMEM columns (two accumulators) and, converged
-  with one elected lane issuing, issues per
+* warp 1 -- allocates 2 x BN TMEM columns (two accumulators) and issues, per
   8-deep K step, three ``tcgen05.mma.cta_group::1.kind::tf32`` (M=128,
   N=BN) reading smem matrix descriptors; ``tcgen05.commit`` frees the stage
   and, after the last K block, publishes the accumulator;
@@ -715,13 +713,11 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     teardown, abort_l = k.label("teardown"), k.label("abort")
     role_mma, role_epi = k.label("rmma"), k.label("repi")
 
-    # ================= producer: warp 0 =================
-    # the whole warp runs the loop (converged, its addresses warp-uniform);
-    # one elected lane issues the copies
+    # ================= producer: warp 0, one lane =================
     k(f"setp.ne.u32 {p}, {warp}, {W_PROD}")
     k(f"@{p} bra {role_mma}")
-    pe = k.reg("pred")
-    k(f"elect.sync _|{pe}, -1")
+    k(f"setp.ne.u32 {p}, {lane}, 0")
+    k(f"@{p} bra {teardown}")
     it, u = k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {it}, 0")
     k(f"mov.u32 {u}, {cta}")
@@ -744,7 +740,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     k(f"xor.b32 {tmp}, {ph}, 1")
     cx.wait(bar("bar_empty", s), tmp, abort_l)
     fb = bar("bar_full", s)
-    k(f"@{pe} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {stage_bytes}")
+    k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {stage_bytes}")
     dst = k.reg("u32")
     k(f"mad.lo.u32 {dst}, {s}, {stage_bytes}, {ring}")
     kc = k.reg("u32")
@@ -753,7 +749,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
                            ("bhi", 2 * a_bytes, rowB), ("blo", 2 * a_bytes + b_bytes, rowB)):
         d2 = k.reg("u32")
         k(f"add.u32 {d2}, {dst}, {off}")
-        k(f"@{pe} cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        k(f"cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
           f"[{d2}], [{tmaps[name]}, {{{kc}, {row}}}], [{fb}]")
     k(f"add.u32 {it}, {it}, 1")
     k(f"add.u32 {kb}, {kb}, 1")
@@ -764,14 +760,12 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     k.place(ue)
     k(f"bra.uni {teardown}")
 
-    # ================= MMA issuer: warp 1 =================
-    # converged warp, one elected lane (lane 0) issues: with lane 0 alone in
-    # the loop every descriptor moves to uniform registers per instruction
+    # ================= MMA issuer: warp 1, one lane =================
     k.place(role_mma)
     k(f"setp.ne.u32 {p}, {warp}, {W_MMA}")
     k(f"@{p} bra {role_epi}")
-    pm = k.reg("pred")
-    k(f"elect.sync _|{pm}, -1")
+    k(f"setp.ne.u32 {p}, {lane}, 0")
+    k(f"@{p} bra {teardown}")
     stall, nostall = k.reg("u32"), k.label("nostall")
     k(f"ld.global.u32 {stall}, [emmy_test_stall]")
     k(f"setp.eq.u32 {p}, {stall}, 0")
@@ -828,17 +822,17 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
             k(f"or.b64 {r}, {r}, 0x{kmaj:016X}")
             d[name] = r
         acc = first if kk == 0 else yes
-        k(f"@{pm} tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['ahi']}, {d['bhi']}, {idr}, {acc}")
-        k(f"@{pm} tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['ahi']}, {d['blo']}, {idr}, {yes}")
-        k(f"@{pm} tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['alo']}, {d['bhi']}, {idr}, {yes}")
+        k(f"tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['ahi']}, {d['bhi']}, {idr}, {acc}")
+        k(f"tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['ahi']}, {d['blo']}, {idr}, {yes}")
+        k(f"tcgen05.mma.cta_group::1.kind::tf32 [{dt}], {d['alo']}, {d['bhi']}, {idr}, {yes}")
     eb = bar("bar_empty", s2)
-    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{eb}]")
+    k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{eb}]")
     k(f"add.u32 {it2}, {it2}, 1")
     k(f"add.u32 {kb2}, {kb2}, 1")
     k(f"setp.lt.u32 {p}, {kb2}, {kblocks}")
     k(f"@{p} bra {mkl}")
     tfb = bar("bar_tfull", a_i)
-    k(f"@{pm} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{tfb}]")
+    k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{tfb}]")
     k(f"add.u32 {acc_it}, {acc_it}, 1")
     k(f"add.u32 {u2}, {u2}, {ncta}")
     k(f"bra.uni {ml}")
