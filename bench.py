@@ -704,10 +704,13 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
     clocks = clk.summary()
     if dom.algo_flops:
         achieved = dom.algo_flops / (dom_ms * 1e-3) / 1e12
-        # a tensor-bound kernel that ran into the power cap is held to the
-        # sustained dense-bf16 figure (cuBLAS over seconds under the cap),
-        # one that did not to the burst figure; both fractions are reported
-        capped = "sw_power_cap" in clocks.get("reasons", [])
+        # a tensor-bound kernel whose clocks the power cap held down (the cap
+        # seen and the median SM clock 5 % or more below the maximum) is held
+        # to the sustained dense-bf16 figure (cuBLAS over seconds under the
+        # cap), any other to the burst figure; both fractions are reported
+        smax = clocks.get("sm_max_mhz") or 0
+        capped = ("sw_power_cap" in clocks.get("reasons", []) and smax
+                  and (clocks.get("sm_mhz") or smax) < 0.95 * smax)
         tf = pk["bf16_tflops_sustained"] if capped else pk["bf16_tflops"]
         which = "sustained" if capped else "burst"
         div = 1.0 if dtype == "bf16" else 6.0
@@ -716,8 +719,9 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
                 "frac_burst": round(achieved / (pk["bf16_tflops"] / div), 4),
                 "frac_sustained": round(achieved / (pk["bf16_tflops_sustained"] / div), 4)}
         if dtype == "bf16":
-            roof["peak_note"] = (f"measured dense bf16, {which} (sw_power_cap "
-                                 f"{'seen' if capped else 'not seen'} in this record's clocks)")
+            roof["peak_note"] = (f"measured dense bf16, {which} (the power cap "
+                                 f"{'held' if capped else 'did not hold'} this record's median "
+                                 f"SM clock below 95 % of the maximum)")
         else:
             # 3xTF32: three TF32 products per useful f32 product; TF32 runs at
             # half the dense bf16 rate, so the useful-flop ceiling is bf16 / 6
