@@ -65,6 +65,12 @@ EPI_ISSUER = 64                  # thread that issues the C stores (warp 2, lane
 W_PROD, W_MMA = 0, 1
 
 
+# A's TF32 hi part is A itself: a kind::tf32 MMA reads only the top 19 bits
+# of each 32-bit operand, so it sees exactly x & 0xffffe000; the pre-pass
+# then writes only A_lo (B must be transposed to K-major anyway).
+RAW_A_HI = True
+
+
 class MatmulPlan:
     pass
 
@@ -379,7 +385,10 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
                 {"entry": f"{spec.entry}_split_b", "block": 256, "grid_per_sm": 8,
                  "grid_max": (K // 32) * (N // 32)},
             ],
-            "tmaps": [tm("tmap_ahi", 0, M, BM), tm("tmap_alo", o_alo, M, BM),
+            "tmaps": [({"sym": "tmap_ahi", "buf": plan.a, "offset": 0, "dtype": "f32",
+                        "dims": [K, M], "strides": [K * 4], "box": [BK, BM], "swizzle": 64}
+                       if RAW_A_HI else tm("tmap_ahi", 0, M, BM)),
+                      tm("tmap_alo", o_alo, M, BM),
                       tm("tmap_bhi", o_bhi, N, BN), tm("tmap_blo", o_blo, N, BN),
                       {"sym": "tmap_c", "buf": plan.c, "offset": 0, "dtype": "f32",
                        "dims": [N, M], "strides": [N * 4], "box": [EPI_COLS, BM],
@@ -428,7 +437,8 @@ def _emit_split_a(spec: KernelSpec, plan) -> Kernel:
     k(f"ld.global.nc.L1::no_allocate.v4.b32 {{{', '.join(x)}}}, [{a}]")
     _split_vec4(k, x, hi, lo)
     w = k.addr(ws, i, 16)
-    k(f"st.global.v4.b32 [{w}], {{{', '.join(hi)}}}")
+    if not RAW_A_HI:
+        k(f"st.global.v4.b32 [{w}], {{{', '.join(hi)}}}")
     k(f"st.global.v4.f32 [{w}+{plan.m * plan.k * 4}], {{{', '.join(lo)}}}")
     k(f"add.u32 {i}, {i}, {st}")
     k(f"bra.uni {lp}")
