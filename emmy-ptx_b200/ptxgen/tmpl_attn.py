@@ -333,8 +333,7 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
             pre.append({"entry": f"{spec.entry}_pre_k", "block": 256, "grid_per_sm": 8,
                         "grid_max": BH * (D // 32) * (S // 32)})
         else:
-            mod.kernels.append(_emit_split_copy(spec, plan, plan.k, off["kh"], off["kl"],
-                                                "_pre_k"))
+            mod.kernels.append(_emit_split_copy(spec, plan, plan.k, None, off["kl"], "_pre_k"))
             pre.append({"entry": f"{spec.entry}_pre_k", "block": 256, "grid_per_sm": 8,
                         "grid_max": max(1, BH * S * D // 4 // 256)})
         mod.kernels.append(_emit_transpose(spec, plan, plan.v, S, D, off["vh"], off["vl"],
@@ -364,7 +363,8 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
         if not lay["q_tmem"]:
             tm += [tmap("tmap_qh", "@ws", off["qh"], D, S, BQ),
                    tmap("tmap_ql", "@ws", off["ql"], D, S, BQ)]
-        tm += [tmap("tmap_kh", "@ws", off["kh"], D, S, plan.bkv),
+        tm += [tmap("tmap_kh", "@ws" if plan.k_trans else plan.k,
+                    off["kh"] if plan.k_trans else 0, D, S, plan.bkv),
                tmap("tmap_kl", "@ws", off["kl"], D, S, plan.bkv),
                tmap("tmap_vh", "@ws", off["vh"], S, D, D), tmap("tmap_vl", "@ws", off["vl"], S, D, D)]
     else:
@@ -376,7 +376,9 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
 
 
 def _emit_split_copy(spec, plan, buf, off_hi, off_lo, suffix) -> Kernel:
-    """x -> (hi, lo) of the same shape (f32)."""
+    """x -> (hi, lo) of the same shape (f32); with ``off_hi`` None only lo
+    (the hi operand is then read from x itself: a kind::tf32 MMA sees only
+    the top 19 bits of each 32-bit value, exactly x & 0xffffe000)."""
     k = Kernel(f"{spec.entry}{suffix}", [(f"p_{n}", ".u64") for n in spec.arg_order])
     X = k.param_ptr(f"p_{buf}")
     ws = k.reg("u64")
@@ -398,7 +400,8 @@ def _emit_split_copy(spec, plan, buf, off_hi, off_lo, suffix) -> Kernel:
         k(f"and.b32 {hi[e]}, {x[e]}, -8192")
         k(f"sub.rn.f32 {lo[e]}, {x[e]}, {hi[e]}")
     w = k.addr(ws, i, 16)
-    k(f"st.global.v4.b32 [{w}+{off_hi}], {{{', '.join(hi)}}}")
+    if off_hi is not None:
+        k(f"st.global.v4.b32 [{w}+{off_hi}], {{{', '.join(hi)}}}")
     k(f"st.global.v4.f32 [{w}+{off_lo}], {{{', '.join(lo)}}}")
     k(f"add.u32 {i}, {i}, {st}")
     k(f"bra.uni {lp}")
