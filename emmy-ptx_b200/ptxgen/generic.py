@@ -23,7 +23,20 @@ under meta.json's launch, with the semantics of the golden model
   loads and shared stores, the commit/wait statements are no-ops and the
   IR's own ``Sync`` orders them;
 * shared-memory buffers are static, or one dynamic pool when meta.json
-  gives a dynamic size, with the XOR swizzle of ``interp.py:578-586``.
+  gives a dynamic size, with the XOR swizzle of ``interp.py:578-586``;
+* ``TmaLoad`` (with its ``TmaDescriptor``) is a real asynchronous copy by the
+  bulk-copy (TMA) engine: one ``cp.async.bulk`` per box row, or per 16-byte
+  chunk under a swizzle, each completing bytes on the IR's mbarrier; parts
+  of the box outside the source are copied from a zeroed module buffer, so
+  every byte arrives through the engine.  No host-built tensor map is
+  needed, so the kernel runs under any launcher.  ``Mbarrier*`` lower to the
+  ``mbarrier`` instructions, the wait bounded by ``%globaltimer`` (2 s,
+  ``emmy_err`` 0x304); a malformed copy (misaligned inner coordinate or
+  destination, box outside its Smem buffer) is skipped with ``emmy_err``
+  0x305 and its bytes completed so no wait is left hanging.  ``SetMaxNReg``
+  lowers to nothing: this lowering does not specialise warps, and the same
+  budget change on every warp of the block can only lower the registers
+  ptxas allotted or, as an increase, wait on registers nobody releases.
 """
 
 from __future__ import annotations
@@ -44,6 +57,31 @@ def _collective(body) -> bool:
 
 
 ERR_OOB = 0x301          # checked mode: an index outside its buffer (access skipped)
+ERR_MBAR_WAIT = 0x304    # an mbarrier wait ran past its limit
+ERR_TMA = 0x305          # a TMA box copy that breaks its alignment or bounds (skipped)
+MBAR_WAIT_NS = 2_000_000_000
+_TMA_SPAN = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}
+
+
+def check_tma_descriptor(d: ir.TmaDescriptor, buf_numel: int, eb: int) -> None:
+    """The limits of a box copy: rank 1..5, box extents 1..256, rows of the
+    view and of the box whole multiples of 16 bytes, a view that stays in its
+    buffer, and under a swizzle a box row exactly the swizzle span."""
+    shape = tuple(int(e) for e in d.src_shape)
+    box = tuple(int(e) for e in d.box_extents)
+    span = _TMA_SPAN.get(str(d.swizzle or "NONE"))
+    if span is None:
+        raise LowerError(f"TMA swizzle {d.swizzle!r}")
+    if not 1 <= len(shape) <= 5 or len(box) != len(shape):
+        raise LowerError("TMA descriptor rank must be 1..5 with a box of the same rank")
+    if min(shape) < 1 or numel(shape) > buf_numel:
+        raise LowerError(f"TMA view {shape} exceeds buffer {d.src_buf!r}")
+    if any(not 1 <= b <= 256 for b in box):
+        raise LowerError("TMA box extents must be 1..256")
+    if (shape[-1] * eb) % 16 or (box[-1] * eb) % 16:
+        raise LowerError("TMA row and box row must be multiples of 16 bytes")
+    if span and box[-1] * eb != span:
+        raise LowerError(f"TMA swizzle {d.swizzle} needs a {span}-byte box row")
 
 
 class Generic:
@@ -77,7 +115,23 @@ class Generic:
             ir.CpAsyncCopy: self.do_cp_async, ir.CpAsyncCommit: lambda st: None,
             ir.CpAsyncWait: lambda st: None, ir.Select: self.do_select,
             ir.ZeroPrologue: self.do_zero_prologue,
+            ir.TmaDescriptor: lambda st: None, ir.TmaLoad: self.do_tma_load,
+            ir.MbarrierInit: self.do_mbar_init, ir.MbarrierArriveExpectTx: self.do_mbar_expect,
+            ir.MbarrierArrive: self.do_mbar_arrive, ir.MbarrierWait: self.do_mbar_wait,
+            ir.SetMaxNReg: lambda st: None,
         }
+        self.tma = {st.name: st for st in ir.walk(spec.op.body)
+                    if isinstance(st, ir.TmaDescriptor)}
+        for d in self.tma.values():
+            if d.src_buf not in spec.args or spec.args[d.src_buf].scalar:
+                raise LowerError(f"TMA descriptor {d.name!r}: no buffer {d.src_buf!r}")
+            a = spec.args[d.src_buf]
+            check_tma_descriptor(d, numel(a.shape), dtype_info(a.dtype)[2])
+        if self.tma:
+            row = max(int(d.box_extents[-1]) * dtype_info(spec.args[d.src_buf].dtype)[2]
+                      for d in self.tma.values())
+            # the source of every box byte outside its view: never written
+            self.mod.add_global(f".visible .global .align 16 .b8 emmy_zeros[{row}];")
         self.smem: dict[str, tuple] = {}     # name -> (shape, dtype, offset)
         self.base: dict[str, str] = {}
 
@@ -99,14 +153,15 @@ class Generic:
         k = self.k
         if not self.smem:
             return
+        al = 1024 if self.tma else 16
         if self.spec.smem_bytes > 0 or off > 48 * 1024:
-            self.mod.add_global(".extern .shared .align 16 .b8 emmy_dyn_smem[];")
+            self.mod.add_global(f".extern .shared .align {al} .b8 emmy_dyn_smem[];")
             self.dyn = True
             r = k.reg("u32")
             k(f"mov.u32 {r}, emmy_dyn_smem")
         else:
             self.dyn = False
-            k.shared(f"\t.shared .align 16 .b8 emmy_smem[{max(16, off)}];")
+            k.shared(f"\t.shared .align {al} .b8 emmy_smem[{max(16, off)}];")
             r = k.reg("u32")
             k(f"mov.u32 {r}, emmy_smem")
         self.smem_base = r
@@ -610,6 +665,212 @@ class Generic:
         k(f"bra {lp}")
         k.place(skip)
         k("barrier.sync 0")
+
+
+    # -- bulk-async transport and mbarriers ----------------------------------
+
+    def mbar_addr(self, name: str, slot) -> str:
+        k = self.k
+        if name not in self.smem or dtype_info(self.smem[name][1])[2] != 8:
+            raise LowerError(f"mbarrier {name!r} is not a Smem array of 8-byte elements")
+        a = k.reg("u32")
+        k(f"add.u32 {a}, {self.smem_base}, {self.smem[name][2]}")
+        if slot is not None:
+            sl = self.lo.coerce(self.lo.ev(slot), "s32")
+            k(f"mad.lo.u32 {a}, {sl.reg}, 8, {a}")
+        return a
+
+    def do_mbar_init(self, st: ir.MbarrierInit) -> None:
+        k = self.k
+        a = self.mbar_addr(st.mbar, st.slot)
+        n = self.lo.coerce(self.lo.ev(st.count) if hasattr(st.count, "free_vars")
+                           else self.lo.const(int(st.count), "s32"), "s32")
+        k(f"{self.guard()}mbarrier.init.shared::cta.b64 [{a}], {n.reg}")
+        # the initialised barrier is visible to the copy engine's completions
+        k("fence.mbarrier_init.release.cluster")
+
+    def do_mbar_expect(self, st: ir.MbarrierArriveExpectTx) -> None:
+        k = self.k
+        a = self.mbar_addr(st.mbar, st.slot)
+        n = self.lo.coerce(self.lo.ev(st.bytes_) if hasattr(st.bytes_, "free_vars")
+                           else self.lo.const(int(st.bytes_), "s32"), "s32")
+        k(f"{self.guard()}mbarrier.arrive.expect_tx.shared::cta.b64 _, [{a}], {n.reg}")
+
+    def do_mbar_arrive(self, st: ir.MbarrierArrive) -> None:
+        a = self.mbar_addr(st.mbar, st.slot)
+        self.k(f"{self.guard()}mbarrier.arrive.shared::cta.b64 _, [{a}]")
+
+    def do_mbar_wait(self, st: ir.MbarrierWait) -> None:
+        """Wait for the completion of phase ``phase`` (parity phase & 1),
+        bounded: past MBAR_WAIT_NS the lane records ERR_MBAR_WAIT and goes on."""
+        k, lo = self.k, self.lo
+        a = self.mbar_addr(st.mbar, st.slot)
+        ph = lo.coerce(lo.ev(st.phase) if hasattr(st.phase, "free_vars")
+                       else lo.const(int(st.phase), "s32"), "s32")
+        par = k.reg("u32")
+        k(f"and.b32 {par}, {ph.reg}, 1")
+        done, loop = k.label("mbw_done"), k.label("mbw")
+        p = k.reg("pred")
+        if lo.mask is not None:
+            k(f"@!{lo.mask} bra {done}")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{a}], {par}")
+        k(f"@{p} bra {done}")
+        t0, t1 = k.reg("u64"), k.reg("u64")
+        k(f"mov.u64 {t0}, %globaltimer")
+        k.place(loop)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{a}], {par}, 100000")
+        k(f"@{p} bra {done}")
+        k(f"mov.u64 {t1}, %globaltimer")
+        k(f"sub.u64 {t1}, {t1}, {t0}")
+        k(f"setp.lt.u64 {p}, {t1}, {MBAR_WAIT_NS}")
+        k(f"@{p} bra {loop}")
+        old = k.reg("u32")
+        k(f"atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_MBAR_WAIT}")
+        k.place(done)
+
+    def do_tma_load(self, st: ir.TmaLoad) -> None:
+        """The box of ``st.desc`` at ``st.coords`` into Smem ``st.smem`` at
+        element ``st.smem_index``, completing its bytes on ``st.mbar``."""
+        k, lo = self.k, self.lo
+        d = self.tma.get(st.desc)
+        if d is None:
+            raise LowerError(f"unknown TMA descriptor {st.desc!r}")
+        if st.smem not in self.smem:
+            raise LowerError(f"TMA destination {st.smem!r} is not a Smem buffer")
+        shape = [int(e) for e in d.src_shape]
+        box = [int(e) for e in d.box_extents]
+        if len(st.coords) != len(shape):
+            raise LowerError("TMA coords and descriptor rank differ")
+        eb = dtype_info(self.spec.args[d.src_buf].dtype)[2]
+        sshape, sdt, soff = self.smem[st.smem]
+        if dtype_info(sdt)[2] != eb:
+            raise LowerError("TMA source and destination element sizes differ")
+        span = _TMA_SPAN[str(d.swizzle or "NONE")]
+        bi, W = box[-1], shape[-1]
+        row_bytes = bi * eb
+        nbox = numel(box)
+        rows = nbox // bi
+        if nbox > numel(sshape):
+            raise LowerError(f"TMA box of {nbox} elements exceeds Smem {st.smem!r}")
+        done = k.label("tma_done")
+        if lo.mask is not None:
+            k(f"@!{lo.mask} bra {done}")
+        coords = [lo.coerce(lo.ev(c), "s32").reg for c in st.coords]
+        idx = st.smem_index if isinstance(st.smem_index, tuple) else (st.smem_index,)
+        dshape = sshape if isinstance(st.smem_index, tuple) else (numel(sshape),)
+        di = self.flat(idx, dshape)
+        bar = self.mbar_addr(st.mbar, st.mbar_slot)
+        dst = k.reg("u32")
+        k(f"mad.lo.u32 {dst}, {di.reg}, {eb}, {self.smem_base}")
+        k(f"add.u32 {dst}, {dst}, {soff}")
+        # checks: inner coordinate on 16 bytes, destination aligned, box inside Smem
+        bad, q = k.reg("pred"), k.reg("pred")
+        t = k.reg("u32")
+        k(f"mul.lo.u32 {t}, {coords[-1]}, {eb}")
+        k(f"and.b32 {t}, {t}, 15")
+        k(f"setp.ne.u32 {bad}, {t}, 0")
+        k(f"and.b32 {t}, {dst}, {(1024 if span else 16) - 1}")
+        k(f"setp.ne.or.u32 {bad}, {t}, 0, {bad}")
+        k(f"setp.gt.u32 {q}, {di.reg}, {numel(sshape) - nbox}")
+        k(f"or.pred {bad}, {bad}, {q}")
+        ok_l = k.label("tma_ok")
+        k(f"@!{bad} bra {ok_l}")
+        old = k.reg("u32")
+        k(f"atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_TMA}")
+        k(f"mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [{bar}], {nbox * eb}")
+        k(f"bra {done}")
+        k.place(ok_l)
+        # generic-proxy accesses to the destination come before the copies
+        k("fence.proxy.async.shared::cta")
+        zeros = k.reg("u64")
+        k(f"mov.u64 {zeros}, emmy_zeros")
+        base = self.base[d.src_buf]
+        # x range of the box that lies inside the view: [lo, hi)
+        xlo, xhi, xend = k.reg("s32"), k.reg("s32"), k.reg("s32")
+        k(f"add.s32 {xend}, {coords[-1]}, {bi}")
+        k(f"max.s32 {xlo}, {coords[-1]}, 0")
+        k(f"min.s32 {xlo}, {xlo}, {xend}")
+        k(f"min.s32 {xhi}, {xend}, {W}")
+        ri = k.reg("u32")
+        k(f"mov.u32 {ri}, 0")
+        head = k.label("tma_row")
+        k.place(head)
+        # outer coordinates of row ri; inside the view?
+        inrow = k.reg("pred")
+        k("setp.eq.u32 {}, 0, 0".format(inrow))
+        rowoff = k.reg("s64")
+        k(f"mov.s64 {rowoff}, 0")
+        rem = k.reg("u32")
+        k(f"mov.u32 {rem}, {ri}")
+        # row-major decode of ri over box[:-1] (innermost outer dim first)
+        outer = []
+        for dim in range(len(shape) - 2, -1, -1):
+            o, oc = k.reg("u32"), k.reg("s32")
+            if dim == 0:
+                k(f"mov.u32 {o}, {rem}")
+            else:
+                k(f"rem.u32 {o}, {rem}, {box[dim]}")
+                k(f"div.u32 {rem}, {rem}, {box[dim]}")
+            k(f"add.s32 {oc}, {coords[dim]}, {o}")
+            k(f"setp.lt.and.u32 {inrow}, {oc}, {shape[dim]}, {inrow}")
+            outer.append((dim, oc))
+        stride = W
+        for dim, oc in outer:          # innermost outer dim first
+            w = k.reg("s64")
+            k(f"mul.wide.s32 {w}, {oc}, {stride}")
+            k(f"add.s64 {rowoff}, {rowoff}, {w}")
+            stride *= shape[dim]
+        lo_r, hi_r = k.reg("s32"), k.reg("s32")
+        k(f"selp.s32 {lo_r}, {xlo}, {coords[-1]}, {inrow}")
+        k(f"selp.s32 {hi_r}, {xhi}, {coords[-1]}, {inrow}")
+        k(f"max.s32 {hi_r}, {hi_r}, {lo_r}")
+        # the source address of element x of this row is base + (rowoff + x) * eb
+        srow = k.reg("u64")
+        k(f"mad.lo.s64 {srow}, {rowoff}, {eb}, {base}")
+        drow = k.reg("u32")
+        k(f"mad.lo.u32 {drow}, {ri}, {row_bytes}, {dst}")
+        cp = "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+        if not span:
+            # zeros [x0, lo), the view's part [lo, hi), zeros [hi, x0 + bi)
+            for a_, b_, from_src in ((coords[-1], lo_r, False), (lo_r, hi_r, True),
+                                     (hi_r, xend, False)):
+                n_, dd, sz = k.reg("s32"), k.reg("u32"), k.reg("u32")
+                skip = k.reg("pred")
+                k(f"sub.s32 {n_}, {b_}, {a_}")
+                k(f"setp.le.s32 {skip}, {n_}, 0")
+                k(f"mul.lo.u32 {sz}, {n_}, {eb}")
+                k(f"sub.s32 {dd}, {a_}, {coords[-1]}")
+                k(f"mad.lo.u32 {dd}, {dd}, {eb}, {drow}")
+                if from_src:
+                    sa = k.reg("u64")
+                    k(f"mad.wide.s32 {sa}, {a_}, {eb}, {srow}")
+                    k(f"@!{skip} {cp} [{dd}], [{sa}], {sz}, [{bar}]")
+                else:
+                    k(f"@!{skip} {cp} [{dd}], [{zeros}], {sz}, [{bar}]")
+        else:
+            m = span // 16 - 1
+            for j in range(row_bytes // 16):
+                # chunk j of the row: inside the view when lo <= x0 + j*16/eb < hi
+                x, o, ph, dd = k.reg("s32"), k.reg("u32"), k.reg("u32"), k.reg("u32")
+                inside, p2 = k.reg("pred"), k.reg("pred")
+                k(f"add.s32 {x}, {coords[-1]}, {j * 16 // eb}")
+                k(f"setp.ge.s32 {inside}, {x}, {lo_r}")
+                k(f"setp.lt.and.s32 {inside}, {x}, {hi_r}, {inside}")
+                k(f"mad.lo.u32 {o}, {ri}, {row_bytes}, {j * 16}")
+                k(f"shr.u32 {ph}, {o}, 7")
+                k(f"and.b32 {ph}, {ph}, {m}")
+                k(f"shl.b32 {ph}, {ph}, 4")
+                k(f"xor.b32 {o}, {o}, {ph}")
+                k(f"add.u32 {dd}, {dst}, {o}")
+                sa = k.reg("u64")
+                k(f"mad.wide.s32 {sa}, {x}, {eb}, {srow}")
+                k(f"selp.b64 {sa}, {sa}, {zeros}, {inside}")
+                k(f"{cp} [{dd}], [{sa}], 16, [{bar}]")
+        k(f"add.u32 {ri}, {ri}, 1")
+        p3 = k.reg("pred")
+        k(f"setp.lt.u32 {p3}, {ri}, {rows}")
+        k(f"@{p3} bra {head}")
+        k.place(done)
 
 
 def emit_generic(spec: KernelSpec, checked: bool = False) -> Module:

@@ -447,6 +447,64 @@ class ZeroPrologue(Node):
     words: int
 
 
+# -- bulk-async transport and mbarriers (starred in the reference's IR table,
+#    ``TASK.md:121-127``; neither its interpreter nor its emitter has them, so
+#    their meaning here is this repository's, stated in ``oracle/interp.py``)
+
+
+@dataclass(repr=False, eq=True)
+class TmaDescriptor(Node):
+    name: str
+    src_buf: str
+    src_shape: tuple
+    box_extents: tuple
+    swizzle: str = "NONE"
+    dtype: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class TmaLoad(Node):
+    smem: str
+    smem_index: Any
+    desc: str
+    coords: tuple
+    mbar: str
+    mbar_slot: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class MbarrierInit(Node):
+    mbar: str
+    count: Any = 1
+    slot: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class MbarrierArriveExpectTx(Node):
+    mbar: str
+    bytes_: Any = 0
+    slot: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class MbarrierArrive(Node):
+    mbar: str
+    slot: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class MbarrierWait(Node):
+    mbar: str
+    phase: Any = 0
+    slot: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class SetMaxNReg(Node):
+    count: int = 0
+    direction: str = "inc"
+
+
 # ---------------------------------------------------------------------------
 # graph level
 # ---------------------------------------------------------------------------
@@ -540,7 +598,8 @@ _CTORS: dict[str, Any] = {
         Dim, ElementwiseImpl, DataType, Var, Literal, BinaryExpr, TernaryExpr, Builtin,
         FuncCallExpr, CastExpr, FlatIndex, Window, Axis, Tile, Load, Assign, Accum, Let, Init,
         Write, Loop, StridedLoop, Cond, Smem, Sync, WarpShuffle, TreeHalve, CpAsyncCopy,
-        CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue,
+        CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue, TmaDescriptor,
+        TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

@@ -20,7 +20,12 @@ re-derives the shape-dependent literals:
                      and its ``[B, H, S, D]`` generalisation with K given
                      untransposed;
 * ``attention_tiled`` -- a01 (the same online softmax, a 4 x 2 output tile
-                     per thread).
+                     per thread);
+* ``tma_box_copy``, ``matmul_tma`` -- kernels written with the bulk-async
+                     transport nodes (``TmaDescriptor``, ``TmaLoad``,
+                     ``Mbarrier*``, ``SetMaxNReg``), which no shipped problem
+                     uses: a box copy with zero fill and swizzle, and the m02
+                     tile schedule fed by box copies instead of ``cp.async``.
 
 At the shipped shapes the generated bodies equal the shipped ones byte for
 byte (``tests/test_irgen.py``); that pins the generator to the reference's
@@ -33,9 +38,10 @@ import json
 import math
 
 from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCopy,
-                 CpAsyncWait, Dim, ElementwiseImpl, Init, Let, Literal, Load, Loop, Smem,
-                 StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var, WarpShuffle, Window,
-                 Write, datatype)
+                 CpAsyncWait, Dim, ElementwiseImpl, Init, Let, Literal, Load, Loop,
+                 MbarrierArriveExpectTx, MbarrierInit, MbarrierWait, SetMaxNReg, Smem,
+                 StridedLoop, Sync, TernaryExpr, Tile, TmaDescriptor, TmaLoad, TreeHalve, Var,
+                 WarpShuffle, Window, Write, datatype)
 
 F32 = datatype("f32")
 
@@ -788,6 +794,140 @@ def attention_bhsd(b: int, h: int, s: int, d: int, dtype: str = "f32",
 # ---------------------------------------------------------------------------
 # the benchmark configurations
 # ---------------------------------------------------------------------------
+
+# ---------------------------------------------------------------------------
+# bulk-async transport: box copies into shared memory under an mbarrier
+# ---------------------------------------------------------------------------
+
+_SMEM_C = {"f32": "float", "f16": "half", "bf16": "__nv_bfloat16", "f64": "double"}
+_EB = {"f32": 4, "f16": 2, "bf16": 2, "f64": 8}
+_MBAR = "unsigned long long"
+
+
+def _tma_issue(tid, loads, nbytes):
+    """Thread ``tid == 0`` announces ``nbytes`` on mbarrier ``bar`` slot 0 and
+    issues the box copies ``loads``."""
+    return Cond(cond=EQ(tid, L(0)),
+                body=(MbarrierArriveExpectTx(mbar="bar", bytes_=L(nbytes), slot=L(0)),) +
+                tuple(loads), else_body=())
+
+
+def _swizzled(e, dtype: str, swizzle: str):
+    """Shared-memory element index of box element ``e`` under a TMA swizzle:
+    byte o moves to o ^ (((o >> 7) & m) << 4)."""
+    span = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}[swizzle]
+    if not span:
+        return e
+    eb = _EB[dtype]
+    sh, cs = 7 - int(math.log2(eb)), 4 - int(math.log2(eb))
+    rowbits = _b("&")(_b(">>")(e, L(sh)), L(span // 16 - 1))
+    return _b("^")(e, _b("<<")(rowbits, L(cs)))
+
+
+def tma_box_copy(rows: int, cols: int, br: int, bc: int, nbr: int, nbc: int, dtype="f32",
+                 swizzle="NONE", off_r=0, off_c=0, threads=128, maxnreg=None, view3=False,
+                 entry="k_tma_box_copy", pid="tma_box_copy"):
+    """out[i*br + r, j*bc + c] = x[i*br + off_r + r, j*bc + off_c + c] (zero
+    outside x): one CTA per (i, j) box; thread 0 initialises the mbarrier,
+    announces the bytes and issues the box copy; every thread waits for phase
+    0, then copies the box out of shared memory (undoing the swizzle).
+    ``view3``: the same copy through a rank-3 view (rows/2, 2, cols) of x
+    and a (br/2, 2, bc) box (rows, br and off_r even)."""
+    eb = _EB[dtype]
+    t = V("t")
+    r0 = ADD(MUL(V("bi"), L(br)), L(off_r))
+    c0 = ADD(MUL(V("bj"), L(bc)), L(off_c))
+    if view3:
+        if rows % 2 or br % 2 or off_r % 2:
+            raise ValueError("view3 needs even rows, br and off_r")
+        view, box = (rows // 2, 2, cols), (br // 2, 2, bc)
+        coords = (ADD(MUL(V("bi"), L(br // 2)), L(off_r // 2)), L(0), c0)
+    else:
+        view, box, coords = (rows, cols), (br, bc), (r0, c0)
+    body = [TmaDescriptor(name="dx", src_buf="x0", src_shape=view, box_extents=box,
+                          swizzle=swizzle, dtype=dtype),
+            Smem(name="tile", extents=(br * bc,), dtype=_SMEM_C[dtype], align=1024),
+            Smem(name="bar", extents=(1,), dtype=_MBAR, align=8)]
+    if maxnreg:
+        body.append(SetMaxNReg(count=maxnreg, direction="dec"))
+    body += [
+        Cond(cond=EQ(t, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
+             else_body=()),
+        Sync(barrier_id=0, count=None, warp=False),
+        _tma_issue(t, [TmaLoad(smem="tile", smem_index=L(0), desc="dx", coords=coords,
+                               mbar="bar", mbar_slot=L(0))], br * bc * eb),
+        MbarrierWait(mbar="bar", phase=L(0), slot=L(0)),
+        strided("e", br * bc, t, L(threads), [
+            Load(names=("v",), input="tile", index=(_swizzled(V("e"), dtype, swizzle),),
+                 dtype=None),
+            write("out", (ADD(MUL(V("bi"), L(br)), DIV(V("e"), L(bc))),
+                          ADD(MUL(V("bj"), L(bc)), MOD(V("e"), L(bc)))), "v",
+                  dtype=datatype(dtype))]),
+    ]
+    tl = tile([ax("bi", nbr), ax("bj", nbc), ax("t", threads)], body, block_threads=threads)
+    return package(entry, "copy", [tl], [("x0", (rows, cols), dtype, 0)], [],
+                   ("out", (nbr * br, nbc * bc), dtype), ["x0", "out"], (nbr * nbc, 1, 1),
+                   (threads, 1, 1), rtol=0.0, atol=0.0, pid=pid)
+
+
+def matmul_tma(m: int, n: int, k: int, entry="k_matmul_tma", pid="matmul_tma"):
+    """C = A.B with m02's 16x32 tile, 8x32 threads and K step of 8, each K
+    step's A (16x8) and B (8x32) boxes brought by two box copies that
+    complete on one mbarrier (phase = step number); the products are summed
+    in K order per output as in m02, and C is written once (no slices)."""
+    BM, BN, BK, TH = 16, 32, 8, 256
+    if m % BM or n % BN or k % BK:
+        raise ValueError("matmul_tma shape must tile by 16x32 with K a multiple of 8")
+    tidl = ADD(MUL(V("a0_u"), L(32)), V("a1_u"))
+    body = [Init(name="acc0__c0_0", identity=0.0, dtype=F32),
+            Init(name="acc0__c1_0", identity=0.0, dtype=F32),
+            TmaDescriptor(name="dA", src_buf="x0", src_shape=(m, k), box_extents=(BM, BK),
+                          swizzle="NONE", dtype="f32"),
+            TmaDescriptor(name="dB", src_buf="x1", src_shape=(k, n), box_extents=(BK, BN),
+                          swizzle="NONE", dtype="f32"),
+            Smem(name="_a_smem", extents=(BM, BK), dtype="float", align=128),
+            Smem(name="_b_smem", extents=(BK, BN), dtype="float", align=128),
+            Smem(name="bar", extents=(1,), dtype=_MBAR, align=8),
+            Cond(cond=EQ(tidl, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
+                 else_body=()),
+            Sync(barrier_id=0, count=None, warp=False)]
+
+    def bcol():
+        return V("a1_u")
+
+    def arow(i):
+        return ADD(MUL(V("a0_u"), L(2)), L(i))
+
+    ki = [Load(names=("in1__c0_0",), input="_b_smem", index=(V("_ki"), bcol()), dtype=None),
+          Load(names=("in0__c0_0",), input="_a_smem", index=(arow(0), V("_ki")), dtype=None),
+          assign("acc0__v__c0_0", "multiply", "in1__c0_0", "in0__c0_0"),
+          accum("acc0__c0_0", "acc0__v__c0_0", "add", ("_ki",)),
+          Load(names=("in0__c1_0",), input="_a_smem", index=(arow(1), V("_ki")), dtype=None),
+          assign("acc0__v__c1_0", "multiply", "in1__c0_0", "in0__c1_0"),
+          accum("acc0__c1_0", "acc0__v__c1_0", "add", ("_ki",))]
+    copies = [TmaLoad(smem="_a_smem", smem_index=L(0), desc="dA",
+                      coords=(MUL(V("a0_b"), L(BM)), V("_ks")), mbar="bar", mbar_slot=L(0)),
+              TmaLoad(smem="_b_smem", smem_index=L(0), desc="dB",
+                      coords=(V("_ks"), MUL(V("a1_b"), L(BN))), mbar="bar", mbar_slot=L(0))]
+    ks = [_tma_issue(tidl, copies, (BM * BK + BK * BN) * 4),
+          MbarrierWait(mbar="bar", phase=DIV(V("_ks"), L(BK)), slot=L(0)),
+          loop("_ki", BK, ki, unroll=True, seed=False),
+          Sync(barrier_id=0, count=None, warp=False)]
+    body.append(strided("_ks", k, L(0), L(BK), ks))
+
+    def orow(i):
+        return ADD(ADD(MUL(V("a0_b"), L(BM)), MUL(V("a0_u"), L(2))), L(i))
+
+    ocol = ADD(MUL(V("a1_b"), L(BN)), V("a1_u"))
+    body.append(write("matmul", (orow(0), ocol), "acc0__c0_0"))
+    body.append(write("matmul", (orow(1), ocol), "acc0__c1_0"))
+    t = tile([ax("a0_b", m // BM, win("a0", m)), ax("a1_b", n // BN, win("a1", n)),
+              ax("a0_u", 8), ax("a1_u", 32)], body, block_threads=TH)
+    return package(entry, "matmul", [t], [("x0", (m, k), "f32", 0), ("x1", (k, n), "f32", 1)],
+                   [], ("matmul", (m, n), "f32"), ["x1", "x0", "matmul"],
+                   ((m // BM) * (n // BN), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid,
+                   kernel_inputs=["x1", "x0"])
+
 
 def bench_kernels():
     """IR + meta for every BASELINE configuration, keyed by a short name."""

@@ -307,6 +307,40 @@ def swizzle_index(flat: np.ndarray, mode) -> np.ndarray:
     return flat ^ (((flat >> shift) & mask) << 3)
 
 
+_TMA_SWIZZLE = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}
+
+
+def tma_check_descriptor(d, buf_numel: int, eb: int) -> None:
+    """The limits a TmaDescriptor must meet (the TMA unit's, plus a view
+    that stays inside its buffer)."""
+    shape = tuple(int(e) for e in d.src_shape)
+    box = tuple(int(e) for e in d.box_extents)
+    span = _TMA_SWIZZLE.get(str(d.swizzle or "NONE"))
+    if span is None:
+        raise ValueError(f"TMA swizzle {d.swizzle!r}")
+    if not 1 <= len(shape) <= 5 or len(box) != len(shape):
+        raise ValueError("TMA descriptor rank must be 1..5 with a box of the same rank")
+    if int(np.prod(shape)) > buf_numel or min(shape) < 1:
+        raise ValueError(f"TMA view {shape} exceeds buffer {d.src_buf!r}")
+    if any(not 1 <= b <= 256 for b in box):
+        raise ValueError("TMA box extents must be 1..256")
+    if (shape[-1] * eb) % 16 or (box[-1] * eb) % 16:
+        raise ValueError("TMA row and box row must be multiples of 16 bytes")
+    if span and box[-1] * eb != span:
+        raise ValueError(f"TMA swizzle {d.swizzle} needs a {span}-byte box row")
+
+
+def tma_swizzle_perm(box, eb: int, swizzle):
+    """Element position of each box element in shared memory under a TMA
+    swizzle (None without one): byte o goes to o ^ (((o >> 7) & m) << 4)."""
+    span = _TMA_SWIZZLE[str(swizzle or "NONE")]
+    if not span:
+        return None
+    m = span // 16 - 1
+    o = np.arange(int(np.prod(box)), dtype=np.int64) * eb
+    return (o ^ (((o >> 7) & m) << 4)) // eb
+
+
 def _kind(dtype) -> str:
     k = dtype_info(dtype)[0]
     return "f32" if k == "bf16" else k
@@ -345,7 +379,13 @@ class Machine:
             ir.CpAsyncCopy: self.do_cp_async, ir.CpAsyncCommit: self.do_nothing,
             ir.CpAsyncWait: self.do_nothing, ir.Select: self.do_select,
             ir.ZeroPrologue: self.do_zero_prologue,
+            ir.TmaDescriptor: self.do_nothing, ir.TmaLoad: self.do_tma_load,
+            ir.MbarrierInit: self.do_mbarrier, ir.MbarrierArriveExpectTx: self.do_mbarrier,
+            ir.MbarrierArrive: self.do_mbarrier, ir.MbarrierWait: self.do_mbarrier,
+            ir.SetMaxNReg: self.do_nothing,
         }
+        self.tma_descs = {st.name: st for st in ir.walk(spec.op.body)
+                          if isinstance(st, ir.TmaDescriptor)}
 
     # -- lane state -------------------------------------------------------
 
@@ -792,6 +832,86 @@ class Machine:
             c = truthy(self.ev(b.select))
             res = Val(kind, np.where(c, coerce(self.env[b.value], kind).a, coerce(res, kind).a))
         self.bind(st.name, res)
+
+    # -- bulk-async transport and mbarriers --------------------------------
+    # Starred in the reference's IR table (``TASK.md:121-127``) and absent
+    # from its interpreter and emitter, so the meaning is defined here; the
+    # CUDA lowering (``ptxgen/generic.py``) follows it.
+
+    def do_mbarrier(self, st) -> None:
+        """MbarrierInit / ArriveExpectTx / Arrive / Wait order copies and
+        threads on the GPU; in the lockstep model every copy has landed when
+        it is issued, so they change no value.  ``mbar`` must name a Smem
+        array of 8-byte elements and ``slot`` (default 0) index into it."""
+        decl = self.smem_decl.get(st.mbar)
+        if decl is None or decl[1].itemsize != 8:
+            raise KeyError(f"mbarrier {st.mbar!r} is not a Smem array of 8-byte elements")
+        if st.slot is not None:
+            slot = as_int64(self.ev(st.slot))
+            m = self.live()
+            if np.any(m & ((slot < 0) | (slot >= int(np.prod(decl[0])))))[()]:
+                raise IndexError(f"mbarrier slot out of range in {st.mbar!r}")
+
+    def do_tma_load(self, st: ir.TmaLoad) -> None:
+        """One box of a buffer into shared memory, landing at once.
+
+        The descriptor views its buffer row-major with ``src_shape`` (at most
+        the buffer's element count); the box is ``box_extents`` elements
+        from origin ``coords`` (both outermost first; the origin may be
+        negative), and box elements outside ``src_shape`` read as zero.  The
+        box lands row-major at element ``smem_index`` of the Smem buffer
+        (a flat offset, or an index into its shape).  With swizzle B32, B64
+        or B128 the box's inner extent is exactly 32, 64 or 128 bytes and
+        byte ``o`` of the box lands at ``o ^ (((o >> 7) & m) << 4)``, m = 1,
+        3 or 7 -- the TMA unit's pattern -- and the destination must sit on a
+        1024-byte boundary (16 bytes without swizzle).  Each active lane
+        issues the copy (IRs issue it from one thread).  Errors, raised here
+        and reported as ``emmy_err`` 0x305 by the CUDA lowering: an inner
+        coordinate not on a 16-byte boundary, a misaligned destination, a
+        box that does not fit the Smem buffer."""
+        d = self.tma_descs.get(st.desc)
+        if d is None:
+            raise KeyError(f"unknown TMA descriptor {st.desc!r}")
+        shape = tuple(int(e) for e in d.src_shape)
+        box = tuple(int(e) for e in d.box_extents)
+        src = self.mem[d.src_buf].reshape(-1)
+        eb = src.dtype.itemsize
+        tma_check_descriptor(d, src.size, eb)
+        if st.smem not in self.smem:
+            raise KeyError(f"TMA destination {st.smem!r} is not a Smem buffer")
+        view = self.smem[st.smem].reshape(self.count, -1)
+        if view.dtype.itemsize != eb:
+            raise ValueError("TMA source and destination element sizes differ")
+        idx = st.smem_index if isinstance(st.smem_index, tuple) else (st.smem_index,)
+        dshape = self.smem_decl[st.smem][0] if isinstance(st.smem_index, tuple) else (
+            view.shape[1],)
+        dst = self.lane_flat(idx, dshape)
+        coords = [np.broadcast_to(as_int64(self.ev(c)), (self.n,)) for c in st.coords]
+        if len(coords) != len(shape):
+            raise ValueError("TMA coords and descriptor rank differ")
+        whole = src[:int(np.prod(shape))].reshape(shape)
+        perm = tma_swizzle_perm(box, eb, d.swizzle)
+        align = 1024 if perm is not None else 16
+        for ln in np.nonzero(self.live())[0]:
+            c = [int(x[ln]) for x in coords]
+            if (c[-1] * eb) % 16:
+                raise ValueError("TMA inner coordinate not on a 16-byte boundary")
+            d0 = int(dst[ln])
+            if (d0 * eb) % align or d0 < 0 or d0 + int(np.prod(box)) > view.shape[1]:
+                raise IndexError(f"TMA box does not fit {st.smem!r} at element {d0}")
+            data = np.zeros(box, dtype=src.dtype)
+            bsl, ssl = [], []
+            for o, b, n in zip(c, box, shape):
+                lo, hi = max(o, 0), min(o + b, n)
+                if hi <= lo:
+                    break
+                bsl.append(slice(lo - o, hi - o))
+                ssl.append(slice(lo, hi))
+            else:
+                data[tuple(bsl)] = whole[tuple(ssl)]
+            flat = data.reshape(-1)
+            pos = d0 + (perm if perm is not None else np.arange(flat.size))
+            view[self.local[ln], pos] = flat
 
     def do_zero_prologue(self, st: ir.ZeroPrologue) -> None:
         """CTA 0 clears the first ``words`` 32-bit words (``interp.py:974-980``)."""
