@@ -36,7 +36,13 @@ under meta.json's launch, with the semantics of the golden model
   0x305 and its bytes completed so no wait is left hanging.  ``SetMaxNReg``
   lowers to nothing: this lowering does not specialise warps, and the same
   budget change on every warp of the block can only lower the registers
-  ptxas allotted or, as an increase, wait on registers nobody releases.
+  ptxas allotted or, as an increase, wait on registers nobody releases;
+* ``RegFragment`` / ``LdmatrixLoad`` / ``MmaSyncPtx`` / ``RegStore`` (the
+  m16n8k16 atom, bf16 or f16 A/B, f32 C) are per-thread registers,
+  ``ldmatrix`` (``.trans`` for a [K][N] B), ``mma.sync`` and per-lane stores
+  in the PTX fragment layout; loads and products update every lane of the
+  warp whatever the mask, stores honour it; a fragment access outside its
+  buffer is skipped with ``emmy_err`` 0x306.
 """
 
 from __future__ import annotations
@@ -59,6 +65,7 @@ def _collective(body) -> bool:
 ERR_OOB = 0x301          # checked mode: an index outside its buffer (access skipped)
 ERR_MBAR_WAIT = 0x304    # an mbarrier wait ran past its limit
 ERR_TMA = 0x305          # a TMA box copy that breaks its alignment or bounds (skipped)
+ERR_FRAG = 0x306         # a fragment load or store outside its buffer (skipped)
 MBAR_WAIT_NS = 2_000_000_000
 _TMA_SPAN = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}
 
@@ -118,8 +125,11 @@ class Generic:
             ir.TmaDescriptor: lambda st: None, ir.TmaLoad: self.do_tma_load,
             ir.MbarrierInit: self.do_mbar_init, ir.MbarrierArriveExpectTx: self.do_mbar_expect,
             ir.MbarrierArrive: self.do_mbar_arrive, ir.MbarrierWait: self.do_mbar_wait,
-            ir.SetMaxNReg: lambda st: None,
+            ir.SetMaxNReg: lambda st: None, ir.RegFragment: self.do_reg_fragment,
+            ir.LdmatrixLoad: self.do_ldmatrix, ir.MmaSyncPtx: self.do_mma_sync,
+            ir.RegStore: self.do_reg_store,
         }
+        self.frags: dict[str, tuple] = {}    # name -> (role, dtype, [[regs] per cell])
         self.tma = {st.name: st for st in ir.walk(spec.op.body)
                     if isinstance(st, ir.TmaDescriptor)}
         for d in self.tma.values():
@@ -871,6 +881,177 @@ class Generic:
         k(f"setp.lt.u32 {p3}, {ri}, {rows}")
         k(f"@{p3} bra {head}")
         k.place(done)
+
+
+    # -- warp-level tensor-core fragments (mma.sync) ------------------------
+
+    def frag_cell(self, ref, index=None) -> tuple[str, list]:
+        name, _, rest = str(ref).partition("[")
+        cell = int(rest.rstrip("]")) if rest else 0
+        if index is not None:
+            if rest:
+                raise LowerError(f"fragment {ref!r} indexed twice")
+            if not isinstance(index, (int, ir.Literal)):
+                raise LowerError("fragment_index must be a literal")
+            cell = int(index.value if isinstance(index, ir.Literal) else index)
+        if name not in self.frags:
+            raise LowerError(f"undeclared fragment {name!r}")
+        cells = self.frags[name][2]
+        if not 0 <= cell < len(cells):
+            raise LowerError(f"fragment cell {cell} of {name!r}")
+        return name, cells[cell]
+
+    def frag_error(self, ok: str) -> None:
+        """Record ERR_FRAG for a lane whose fragment access left its buffer."""
+        k = self.k
+        skip, old = k.label("frag_ok"), k.reg("u32")
+        k(f"@{ok} bra {skip}")
+        k(f"atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_FRAG}")
+        k.place(skip)
+
+    def do_reg_fragment(self, st: ir.RegFragment) -> None:
+        k = self.k
+        role = str(st.role).lower()
+        if str(st.shape) != "m16n8k16":
+            raise LowerError(f"fragment shape {st.shape!r}")
+        dt = dtype_info(st.dtype)[0]
+        if (role in ("a", "b") and dt not in ("bf16", "f16")) or (role == "c" and dt != "f32"):
+            raise LowerError(f"{role} fragment of {st.dtype!r}")
+        nregs = {"a": 4, "b": 2, "c": 4}[role]
+        if st.name not in self.frags:
+            cells = [k.regs("f32" if role == "c" else "b32", nregs)
+                     for _ in range(int(st.count or 1))]
+            self.frags[st.name] = (role, dt, cells)
+        role0, dt0, cells = self.frags[st.name]
+        if (role0, dt0, len(cells)) != (role, dt, int(st.count or 1)):
+            raise LowerError(f"fragment {st.name!r} declared twice differently")
+        for cell in cells:
+            for r in cell:
+                k(f"mov.b32 {r}, 0")
+
+    def do_ldmatrix(self, st: ir.LdmatrixLoad) -> None:
+        k, lo = self.k, self.lo
+        for opt in ("staged", "gmem_guard", "k_zero", "pair_frag", "byte_slab",
+                    "scale_buffer", "scale_index", "scale_ldm", "fragment_layout"):
+            if getattr(st, opt) not in (None, False, "NONE"):
+                raise LowerError(f"LdmatrixLoad option {opt}")
+        name, regs = self.frag_cell(st.frag, st.fragment_index)
+        role = self.frags[name][0]
+        if role != str(st.role).lower() or role not in ("a", "b"):
+            raise LowerError(f"LdmatrixLoad role {st.role!r} into {role} fragment {name!r}")
+        if st.src_buffer not in self.smem or dtype_info(self.smem[st.src_buffer][1])[2] != 2:
+            raise LowerError("LdmatrixLoad reads a 16-bit Smem buffer")
+        shape, _, off = self.smem[st.src_buffer]
+        ldm = int(st.ldm) if st.ldm is not None else int(shape[-1])
+        lane = lo.env["lane"].reg
+        r, c = k.reg("s32"), k.reg("s32")
+        # the row this lane addresses: A rows 0-15 for k 0-7 (lanes 0-15) and
+        # k 8-15 (lanes 16-31); B [N][K]: n 0-7 for k 0-7 and 8-15 (lanes
+        # 0-15); B [K][N] (.trans): k 0-15 (lanes 0-15)
+        if role == "a":
+            k(f"and.b32 {r}, {lane}, 15")
+            k(f"shr.b32 {c}, {lane}, 4")
+            k(f"shl.b32 {c}, {c}, 3")
+        elif st.b_trans:
+            k(f"and.b32 {r}, {lane}, 15")
+            k(f"mov.b32 {c}, 0")
+        else:
+            k(f"and.b32 {r}, {lane}, 7")
+            k(f"shr.b32 {c}, {lane}, 3")
+            k(f"and.b32 {c}, {c}, 1")
+            k(f"shl.b32 {c}, {c}, 3")
+        r0 = lo.coerce(lo.ev(st.src_index[0]), "s32").reg
+        c0 = lo.coerce(lo.ev(st.src_index[1]), "s32").reg
+        flat = k.reg("s32")
+        k(f"add.s32 {r}, {r}, {r0}")
+        k(f"add.s32 {c}, {c}, {c0}")
+        k(f"mad.lo.s32 {flat}, {r}, {ldm}, {c}")
+        fl = self.swizzle(Val(flat, "s32"), st.swizzle).reg
+        ok = k.reg("pred")
+        k(f"setp.le.u32 {ok}, {fl}, {numel(shape) - 8}")
+        self.frag_error(ok)
+        safe, a = k.reg("s32"), k.reg("u32")
+        k(f"selp.s32 {safe}, {fl}, 0, {ok}")
+        k(f"mad.lo.u32 {a}, {safe}, 2, {self.smem_base}")
+        if off:
+            k(f"add.u32 {a}, {a}, {off}")
+        if role == "a":
+            k(f"ldmatrix.sync.aligned.m8n8.x4.shared.b16 {{{', '.join(regs)}}}, [{a}]")
+        else:
+            tr = ".trans" if st.b_trans else ""
+            k(f"ldmatrix.sync.aligned.m8n8.x2{tr}.shared.b16 {{{', '.join(regs)}}}, [{a}]")
+
+    def do_mma_sync(self, st: ir.MmaSyncPtx) -> None:
+        if str(st.shape) != "m16n8k16" or st.b_row_major or st.sfa_frag or st.sfb_frag:
+            raise LowerError("MmaSyncPtx: m16n8k16, B column-major, no scales")
+        an, a = self.frag_cell(st.a_frag)
+        bn, b = self.frag_cell(st.b_frag)
+        cn, c = self.frag_cell(st.c_frag)
+        if (self.frags[an][0], self.frags[bn][0], self.frags[cn][0]) != ("a", "b", "c"):
+            raise LowerError("MmaSyncPtx takes a, b and c fragments")
+        ab = self.frags[an][1]
+        if self.frags[bn][1] != ab:
+            raise LowerError("MmaSyncPtx: A and B of different types")
+        self.k(f"mma.sync.aligned.m16n8k16.row.col.f32.{ab}.{ab}.f32 "
+               f"{{{', '.join(c)}}}, {{{', '.join(a)}}}, {{{', '.join(b)}}}, "
+               f"{{{', '.join(c)}}}")
+
+    def do_reg_store(self, st: ir.RegStore) -> None:
+        k, lo = self.k, self.lo
+        for opt in ("epilogue", "extra_frags", "fragment_layout", "volta_interleaved",
+                    "row_dim", "col_dim"):
+            if getattr(st, opt) not in (None, False, (), []):
+                raise LowerError(f"RegStore option {opt}")
+        if str(st.swizzle or "NONE") != "NONE":
+            raise LowerError("RegStore swizzle")
+        name, regs = self.frag_cell(st.frag, st.fragment_index)
+        if self.frags[name][0] != "c":
+            raise LowerError("RegStore stores a c fragment")
+        if st.dst_buffer not in self.base:
+            raise LowerError(f"RegStore into {st.dst_buffer!r}")
+        shape = self.spec.args[st.dst_buffer].shape
+        ldm = int(st.ldm) if st.ldm is not None else int(shape[-1])
+        lane = lo.env["lane"].reg
+        g, t = k.reg("s32"), k.reg("s32")
+        k(f"shr.b32 {g}, {lane}, 2")
+        k(f"and.b32 {t}, {lane}, 3")
+        k(f"shl.b32 {t}, {t}, 1")
+        r0 = lo.coerce(lo.ev(st.dst_index[0]), "s32").reg
+        c0 = lo.coerce(lo.ev(st.dst_index[1]), "s32").reg
+        mg = lo.coerce(lo.ev(st.m_guard), "s32").reg if st.m_guard is not None else None
+        ng = lo.coerce(lo.ev(st.n_guard), "s32").reg if st.n_guard is not None else None
+        dt = self.spec.args[st.dst_buffer].dtype
+        for i, v in enumerate(regs):
+            row, col, idx = k.reg("s32"), k.reg("s32"), k.reg("s32")
+            k(f"add.s32 {row}, {r0}, {g}")
+            if i // 2:
+                k(f"add.s32 {row}, {row}, 8")
+            k(f"add.s32 {col}, {c0}, {t}")
+            if i % 2:
+                k(f"add.s32 {col}, {col}, 1")
+            k(f"mad.lo.s32 {idx}, {row}, {ldm}, {col}")
+            want = k.reg("pred")
+            k("setp.eq.u32 {}, 0, 0".format(want))
+            if mg is not None:
+                k(f"setp.lt.and.s32 {want}, {row}, {mg}, {want}")
+            if ng is not None:
+                k(f"setp.lt.and.s32 {want}, {col}, {ng}, {want}")
+            if lo.mask is not None:
+                k(f"and.pred {want}, {want}, {lo.mask}")
+            inb, ok = k.reg("pred"), k.reg("pred")
+            k(f"setp.lt.u32 {inb}, {idx}, {numel(shape)}")
+            # a wanted element outside the buffer is an error, not a store
+            k(f"not.pred {ok}, {want}")
+            k(f"or.pred {ok}, {ok}, {inb}")
+            self.frag_error(ok)
+            k(f"and.pred {want}, {want}, {inb}")
+            safe = k.reg("s32")
+            k(f"selp.s32 {safe}, {idx}, 0, {inb}")
+            a, sh, _ = self.addr(st.dst_buffer, Val(safe, "s32"))
+            saved = lo.mask
+            lo.mask = want
+            self.store_elem(a, sh, dt, Val(v, "f32"), atomic=bool(st.atomic))
+            lo.mask = saved
 
 
 def emit_generic(spec: KernelSpec, checked: bool = False) -> Module:

@@ -505,6 +505,74 @@ class SetMaxNReg(Node):
     direction: str = "inc"
 
 
+# -- warp-level tensor-core fragments (``mma.sync``), starred in the same
+#    table (``TASK.md:146-158``)
+
+
+@dataclass(repr=False, eq=True)
+class RegFragment(Node):
+    name: str
+    role: str = "c"
+    shape: Any = "m16n8k16"
+    dtype: Any = "bf16"
+    count: int = 1
+    nregs: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class LdmatrixLoad(Node):
+    frag: str
+    src_buffer: str
+    src_index: tuple
+    role: str = "a"
+    ldm: Any = None
+    swizzle: str = "NONE"
+    staged: Any = None
+    gmem_guard: Any = None
+    k_zero: Any = None
+    b_trans: bool = False
+    pair_frag: Any = None
+    byte_slab: Any = None
+    scale_buffer: Any = None
+    scale_index: Any = None
+    scale_ldm: Any = None
+    fragment_layout: Any = None
+    fragment_index: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class MmaSyncPtx(Node):
+    c_frag: str
+    a_frag: str
+    b_frag: str
+    shape: Any = "m16n8k16"
+    ab_dtype: Any = "bf16"
+    c_dtype: Any = "f32"
+    b_row_major: bool = False
+    sfa_frag: Any = None
+    sfb_frag: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class RegStore(Node):
+    dst_buffer: str
+    dst_index: tuple
+    frag: str
+    shape: Any = "m16n8k16"
+    ldm: Any = None
+    epilogue: Any = None
+    extra_frags: Any = None
+    m_guard: Any = None
+    n_guard: Any = None
+    atomic: bool = False
+    fragment_layout: Any = None
+    volta_interleaved: Any = None
+    fragment_index: Any = None
+    swizzle: str = "NONE"
+    row_dim: Any = None
+    col_dim: Any = None
+
+
 # ---------------------------------------------------------------------------
 # graph level
 # ---------------------------------------------------------------------------
@@ -600,6 +668,7 @@ _CTORS: dict[str, Any] = {
         Write, Loop, StridedLoop, Cond, Smem, Sync, WarpShuffle, TreeHalve, CpAsyncCopy,
         CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue, TmaDescriptor,
         TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
+        RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

@@ -25,7 +25,10 @@ re-derives the shape-dependent literals:
                      transport nodes (``TmaDescriptor``, ``TmaLoad``,
                      ``Mbarrier*``, ``SetMaxNReg``), which no shipped problem
                      uses: a box copy with zero fill and swizzle, and the m02
-                     tile schedule fed by box copies instead of ``cp.async``.
+                     tile schedule fed by box copies instead of ``cp.async``;
+* ``matmul_mma``  -- a 16-bit matmul on warp-level tensor-core fragments
+                     (``RegFragment``, ``LdmatrixLoad``, ``MmaSyncPtx``,
+                     ``RegStore``) fed by box copies.
 
 At the shipped shapes the generated bodies equal the shipped ones byte for
 byte (``tests/test_irgen.py``); that pins the generator to the reference's
@@ -39,9 +42,9 @@ import math
 
 from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCopy,
                  CpAsyncWait, Dim, ElementwiseImpl, Init, Let, Literal, Load, Loop,
-                 MbarrierArriveExpectTx, MbarrierInit, MbarrierWait, SetMaxNReg, Smem,
-                 StridedLoop, Sync, TernaryExpr, Tile, TmaDescriptor, TmaLoad, TreeHalve, Var,
-                 WarpShuffle, Window, Write, datatype)
+                 LdmatrixLoad, MbarrierArriveExpectTx, MbarrierInit, MbarrierWait, MmaSyncPtx,
+                 RegFragment, RegStore, SetMaxNReg, Smem, StridedLoop, Sync, TernaryExpr, Tile,
+                 TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, Window, Write, datatype)
 
 F32 = datatype("f32")
 
@@ -927,6 +930,61 @@ def matmul_tma(m: int, n: int, k: int, entry="k_matmul_tma", pid="matmul_tma"):
                    [], ("matmul", (m, n), "f32"), ["x1", "x0", "matmul"],
                    ((m // BM) * (n // BN), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid,
                    kernel_inputs=["x1", "x0"])
+
+
+def matmul_mma(m: int, n: int, k: int, dtype="bf16", m_valid=None, n_valid=None,
+               entry="k_matmul_mma", pid="matmul_mma"):
+    """C = A.B (A [m, k], B [k, n] in bf16 or f16, C in f32) on m16n8k16
+    fragments: a 64 x 32 C tile per CTA of four warps, warp w owning rows
+    16w..16w+15 as four 16 x 8 cells; per K step of 16 thread 0 brings the
+    A (64 x 16) and B (16 x 32) boxes with two box copies on one mbarrier,
+    each warp loads its A cell and the four B cells (``ldmatrix``, B [K][N]
+    transposed) and accumulates four products.  ``m_valid`` / ``n_valid``:
+    rows and columns of C stored (the guards of ``RegStore``)."""
+    BM, BN, BK, TH = 64, 32, 16, 128
+    if m % BM or n % BN or k % BK:
+        raise ValueError("matmul_mma shape must tile by 64x32 with K a multiple of 16")
+    t = V("t")
+    nb = (BM * BK + BK * BN) * 2
+    body = [TmaDescriptor(name="dA", src_buf="x0", src_shape=(m, k), box_extents=(BM, BK),
+                          swizzle="NONE", dtype=dtype),
+            TmaDescriptor(name="dB", src_buf="x1", src_shape=(k, n), box_extents=(BK, BN),
+                          swizzle="NONE", dtype=dtype),
+            Smem(name="_a_smem", extents=(BM, BK), dtype=_SMEM_C[dtype], align=128),
+            Smem(name="_b_smem", extents=(BK, BN), dtype=_SMEM_C[dtype], align=128),
+            Smem(name="bar", extents=(1,), dtype=_MBAR, align=8),
+            RegFragment(name="fa", role="a", shape="m16n8k16", dtype=dtype, count=1, nregs=4),
+            RegFragment(name="fb", role="b", shape="m16n8k16", dtype=dtype, count=4, nregs=2),
+            RegFragment(name="fc", role="c", shape="m16n8k16", dtype="f32", count=4, nregs=4),
+            Cond(cond=EQ(t, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
+                 else_body=()),
+            Sync(barrier_id=0, count=None, warp=False)]
+    copies = [TmaLoad(smem="_a_smem", smem_index=L(0), desc="dA",
+                      coords=(MUL(V("bm"), L(BM)), V("_ks")), mbar="bar", mbar_slot=L(0)),
+              TmaLoad(smem="_b_smem", smem_index=L(0), desc="dB",
+                      coords=(V("_ks"), MUL(V("bn"), L(BN))), mbar="bar", mbar_slot=L(0))]
+    ks = [_tma_issue(t, copies, nb),
+          MbarrierWait(mbar="bar", phase=DIV(V("_ks"), L(BK)), slot=L(0)),
+          LdmatrixLoad(frag="fa", src_buffer="_a_smem", src_index=(MUL(V("warp"), L(16)), L(0)),
+                       role="a")]
+    for j in range(BN // 8):
+        ks += [LdmatrixLoad(frag="fb", src_buffer="_b_smem", src_index=(L(0), L(8 * j)),
+                            role="b", b_trans=True, fragment_index=L(j)),
+               MmaSyncPtx(c_frag=f"fc[{j}]", a_frag="fa", b_frag=f"fb[{j}]", shape="m16n8k16",
+                          ab_dtype=dtype, c_dtype="f32")]
+    ks.append(Sync(barrier_id=0, count=None, warp=False))
+    body.append(strided("_ks", k, L(0), L(BK), ks))
+    for j in range(BN // 8):
+        body.append(RegStore(dst_buffer="matmul",
+                             dst_index=(ADD(MUL(V("bm"), L(BM)), MUL(V("warp"), L(16))),
+                                        ADD(MUL(V("bn"), L(BN)), L(8 * j))),
+                             frag="fc", fragment_index=L(j),
+                             m_guard=None if m_valid is None else L(m_valid),
+                             n_guard=None if n_valid is None else L(n_valid)))
+    tl = tile([ax("bm", m // BM), ax("bn", n // BN), ax("t", TH)], body, block_threads=TH)
+    return package(entry, "matmul", [tl], [("x0", (m, k), dtype, 0), ("x1", (k, n), dtype, 1)],
+                   [], ("matmul", (m, n), "f32"), ["x0", "x1", "matmul"],
+                   ((m // BM) * (n // BN), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid)
 
 
 def bench_kernels():

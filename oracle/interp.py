@@ -330,6 +330,30 @@ def tma_check_descriptor(d, buf_numel: int, eb: int) -> None:
         raise ValueError(f"TMA swizzle {d.swizzle} needs a {span}-byte box row")
 
 
+def mma_layout(role: str):
+    """Row and column of every register-fragment element of each of the 32
+    lanes of an ``mma.m16n8k16`` (16-bit A and B, f32 C), as [32, E] arrays
+    -- A: (m, k), 8 elements; B: (k, n), 4; C: (m, n), 4 -- the layouts the
+    PTX ISA gives for that shape: g = lane >> 2, t = lane & 3."""
+    lane = np.arange(32)
+    g, t = (lane >> 2)[:, None], (lane & 3)[:, None]
+    if role == "a":
+        i = np.arange(8)[None]
+        return g + 8 * ((i // 2) % 2), 2 * t + (i % 2) + 8 * (i // 4)
+    if role == "b":
+        i = np.arange(4)[None]
+        return 2 * t + (i % 2) + 8 * (i // 2), np.broadcast_to(g, (32, 4))
+    i = np.arange(4)[None]
+    return g + 8 * (i // 2), 2 * t + (i % 2)
+
+
+def _kind_np(dt: np.dtype) -> str:
+    if _BF16 is not None and dt == np.dtype(_BF16):
+        return "f32"
+    return {np.dtype(np.float32): "f32", np.dtype(np.float64): "f64",
+            np.dtype(np.float16): "f16"}[np.dtype(dt)]
+
+
 def tma_swizzle_perm(box, eb: int, swizzle):
     """Element position of each box element in shared memory under a TMA
     swizzle (None without one): byte o goes to o ^ (((o >> 7) & m) << 4)."""
@@ -382,8 +406,12 @@ class Machine:
             ir.TmaDescriptor: self.do_nothing, ir.TmaLoad: self.do_tma_load,
             ir.MbarrierInit: self.do_mbarrier, ir.MbarrierArriveExpectTx: self.do_mbarrier,
             ir.MbarrierArrive: self.do_mbarrier, ir.MbarrierWait: self.do_mbarrier,
-            ir.SetMaxNReg: self.do_nothing,
+            ir.SetMaxNReg: self.do_nothing, ir.RegFragment: self.do_reg_fragment,
+            ir.LdmatrixLoad: self.do_ldmatrix, ir.MmaSyncPtx: self.do_mma_sync,
+            ir.RegStore: self.do_reg_store,
         }
+        self.frags: dict[str, np.ndarray] = {}
+        self.frag_role: dict[str, tuple[str, str]] = {}
         self.tma_descs = {st.name: st for st in ir.walk(spec.op.body)
                           if isinstance(st, ir.TmaDescriptor)}
 
@@ -912,6 +940,153 @@ class Machine:
             flat = data.reshape(-1)
             pos = d0 + (perm if perm is not None else np.arange(flat.size))
             view[self.local[ln], pos] = flat
+
+    # -- warp-level tensor-core fragments (mma.sync) ------------------------
+    # Starred in the reference's IR table (``TASK.md:146-158``) with no
+    # behaviour in its interpreter; defined here for the m16n8k16 atom with
+    # 16-bit A/B (bf16 or f16) and an f32 C.  A fragment is a per-lane array
+    # (``count`` cells of 8 A, 4 B or 4 C elements per lane) laid out as the
+    # PTX ISA lays out the registers of ``mma.m16n8k16`` (``mma_layout``).
+    # Loads and the product are warp-collective: they update every lane of
+    # the warp whatever the lane mask; stores honour it.
+
+    def _frag_ref(self, ref, index=None):
+        name, _, rest = str(ref).partition("[")
+        cell = int(rest.rstrip("]")) if rest else 0
+        if index is not None:
+            if rest:
+                raise ValueError(f"fragment {ref!r} indexed twice")
+            cell = int(as_int64(self.ev(index)).reshape(-1)[0]) if hasattr(
+                index, "free_vars") else int(index)
+        f = self.frags.get(name)
+        if f is None:
+            raise KeyError(f"undeclared fragment {name!r}")
+        if not 0 <= cell < f.shape[0]:
+            raise IndexError(f"fragment cell {cell} of {name!r}")
+        return name, cell
+
+    def _warps(self) -> int:
+        if self.T % 32:
+            raise ValueError("fragment operations need whole warps")
+        return self.n // 32
+
+    def do_reg_fragment(self, st: ir.RegFragment) -> None:
+        role = str(st.role).lower()
+        if str(st.shape) != "m16n8k16":
+            raise NotImplementedError(f"fragment shape {st.shape!r}")
+        dt = dtype_info(st.dtype)[0]
+        if role in ("a", "b") and dt not in ("bf16", "f16"):
+            raise NotImplementedError(f"{role} fragment of {st.dtype!r}")
+        if role == "c" and dt != "f32":
+            raise NotImplementedError(f"c fragment of {st.dtype!r}")
+        elems = {"a": 8, "b": 4, "c": 4}[role]
+        self.frags[st.name] = np.zeros((int(st.count or 1), self.n, elems), np.float32)
+        self.frag_role[st.name] = (role, dt)
+
+    def do_ldmatrix(self, st: ir.LdmatrixLoad) -> None:
+        """Fill one A or B cell from a 16-bit Smem buffer.  ``src_index`` =
+        (row, col) of the cell's origin, the same on every lane of a warp;
+        element (r, c) of the buffer is at r * ldm + c (``ldm`` defaults to
+        the buffer's last extent), then the IR's shared-memory swizzle.  A
+        (16 x 16, m by k) reads rows r0 + m, columns c0 + k; B (16 x 8, k by
+        n) reads rows r0 + n, columns c0 + k, or with ``b_trans`` rows r0 + k,
+        columns c0 + n."""
+        for opt in ("staged", "gmem_guard", "k_zero", "pair_frag", "byte_slab",
+                    "scale_buffer", "scale_index", "scale_ldm", "fragment_layout"):
+            if getattr(st, opt) not in (None, False, "NONE"):
+                raise NotImplementedError(f"LdmatrixLoad option {opt}")
+        name, cell = self._frag_ref(st.frag, st.fragment_index)
+        role, _ = self.frag_role[name]
+        if role != str(st.role).lower() or role not in ("a", "b"):
+            raise ValueError(f"LdmatrixLoad role {st.role!r} into {role} fragment {name!r}")
+        if st.src_buffer not in self.smem or self.smem[st.src_buffer].dtype.itemsize != 2:
+            raise ValueError("LdmatrixLoad reads a 16-bit Smem buffer")
+        view = self.smem[st.src_buffer].reshape(self.count, -1)
+        shape = self.smem_decl[st.src_buffer][0]
+        ldm = int(st.ldm) if st.ldm is not None else int(shape[-1])
+        w = self._warps()
+        r0 = np.broadcast_to(as_int64(self.ev(st.src_index[0])), (self.n,)).reshape(w, 32)
+        c0 = np.broadcast_to(as_int64(self.ev(st.src_index[1])), (self.n,)).reshape(w, 32)
+        if np.any(r0 != r0[:, :1]) or np.any(c0 != c0[:, :1]):
+            raise ValueError("LdmatrixLoad origin differs within a warp")
+        rows, cols = mma_layout(role)               # [32, E]: (m, k) or (k, n)
+        if role == "a":
+            rr, cc = rows, cols
+        elif st.b_trans:
+            rr, cc = rows, cols                     # buffer [K][N]
+        else:
+            rr, cc = cols, rows                     # buffer [N][K]
+        flat = (r0[:, :1, None] + rr[None]) * ldm + (c0[:, :1, None] + cc[None])
+        flat = swizzle_index(flat, st.swizzle)
+        if np.any((flat < 0) | (flat >= view.shape[1])):
+            raise IndexError(f"LdmatrixLoad outside {st.src_buffer!r}")
+        ci = self.local.reshape(w, 32)[:, :, None]
+        vals = view[np.broadcast_to(ci, flat.shape), flat].astype(np.float32)
+        self.frags[name][cell] = vals.reshape(self.n, -1)
+
+    def do_mma_sync(self, st: ir.MmaSyncPtx) -> None:
+        """c = a . b + c per warp on one m16n8k16 cell: the exact products
+        summed with the accumulator and rounded once to f32 (the tensor core
+        adds in an order and width of its own; the CUDA path is held to a
+        bound, not to bits)."""
+        if str(st.shape) != "m16n8k16" or st.b_row_major or st.sfa_frag or st.sfb_frag:
+            raise NotImplementedError("MmaSyncPtx: m16n8k16, B column-major, no scales")
+        w = self._warps()
+        (an, ac), (bn, bc), (cn, cc) = (self._frag_ref(x) for x in
+                                        (st.a_frag, st.b_frag, st.c_frag))
+        ar, acl = mma_layout("a")
+        br_, bcl = mma_layout("b")
+        cr, ccl = mma_layout("c")
+        A = np.zeros((w, 16, 16))
+        B = np.zeros((w, 16, 8))
+        Cm = np.zeros((w, 16, 8))
+        af = self.frags[an][ac].reshape(w, 32, -1)
+        bf = self.frags[bn][bc].reshape(w, 32, -1)
+        cf = self.frags[cn][cc].reshape(w, 32, -1)
+        A[:, ar, acl] = af
+        B[:, br_, bcl] = bf
+        Cm[:, cr, ccl] = cf
+        D = (np.einsum("wmk,wkn->wmn", A, B) + Cm).astype(np.float32)
+        self.frags[cn][cc] = D[:, cr, ccl].reshape(self.n, -1)
+
+    def do_reg_store(self, st: ir.RegStore) -> None:
+        """Each active lane stores its C elements: element (m, n) of the cell
+        to (r0 + m) * ldm + c0 + n of the buffer (``ldm`` defaults to its
+        last extent), only where r0 + m < ``m_guard`` and c0 + n < ``n_guard``
+        when given; ``atomic`` adds.  (r0, c0) = ``dst_index`` of the lane."""
+        for opt in ("epilogue", "extra_frags", "fragment_layout", "volta_interleaved",
+                    "row_dim", "col_dim"):
+            if getattr(st, opt) not in (None, False, (), []):
+                raise NotImplementedError(f"RegStore option {opt}")
+        if str(st.swizzle or "NONE") != "NONE":
+            raise NotImplementedError("RegStore swizzle")
+        name, cell = self._frag_ref(st.frag, st.fragment_index)
+        if self.frag_role[name][0] != "c":
+            raise ValueError("RegStore stores a c fragment")
+        arr = self.mem[st.dst_buffer]
+        ldm = int(st.ldm) if st.ldm is not None else int(arr.shape[-1])
+        r0 = np.broadcast_to(as_int64(self.ev(st.dst_index[0])), (self.n,))
+        c0 = np.broadcast_to(as_int64(self.ev(st.dst_index[1])), (self.n,))
+        cr, ccl = mma_layout("c")
+        lane = (self.tid & 31).astype(np.int64)
+        rows = r0[:, None] + cr[lane]
+        cols = c0[:, None] + ccl[lane]
+        ok = np.broadcast_to(self.live()[:, None], rows.shape).copy()
+        for guard, idx in ((st.m_guard, rows), (st.n_guard, cols)):
+            if guard is not None:
+                lim = np.broadcast_to(as_int64(self.ev(guard)), (self.n,))
+                ok &= idx < lim[:, None]
+        flat = (rows * ldm + cols)[ok]
+        vals = self.frags[name][cell][ok]
+        out = arr.reshape(-1)
+        if np.any((flat < 0) | (flat >= out.size)):
+            raise IndexError(f"RegStore outside {st.dst_buffer!r}")
+        data = coerce(Val("f32", vals.astype(np.float32)), _kind_np(out.dtype)).a
+        if st.atomic:
+            for f, v in zip(flat, data):            # lanes in order, one rounding each
+                out[f] = (out[f] + v).astype(out.dtype)
+        else:
+            out[flat] = data
 
     def do_zero_prologue(self, st: ir.ZeroPrologue) -> None:
         """CTA 0 clears the first ``words`` 32-bit words (``interp.py:974-980``)."""

@@ -117,3 +117,36 @@ def test_unarrived_wait_gives_up_and_reports():
     good = box_case(BOX_CASES[1], name="tbafter")
     xi = box_inputs(good)
     assert np.array_equal(_run(good, xi)["out"], box_reference(BOX_CASES[1], xi["x0"]))
+
+
+def _mma_case(m, n, k, dt, seed, **kw):
+    from oracle.interp import storage_dtype
+    spec = load_kernel_data(*irgen.matmul_mma(m, n, k, dt, **kw), f"mma{m}{n}{k}{dt}")
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((m, k)).astype(storage_dtype(dt))
+    b = rng.standard_normal((k, n)).astype(storage_dtype(dt))
+    return spec, a, b
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("mnk", [(64, 32, 16), (128, 64, 96), (256, 128, 512)])
+def test_matmul_mma_fragments(mnk, dt):
+    """``ldmatrix`` + ``mma.sync`` in the PTX fragment layouts against the
+    oracle: any layout slip moves whole products (errors of order one); the
+    tensor core's own accumulation stays within 2^-17 of sum |a||b| per
+    element."""
+    m, n, k = mnk
+    spec, a, b = _mma_case(m, n, k, dt, m + k)
+    want = interpret(spec, {"x0": a.copy(), "x1": b.copy()})["matmul"]
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    assert np.all(np.abs(got - want) <= 2.0 ** -17 * scale + 1e-30)
+
+
+def test_matmul_mma_store_guards():
+    spec, a, b = _mma_case(128, 64, 64, "bf16", 9, m_valid=100, n_valid=50)
+    want = interpret(spec, {"x0": a.copy(), "x1": b.copy()})["matmul"]
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    assert np.all(got[100:] == 0) and np.all(got[:, 50:] == 0)
+    scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    assert np.all(np.abs(got - want) <= 2.0 ** -17 * scale + 1e-30)

@@ -125,3 +125,89 @@ def test_tma_kernels_assemble(tmp_path):
         r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
                            capture_output=True, text=True)
         assert r.returncode == 0, r.stderr[-2000:]
+
+
+# -- warp-level tensor-core fragments ------------------------------------------
+
+def _mma_inputs(m, n, k, dt, seed=0):
+    from oracle.interp import storage_dtype
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((m, k)).astype(storage_dtype(dt)),
+            rng.standard_normal((k, n)).astype(storage_dtype(dt)))
+
+
+def _mma_steps_reference(a, b, guard=None):
+    """C summed one K step of 16 at a time: exact products of the step plus
+    the running C, rounded once to f32 per step."""
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    c = np.zeros((a.shape[0], b.shape[1]), np.float32)
+    for k0 in range(0, a.shape[1], 16):
+        c = (a64[:, k0:k0 + 16] @ b64[k0:k0 + 16] + c).astype(np.float32)
+    if guard:
+        c[guard[0]:] = 0
+        c[:, guard[1]:] = 0
+    return c
+
+
+def test_mma_layout_covers_each_cell_once():
+    from oracle.interp import mma_layout
+    for role, shape in (("a", (16, 16)), ("b", (16, 8)), ("c", (16, 8))):
+        r, c = mma_layout(role)
+        cells = set(zip(r.ravel().tolist(), c.ravel().tolist()))
+        assert len(cells) == r.size == shape[0] * shape[1]
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_oracle_matmul_mma(dt):
+    spec = load_kernel_data(*irgen.matmul_mma(128, 64, 96, dt), "mm")
+    a, b = _mma_inputs(128, 64, 96, dt)
+    got = interpret(spec, {"x0": a, "x1": b})["matmul"]
+    assert np.array_equal(got, _mma_steps_reference(a, b))
+
+
+def test_oracle_matmul_mma_guards():
+    spec = load_kernel_data(*irgen.matmul_mma(128, 64, 32, "bf16", m_valid=100, n_valid=50),
+                            "mmg")
+    a, b = _mma_inputs(128, 64, 32, "bf16", 1)
+    got = interpret(spec, {"x0": a, "x1": b})["matmul"]
+    assert np.array_equal(got, _mma_steps_reference(a, b, (100, 50)))
+
+
+def test_fragment_nodes_round_trip():
+    nodes = [ir.RegFragment(name="fa", role="a", shape="m16n8k16", dtype="bf16", count=1,
+                            nregs=4),
+             ir.LdmatrixLoad(frag="fb", src_buffer="s", src_index=(irgen.L(0), irgen.L(8)),
+                             role="b", b_trans=True, fragment_index=irgen.L(1)),
+             ir.MmaSyncPtx(c_frag="fc[1]", a_frag="fa", b_frag="fb[1]"),
+             ir.RegStore(dst_buffer="o", dst_index=(irgen.V("r"), irgen.L(0)), frag="fc",
+                         fragment_index=irgen.L(1), m_guard=irgen.L(100))]
+    for n in nodes:
+        assert ir.parse_stmt(repr(n)) == n
+
+
+def test_fragment_options_not_lowered_are_refused():
+    gm = irgen.matmul_mma(64, 32, 16)
+    spec = load_kernel_data(gm[0], gm[1], "mmopt")
+    body = list(spec.op.body[0].body)
+    for i, st in enumerate(body):
+        if isinstance(st, ir.RegStore):
+            st.epilogue = "relu"
+            break
+    spec.op.body[0].body = tuple(body)
+    with pytest.raises(LowerError, match="epilogue"):
+        emit_generic(spec)
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+def test_fragment_kernels_assemble(tmp_path):
+    for i, gm in enumerate((irgen.matmul_mma(128, 64, 64, "bf16"),
+                            irgen.matmul_mma(64, 96, 32, "f16", m_valid=50, n_valid=70))):
+        f = tmp_path / f"m{i}.ptx"
+        ptx = compile_kernel(load_kernel_data(gm[0], gm[1], f"m{i}"))
+        assert "ldmatrix.sync.aligned.m8n8.x4.shared.b16" in ptx
+        assert "ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16" in ptx
+        assert "mma.sync.aligned.m16n8k16.row.col.f32" in ptx
+        f.write_text(ptx)
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-2000:]
