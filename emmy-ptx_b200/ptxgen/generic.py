@@ -42,7 +42,18 @@ under meta.json's launch, with the semantics of the golden model
   ``ldmatrix`` (``.trans`` for a [K][N] B), ``mma.sync`` and per-lane stores
   in the PTX fragment layout; loads and products update every lane of the
   warp whatever the mask, stores honour it; a fragment access outside its
-  buffer is skipped with ``emmy_err`` 0x306.
+  buffer is skipped with ``emmy_err`` 0x306;
+* ``Wgmma*`` run on the 5th-generation tensor cores: each warpgroup's
+  accumulator fragments live in its own TMEM columns while products are in
+  flight (``tcgen05.st`` of the registers before the first product,
+  ``tcgen05.ld`` back after ``WgmmaWait``, the ``16x256b`` shape whose
+  per-thread layout is the warpgroup accumulator's); one thread of the
+  group issues ``tcgen05.mma.cta_group::1.kind::f16`` (M = 64) from the
+  descriptors' shared-memory operands, ``WgmmaCommit`` is a
+  ``tcgen05.commit`` to a per-warpgroup mbarrier and ``WgmmaWait`` a
+  bounded wait on it.  The CTA allocates its TMEM once at the start and
+  frees it at the end.  An operand outside its buffer or misaligned skips
+  the product with ``emmy_err`` 0x307.
 """
 
 from __future__ import annotations
@@ -66,6 +77,18 @@ ERR_OOB = 0x301          # checked mode: an index outside its buffer (access ski
 ERR_MBAR_WAIT = 0x304    # an mbarrier wait ran past its limit
 ERR_TMA = 0x305          # a TMA box copy that breaks its alignment or bounds (skipped)
 ERR_FRAG = 0x306         # a fragment load or store outside its buffer (skipped)
+ERR_WGMMA = 0x307        # a wgmma operand outside its buffer or misaligned (skipped)
+_WG_LAYOUT = {"NONE": 0, "B32": 6, "B64": 4, "B128": 2}   # tcgen05 descriptor bits 61-63
+
+
+def wgmma_n(shape) -> int:
+    """N of an ``m64nNk16`` shape string (0 for any other)."""
+    s = str(shape)
+    if s.startswith("m64n") and s.endswith("k16") and s[4:-3].isdigit():
+        n = int(s[4:-3])
+        if n % 8 == 0 and 8 <= n <= 256:
+            return n
+    return 0
 MBAR_WAIT_NS = 2_000_000_000
 _TMA_SPAN = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}
 
@@ -127,9 +150,14 @@ class Generic:
             ir.MbarrierArrive: self.do_mbar_arrive, ir.MbarrierWait: self.do_mbar_wait,
             ir.SetMaxNReg: lambda st: None, ir.RegFragment: self.do_reg_fragment,
             ir.LdmatrixLoad: self.do_ldmatrix, ir.MmaSyncPtx: self.do_mma_sync,
-            ir.RegStore: self.do_reg_store,
+            ir.RegStore: self.do_reg_store, ir.WgmmaDescriptor: self.do_wgmma_desc,
+            ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: lambda st: None,
+            ir.WgmmaCommit: self.do_wgmma_commit, ir.WgmmaWait: self.do_wgmma_wait,
         }
         self.frags: dict[str, tuple] = {}    # name -> (role, dtype, [[regs] per cell])
+        self.wg = None                       # warpgroup tensor-core state (setup_wgmma)
+        self.wgdesc: dict[str, tuple] = {}
+        self.frag_shape: dict[str, str] = {}
         self.tma = {st.name: st for st in ir.walk(spec.op.body)
                     if isinstance(st, ir.TmaDescriptor)}
         for d in self.tma.values():
@@ -195,7 +223,9 @@ class Generic:
         lo.bind("lane", Val(lane, "s32"))
         lo.bind("warp", Val(warp, "s32"))
         self.tid = tid
+        self.setup_wgmma()
         lo.run(spec.op.body)
+        self.finish_wgmma()
         self.mod.kernels.append(k)
         self.mod.plan = {"entry": spec.entry, "kind": "generic", "block": int(spec.block[0]),
                          "grid_max": int(spec.grid[0] * spec.grid[1] * spec.grid[2]),
@@ -470,7 +500,11 @@ class Generic:
             if lo.mask is not None:
                 k(f"@!{lo.mask} bra {done}")
         lo.env[axis] = Val(var, "s32")
+        before = self.wg_state()
         lo.run(body)
+        if self.wg_state() != before:
+            raise LowerError("wgmma products must be committed and waited for inside each "
+                             "loop iteration")
         k(f"add.s32 {var}, {var}, {step.reg}")
         k(f"bra {head}")
         k.place(done)
@@ -912,16 +946,18 @@ class Generic:
     def do_reg_fragment(self, st: ir.RegFragment) -> None:
         k = self.k
         role = str(st.role).lower()
-        if str(st.shape) != "m16n8k16":
-            raise LowerError(f"fragment shape {st.shape!r}")
+        wg_n = wgmma_n(st.shape)
+        if str(st.shape) != "m16n8k16" and not (role == "c" and wg_n):
+            raise LowerError(f"{role} fragment shape {st.shape!r}")
         dt = dtype_info(st.dtype)[0]
         if (role in ("a", "b") and dt not in ("bf16", "f16")) or (role == "c" and dt != "f32"):
             raise LowerError(f"{role} fragment of {st.dtype!r}")
-        nregs = {"a": 4, "b": 2, "c": 4}[role]
+        nregs = {"a": 4, "b": 2, "c": wg_n // 2 if wg_n else 4}[role]
         if st.name not in self.frags:
             cells = [k.regs("f32" if role == "c" else "b32", nregs)
                      for _ in range(int(st.count or 1))]
             self.frags[st.name] = (role, dt, cells)
+            self.frag_shape[st.name] = str(st.shape)
         role0, dt0, cells = self.frags[st.name]
         if (role0, dt0, len(cells)) != (role, dt, int(st.count or 1)):
             raise LowerError(f"fragment {st.name!r} declared twice differently")
@@ -1018,17 +1054,24 @@ class Generic:
         k(f"shl.b32 {t}, {t}, 1")
         r0 = lo.coerce(lo.ev(st.dst_index[0]), "s32").reg
         c0 = lo.coerce(lo.ev(st.dst_index[1]), "s32").reg
+        if wgmma_n(self.frag_shape.get(name)):
+            # warpgroup accumulator: warp w of the group holds rows 16w..16w+15
+            wr = k.reg("s32")
+            k(f"shr.b32 {wr}, {self.tid}, 5")
+            k(f"and.b32 {wr}, {wr}, 3")
+            k(f"mad.lo.s32 {g}, {wr}, 16, {g}")
         mg = lo.coerce(lo.ev(st.m_guard), "s32").reg if st.m_guard is not None else None
         ng = lo.coerce(lo.ev(st.n_guard), "s32").reg if st.n_guard is not None else None
         dt = self.spec.args[st.dst_buffer].dtype
-        for i, v in enumerate(regs):
+        for e, v in enumerate(regs):
+            j, i = e // 4, e % 4
             row, col, idx = k.reg("s32"), k.reg("s32"), k.reg("s32")
             k(f"add.s32 {row}, {r0}, {g}")
             if i // 2:
                 k(f"add.s32 {row}, {row}, 8")
             k(f"add.s32 {col}, {c0}, {t}")
-            if i % 2:
-                k(f"add.s32 {col}, {col}, 1")
+            if i % 2 or j:
+                k(f"add.s32 {col}, {col}, {8 * j + i % 2}")
             k(f"mad.lo.s32 {idx}, {row}, {ldm}, {col}")
             want = k.reg("pred")
             k("setp.eq.u32 {}, 0, 0".format(want))
@@ -1052,6 +1095,253 @@ class Generic:
             lo.mask = want
             self.store_elem(a, sh, dt, Val(v, "f32"), atomic=bool(st.atomic))
             lo.mask = saved
+
+
+    # -- warpgroup products on tcgen05 ----------------------------------------
+
+    def setup_wgmma(self) -> None:
+        """TMEM for every warpgroup's accumulators, allocated once by warp 0,
+        and one commit mbarrier per warpgroup."""
+        mmas = [st for st in ir.walk(self.spec.op.body) if isinstance(st, ir.WgmmaMma)]
+        if not mmas:
+            return
+        k = self.k
+        block = int(self.spec.block[0])
+        if block % 128:
+            raise LowerError("wgmma needs whole warpgroups (blocks of 128 threads)")
+        nwg = block // 128
+        cols: dict[str, int] = {}
+        for st in mmas:
+            n = wgmma_n(st.shape)
+            if not n:
+                raise LowerError(f"WgmmaMma shape {st.shape!r}")
+            name = str(st.c_frags).partition("[")[0]
+            cols[name] = max(cols.get(name, 0), n)
+        offs, total = {}, 0
+        for name, n in cols.items():
+            offs[name] = total
+            total += n
+        per_wg = max(32, 1 << (total - 1).bit_length())
+        ncols = max(32, 1 << (nwg * per_wg - 1).bit_length())
+        if ncols > 512:
+            raise LowerError(f"wgmma accumulators need {ncols} TMEM columns (512 at most)")
+        k.shared(f"\t.shared .align 8 .b64 emmy_wg_bar[{nwg}];")
+        k.shared("\t.shared .align 4 .u32 emmy_tmem_slot;")
+        p = k.reg("pred")
+        warp, wg = k.reg("u32"), k.reg("u32")
+        k(f"shr.u32 {warp}, {self.tid}, 5")
+        k(f"shr.u32 {wg}, {self.tid}, 7")
+        skip = k.label("wg_init")
+        k(f"setp.ne.u32 {p}, {self.tid}, 0")
+        k(f"@{p} bra {skip}")
+        for i in range(nwg):
+            k(f"mbarrier.init.shared::cta.b64 [emmy_wg_bar+{8 * i}], 1")
+        k("fence.mbarrier_init.release.cluster")
+        k.place(skip)
+        skip2 = k.label("wg_alloc")
+        k(f"setp.ne.u32 {p}, {warp}, 0")
+        k(f"@{p} bra {skip2}")
+        slot = k.reg("u32")
+        k(f"mov.u32 {slot}, emmy_tmem_slot")
+        k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{slot}], {ncols}")
+        k("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned")
+        k.place(skip2)
+        k("tcgen05.fence::before_thread_sync")
+        k("barrier.sync 0")
+        k("tcgen05.fence::after_thread_sync")
+        tmem, tcol, lanef, bar, ph, issuer = (k.reg("u32") for _ in range(6))
+        k(f"ld.shared.u32 {tmem}, [emmy_tmem_slot]")
+        k(f"mad.lo.u32 {tcol}, {wg}, {per_wg}, {tmem}")
+        k(f"and.b32 {lanef}, {warp}, 3")
+        k(f"shl.b32 {lanef}, {lanef}, 21")          # (32 * (warp % 4)) << 16
+        k(f"mov.u32 {bar}, emmy_wg_bar")
+        k(f"mad.lo.u32 {bar}, {wg}, 8, {bar}")
+        k(f"mov.u32 {ph}, 0")
+        ip = k.reg("pred")
+        k(f"and.b32 {issuer}, {self.tid}, 127")
+        k(f"setp.eq.u32 {ip}, {issuer}, 0")
+        self.wg = {"ncols": ncols, "offs": offs, "tmem": tmem, "tcol": tcol, "lane": lanef,
+                   "bar": bar, "ph": ph, "issuer": ip, "wg": wg, "resident": set(),
+                   "pending": False}
+
+    def finish_wgmma(self) -> None:
+        if self.wg is None:
+            return
+        k = self.k
+        if self.wg["resident"] or self.wg["pending"]:
+            raise LowerError("wgmma products left in flight at the end of the kernel")
+        k("tcgen05.fence::before_thread_sync")
+        k("barrier.sync 0")
+        p, warp = k.reg("pred"), k.reg("u32")
+        skip = k.label("wg_free")
+        k(f"shr.u32 {warp}, {self.tid}, 5")
+        k(f"setp.ne.u32 {p}, {warp}, 0")
+        k(f"@{p} bra {skip}")
+        k("tcgen05.fence::after_thread_sync")
+        k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {self.wg['tmem']}, {self.wg['ncols']}")
+        k.place(skip)
+
+    def wg_state(self):
+        return None if self.wg is None else (frozenset(self.wg["resident"]), self.wg["pending"])
+
+    def do_wgmma_desc(self, st: ir.WgmmaDescriptor) -> None:
+        k, lo = self.k, self.lo
+        if st.smem not in self.smem or dtype_info(self.smem[st.smem][1])[2] != 2:
+            raise LowerError("wgmma descriptors address a 16-bit Smem buffer")
+        swz = str(st.swizzle or "NONE")
+        if swz not in _WG_LAYOUT:
+            raise LowerError(f"wgmma descriptor swizzle {swz!r}")
+        shape, _, off = self.smem[st.smem]
+        if swz != "NONE" and off % 1024:
+            raise LowerError(f"swizzled wgmma operand {st.smem!r} needs 1024-byte alignment")
+        idx = st.smem_index if st.smem_index is not None else ir.Literal(0, None)
+        tup = idx if isinstance(idx, tuple) else (idx,)
+        el = self.flat(tup, shape if len(tup) > 1 else (numel(shape),)).reg
+        a, d = k.reg("u32"), k.reg("u64")
+        k(f"mad.lo.u32 {a}, {el}, 2, {self.smem_base}")
+        if off:
+            k(f"add.u32 {a}, {a}, {off}")
+        lbo, sbo = int(st.lbo_bytes or 0), int(st.sbo_bytes or 0)
+        fixed = ((lbo >> 4) << 16) | ((sbo >> 4) << 32) | (1 << 46) | (_WG_LAYOUT[swz] << 61)
+        t = k.reg("u32")
+        k(f"shr.u32 {t}, {a}, 4")
+        k(f"and.b32 {t}, {t}, 16383")
+        k(f"cvt.u64.u32 {d}, {t}")
+        k(f"or.b64 {d}, {d}, 0x{fixed:016X}")
+        self.wgdesc[st.name] = (d, el, st.smem, swz, lbo, sbo)
+
+    def wg_operand_ok(self, name: str, rows: int) -> str:
+        """Predicate: the operand's first byte is 16-byte aligned and every
+        byte the product reads lies inside its Smem buffer."""
+        k = self.k
+        if name not in self.wgdesc:
+            raise LowerError(f"unknown wgmma descriptor {name!r}")
+        _, el, smem, swz, lbo, sbo = self.wgdesc[name]
+        size = numel(self.smem[smem][0]) * 2
+        span = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}[swz]
+        b, t = k.reg("u32"), k.reg("u32")
+        ok, q = k.reg("pred"), k.reg("pred")
+        k(f"shl.b32 {b}, {el}, 1")
+        k(f"and.b32 {t}, {b}, 15")
+        k(f"setp.eq.u32 {ok}, {t}, 0")
+        if span:
+            # the 16-deep K slice stays inside one swizzled row
+            k(f"rem.u32 {t}, {b}, {span}")
+            k(f"setp.le.and.u32 {ok}, {t}, {span - 32}, {ok}")
+            k(f"sub.u32 {t}, {b}, {t}")
+            end = (rows // 8 - 1) * sbo + 8 * span
+        else:
+            k(f"mov.u32 {t}, {b}")
+            end = (rows // 8 - 1) * sbo + lbo + 8 * 16
+        k(f"setp.le.u32 {q}, {t}, {max(-1, size - end)}")
+        k(f"and.pred {ok}, {ok}, {q}")
+        if size - end < 0:
+            k(f"setp.ne.u32 {ok}, 0, 0")
+        return ok
+
+    def do_wgmma(self, st: ir.WgmmaMma) -> None:
+        k, lo, wg = self.k, self.lo, self.wg
+        n = wgmma_n(st.shape)
+        if wg is None or not n:
+            raise LowerError(f"WgmmaMma shape {st.shape!r}")
+        if st.a_frag is not None or st.a_desc is None or st.trans_a or st.trans_b:
+            raise LowerError("WgmmaMma: A and B K-major from shared-memory descriptors")
+        name, regs = self.frag_cell(st.c_frags)
+        if self.frags[name][0] != "c" or wgmma_n(self.frag_shape[name]) != n:
+            raise LowerError("WgmmaMma needs a c fragment of its own shape")
+        ab = dtype_info(st.ab_dtype)[0]
+        if ab not in ("bf16", "f16"):
+            raise LowerError(f"WgmmaMma of {st.ab_dtype!r}")
+        ok = self.wg_operand_ok(st.a_desc, 64)
+        okb = self.wg_operand_ok(st.b_desc, n)
+        k(f"and.pred {ok}, {ok}, {okb}")
+        col = k.reg("u32")
+        k(f"add.u32 {col}, {wg['tcol']}, {wg['offs'][name]}")
+        if name not in wg["resident"]:
+            ta = k.reg("u32")
+            k(f"add.u32 {ta}, {col}, {wg['lane']}")
+            k(f"tcgen05.st.sync.aligned.16x256b.x{n // 8}.b32 [{ta}], {{{', '.join(regs)}}}")
+            k("tcgen05.wait::st.sync.aligned")
+            wg["resident"].add(name)
+        # operands (written through either proxy) and C visible to the MMA
+        k("fence.proxy.async.shared::cta")
+        k("tcgen05.fence::before_thread_sync")
+        bid = "15" if int(self.spec.block[0]) == 128 else self.wg_barrier_id()
+        k(f"barrier.sync {bid}, 128")
+        k("tcgen05.fence::after_thread_sync")
+        sd = (lo.truthy(lo.ev(st.scale_d)).reg if hasattr(st.scale_d, "free_vars") else None)
+        if sd is None:
+            sd = k.reg("pred")
+            k(f"setp.ne.u32 {sd}, {1 if st.scale_d else 0}, 0")
+        fmt = 1 if ab == "bf16" else 0
+        idesc = (1 << 4) | (fmt << 7) | (fmt << 10) | ((n >> 3) << 17) | ((64 >> 4) << 24)
+        idr = k.reg("u32")
+        k(f"mov.u32 {idr}, {idesc}")
+        go, bad = k.reg("pred"), k.reg("pred")
+        k(f"and.pred {go}, {wg['issuer']}, {ok}")
+        k(f"not.pred {bad}, {ok}")
+        k(f"and.pred {bad}, {bad}, {wg['issuer']}")
+        old = k.reg("u32")
+        k(f"@{bad} atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_WGMMA}")
+        k(f"@{go} tcgen05.mma.cta_group::1.kind::f16 [{col}], {self.wgdesc[st.a_desc][0]}, "
+          f"{self.wgdesc[st.b_desc][0]}, {idr}, {sd}")
+
+    def wg_barrier_id(self) -> str:
+        """Named barrier of this thread's warpgroup: 15 - warpgroup."""
+        k = self.k
+        r = k.reg("u32")
+        k(f"sub.u32 {r}, 15, {self.wg['wg']}")
+        return r
+
+    def do_wgmma_commit(self, st: ir.WgmmaCommit) -> None:
+        wg = self.wg
+        if wg is None:
+            raise LowerError("WgmmaCommit without a WgmmaMma")
+        if wg["pending"]:
+            raise LowerError("two WgmmaCommit without a WgmmaWait between them")
+        self.k(f"@{wg['issuer']} tcgen05.commit.cta_group::1.mbarrier::arrive::one."
+               f"shared::cluster.b64 [{wg['bar']}]")
+        wg["pending"] = True
+
+    def do_wgmma_wait(self, st: ir.WgmmaWait) -> None:
+        k, wg = self.k, self.wg
+        if int(st.group or 0) != 0:
+            raise LowerError("WgmmaWait with groups left in flight")
+        if wg is None:
+            return
+        if not wg["pending"]:
+            if wg["resident"]:
+                raise LowerError("WgmmaWait on products that were never committed")
+            return
+        # bounded wait for this commit's phase, then the accumulators back
+        done, loop = k.label("wgw_done"), k.label("wgw")
+        p = k.reg("pred")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{wg['bar']}], {wg['ph']}")
+        k(f"@{p} bra {done}")
+        t0, t1 = k.reg("u64"), k.reg("u64")
+        k(f"mov.u64 {t0}, %globaltimer")
+        k.place(loop)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{wg['bar']}], {wg['ph']}, 100000")
+        k(f"@{p} bra {done}")
+        k(f"mov.u64 {t1}, %globaltimer")
+        k(f"sub.u64 {t1}, {t1}, {t0}")
+        k(f"setp.lt.u64 {p}, {t1}, {MBAR_WAIT_NS}")
+        k(f"@{p} bra {loop}")
+        old = k.reg("u32")
+        k(f"atom.global.cas.b32 {old}, [emmy_err], 0, {ERR_MBAR_WAIT}")
+        k.place(done)
+        k(f"xor.b32 {wg['ph']}, {wg['ph']}, 1")
+        k("tcgen05.fence::after_thread_sync")
+        for name in sorted(wg["resident"]):
+            regs = self.frags[name][2][0]
+            n = 2 * len(regs)
+            ta = k.reg("u32")
+            k(f"add.u32 {ta}, {wg['tcol']}, {wg['offs'][name]}")
+            k(f"add.u32 {ta}, {ta}, {wg['lane']}")
+            k(f"tcgen05.ld.sync.aligned.16x256b.x{n // 8}.b32 {{{', '.join(regs)}}}, [{ta}]")
+        k("tcgen05.wait::ld.sync.aligned")
+        wg["resident"].clear()
+        wg["pending"] = False
 
 
 def emit_generic(spec: KernelSpec, checked: bool = False) -> Module:

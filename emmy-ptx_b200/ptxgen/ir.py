@@ -573,6 +573,48 @@ class RegStore(Node):
     col_dim: Any = None
 
 
+# -- warpgroup tensor-core products (``wgmma``), starred in the same table
+#    (``TASK.md:162-172``)
+
+
+@dataclass(repr=False, eq=True)
+class WgmmaDescriptor(Node):
+    name: str
+    smem: str
+    smem_index: Any = None
+    swizzle: str = "B128"
+    lbo_bytes: Any = 16
+    sbo_bytes: Any = 1024
+
+
+@dataclass(repr=False, eq=True)
+class WgmmaMma(Node):
+    c_frags: str
+    b_desc: str
+    shape: Any = "m64n64k16"
+    ab_dtype: Any = "bf16"
+    a_desc: Any = None
+    a_frag: Any = None
+    scale_d: Any = 1
+    trans_a: Any = 0
+    trans_b: Any = 0
+
+
+@dataclass(repr=False, eq=True)
+class WgmmaFence(Node):
+    pass
+
+
+@dataclass(repr=False, eq=True)
+class WgmmaCommit(Node):
+    pass
+
+
+@dataclass(repr=False, eq=True)
+class WgmmaWait(Node):
+    group: int = 0
+
+
 # ---------------------------------------------------------------------------
 # graph level
 # ---------------------------------------------------------------------------
@@ -668,7 +710,8 @@ _CTORS: dict[str, Any] = {
         Write, Loop, StridedLoop, Cond, Smem, Sync, WarpShuffle, TreeHalve, CpAsyncCopy,
         CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue, TmaDescriptor,
         TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
-        RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
+        RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore, WgmmaDescriptor, WgmmaMma, WgmmaFence,
+        WgmmaCommit, WgmmaWait,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

@@ -28,7 +28,11 @@ re-derives the shape-dependent literals:
                      tile schedule fed by box copies instead of ``cp.async``;
 * ``matmul_mma``  -- a 16-bit matmul on warp-level tensor-core fragments
                      (``RegFragment``, ``LdmatrixLoad``, ``MmaSyncPtx``,
-                     ``RegStore``) fed by box copies.
+                     ``RegStore``) fed by box copies;
+* ``matmul_wgmma`` -- C = A.B^T (B given K-major, [N][K]) on warpgroup
+                     products (``WgmmaDescriptor``, ``WgmmaMma``,
+                     ``WgmmaFence/Commit/Wait``) over 128-byte-swizzled box
+                     copies.
 
 At the shipped shapes the generated bodies equal the shipped ones byte for
 byte (``tests/test_irgen.py``); that pins the generator to the reference's
@@ -44,7 +48,8 @@ from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCo
                  CpAsyncWait, Dim, ElementwiseImpl, Init, Let, Literal, Load, Loop,
                  LdmatrixLoad, MbarrierArriveExpectTx, MbarrierInit, MbarrierWait, MmaSyncPtx,
                  RegFragment, RegStore, SetMaxNReg, Smem, StridedLoop, Sync, TernaryExpr, Tile,
-                 TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, Window, Write, datatype)
+                 TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, WgmmaCommit,
+                 WgmmaDescriptor, WgmmaFence, WgmmaMma, WgmmaWait, Window, Write, datatype)
 
 F32 = datatype("f32")
 
@@ -985,6 +990,63 @@ def matmul_mma(m: int, n: int, k: int, dtype="bf16", m_valid=None, n_valid=None,
     return package(entry, "matmul", [tl], [("x0", (m, k), dtype, 0), ("x1", (k, n), dtype, 1)],
                    [], ("matmul", (m, n), "f32"), ["x0", "x1", "matmul"],
                    ((m // BM) * (n // BN), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid)
+
+
+def matmul_wgmma(m: int, n: int, k: int, dtype="bf16", bn=64, groups=1, swizzle="B128",
+                 m_valid=None, n_valid=None, entry="k_matmul_wgmma", pid="matmul_wgmma"):
+    """C[m, n] = sum_k A[m, k] * Bt[n, k] (A, Bt bf16 or f16, C f32): each
+    warpgroup owns a 64 x ``bn`` C tile (``groups`` warpgroups per CTA, tiles
+    stacked along M); per K step of 64 thread 0 brings A (64*groups x 64)
+    and Bt (bn x 64) with two box copies (``swizzle``), then each group
+    issues four k16 products from descriptors that advance 32 bytes along
+    the swizzled rows, commits and waits."""
+    BK, TH = 64, 128 * groups
+    BM = 64 * groups
+    if m % BM or n % bn or k % BK:
+        raise ValueError("matmul_wgmma shape must tile by (64*groups) x bn x 64")
+    t = V("t")
+    nb = (BM * BK + bn * BK) * 2
+    cshape = f"m64n{bn}k16"
+    body = [TmaDescriptor(name="dA", src_buf="x0", src_shape=(m, k), box_extents=(BM, BK),
+                          swizzle=swizzle, dtype=dtype),
+            TmaDescriptor(name="dB", src_buf="x1", src_shape=(n, k), box_extents=(bn, BK),
+                          swizzle=swizzle, dtype=dtype),
+            Smem(name="_a_smem", extents=(BM, BK), dtype=_SMEM_C[dtype], align=1024),
+            Smem(name="_b_smem", extents=(bn, BK), dtype=_SMEM_C[dtype], align=1024),
+            Smem(name="bar", extents=(1,), dtype=_MBAR, align=8),
+            RegFragment(name="fc", role="c", shape=cshape, dtype="f32", count=1,
+                        nregs=bn // 2),
+            Cond(cond=EQ(t, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
+                 else_body=()),
+            Sync(barrier_id=0, count=None, warp=False)]
+    copies = [TmaLoad(smem="_a_smem", smem_index=L(0), desc="dA",
+                      coords=(MUL(V("bm"), L(BM)), V("_ks")), mbar="bar", mbar_slot=L(0)),
+              TmaLoad(smem="_b_smem", smem_index=L(0), desc="dB",
+                      coords=(MUL(V("bn"), L(bn)), V("_ks")), mbar="bar", mbar_slot=L(0))]
+    grp = DIV(V("t"), L(128))
+    ks = [_tma_issue(t, copies, nb),
+          MbarrierWait(mbar="bar", phase=DIV(V("_ks"), L(BK)), slot=L(0)),
+          WgmmaFence()]
+    for j in range(BK // 16):
+        ks += [WgmmaDescriptor(name="da", smem="_a_smem",
+                               smem_index=ADD(MUL(grp, L(64 * BK)), L(16 * j)),
+                               swizzle=swizzle, lbo_bytes=16, sbo_bytes=1024),
+               WgmmaDescriptor(name="db", smem="_b_smem", smem_index=L(16 * j), swizzle=swizzle,
+                               lbo_bytes=16, sbo_bytes=1024),
+               WgmmaMma(c_frags="fc", b_desc="db", shape=cshape, ab_dtype=dtype, a_desc="da",
+                        scale_d=BinaryExpr(op=">", left=ADD(V("_ks"), L(16 * j)), right=L(0)))]
+    ks += [WgmmaCommit(), WgmmaWait(group=0), Sync(barrier_id=0, count=None, warp=False)]
+    body.append(strided("_ks", k, L(0), L(BK), ks))
+    body.append(RegStore(dst_buffer="matmul",
+                         dst_index=(ADD(MUL(V("bm"), L(BM)), MUL(grp, L(64))),
+                                    MUL(V("bn"), L(bn))),
+                         frag="fc", shape=cshape,
+                         m_guard=None if m_valid is None else L(m_valid),
+                         n_guard=None if n_valid is None else L(n_valid)))
+    tl = tile([ax("bm", m // BM), ax("bn", n // bn), ax("t", TH)], body, block_threads=TH)
+    return package(entry, "matmul", [tl], [("x0", (m, k), dtype, 0), ("x1", (n, k), dtype, 1)],
+                   [], ("matmul", (m, n), "f32"), ["x0", "x1", "matmul"],
+                   ((m // BM) * (n // bn), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid)
 
 
 def bench_kernels():

@@ -347,6 +347,28 @@ def mma_layout(role: str):
     return g + 8 * (i // 2), 2 * t + (i % 2)
 
 
+def wgmma_n(shape) -> int:
+    """N of an ``m64nNk16`` shape string (0 for any other)."""
+    s = str(shape)
+    if s.startswith("m64n") and s.endswith("k16"):
+        n = int(s[4:-3])
+        if n % 8 == 0 and 8 <= n <= 256:
+            return n
+    return 0
+
+
+def wgmma_c_layout(n: int):
+    """Row and column of the N/2 accumulator elements of each of the 128
+    threads of a warpgroup for an m64nNk16 product: warp w holds rows
+    16w..16w+15 as N/8 blocks of the m16n8 accumulator layout."""
+    tid = np.arange(128)
+    w, lane = (tid >> 5)[:, None], tid & 31
+    g, t = (lane >> 2)[:, None], (lane & 3)[:, None]
+    e = np.arange(n // 2)[None]
+    j, i = e // 4, e % 4
+    return 16 * w + g + 8 * (i // 2), 8 * j + 2 * t + (i % 2)
+
+
 def _kind_np(dt: np.dtype) -> str:
     if _BF16 is not None and dt == np.dtype(_BF16):
         return "f32"
@@ -408,10 +430,14 @@ class Machine:
             ir.MbarrierArrive: self.do_mbarrier, ir.MbarrierWait: self.do_mbarrier,
             ir.SetMaxNReg: self.do_nothing, ir.RegFragment: self.do_reg_fragment,
             ir.LdmatrixLoad: self.do_ldmatrix, ir.MmaSyncPtx: self.do_mma_sync,
-            ir.RegStore: self.do_reg_store,
+            ir.RegStore: self.do_reg_store, ir.WgmmaDescriptor: self.do_wgmma_desc,
+            ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: self.do_nothing,
+            ir.WgmmaCommit: self.do_nothing, ir.WgmmaWait: self.do_wgmma_wait,
         }
+        self.wg_desc: dict[str, tuple] = {}
         self.frags: dict[str, np.ndarray] = {}
         self.frag_role: dict[str, tuple[str, str]] = {}
+        self.frag_shape: dict[str, str] = {}
         self.tma_descs = {st.name: st for st in ir.walk(spec.op.body)
                           if isinstance(st, ir.TmaDescriptor)}
 
@@ -972,16 +998,18 @@ class Machine:
 
     def do_reg_fragment(self, st: ir.RegFragment) -> None:
         role = str(st.role).lower()
-        if str(st.shape) != "m16n8k16":
-            raise NotImplementedError(f"fragment shape {st.shape!r}")
+        wg_n = wgmma_n(st.shape)
+        if str(st.shape) != "m16n8k16" and not (role == "c" and wg_n):
+            raise NotImplementedError(f"{role} fragment shape {st.shape!r}")
         dt = dtype_info(st.dtype)[0]
         if role in ("a", "b") and dt not in ("bf16", "f16"):
             raise NotImplementedError(f"{role} fragment of {st.dtype!r}")
         if role == "c" and dt != "f32":
             raise NotImplementedError(f"c fragment of {st.dtype!r}")
-        elems = {"a": 8, "b": 4, "c": 4}[role]
+        elems = {"a": 8, "b": 4, "c": wg_n // 2 if wg_n else 4}[role]
         self.frags[st.name] = np.zeros((int(st.count or 1), self.n, elems), np.float32)
         self.frag_role[st.name] = (role, dt)
+        self.frag_shape[st.name] = str(st.shape)
 
     def do_ldmatrix(self, st: ir.LdmatrixLoad) -> None:
         """Fill one A or B cell from a 16-bit Smem buffer.  ``src_index`` =
@@ -1049,6 +1077,85 @@ class Machine:
         D = (np.einsum("wmk,wkn->wmn", A, B) + Cm).astype(np.float32)
         self.frags[cn][cc] = D[:, cr, ccl].reshape(self.n, -1)
 
+    # -- warpgroup products (wgmma) ------------------------------------------
+    # Starred (``TASK.md:162-172``), no behaviour in the reference; defined
+    # here for m64nNk16 with 16-bit A and B read from shared memory through
+    # descriptors, both K-major (A [M][K], B [N][K]), and an f32 C fragment
+    # per warpgroup (``wgmma_c_layout``).  A product lands at once; fence,
+    # commit and wait order it on the GPU.  Warpgroup-collective: every lane
+    # of the group takes part whatever the lane mask.
+
+    def do_wgmma_desc(self, st: ir.WgmmaDescriptor) -> None:
+        """Record a descriptor: the Smem buffer, the element where the
+        operand starts (the same on every lane of a warpgroup), the layout
+        (``swizzle`` NONE, B32, B64 or B128) and its byte strides."""
+        if st.smem not in self.smem or self.smem[st.smem].dtype.itemsize != 2:
+            raise ValueError("wgmma descriptors address a 16-bit Smem buffer")
+        idx = st.smem_index if st.smem_index is not None else ir.Literal(0, None)
+        idx = idx if isinstance(idx, tuple) else (idx,)
+        shape = self.smem_decl[st.smem][0] if len(idx) > 1 else (self.smem[st.smem][0].size,)
+        start = self.lane_flat(idx, shape)
+        g = self._warpgroups()
+        s2 = start.reshape(g, 128)
+        if np.any(s2 != s2[:, :1]):
+            raise ValueError("wgmma descriptor start differs within a warpgroup")
+        self.wg_desc[st.name] = (st.smem, s2[:, 0].astype(np.int64), str(st.swizzle or "NONE"),
+                                 int(st.lbo_bytes or 0), int(st.sbo_bytes or 0))
+
+    def _warpgroups(self) -> int:
+        if self.T % 128:
+            raise ValueError("wgmma needs whole warpgroups (blocks of 128 threads)")
+        return self.n // 128
+
+    def _wgmma_operand(self, name: str, rows: int) -> np.ndarray:
+        """[warpgroups, rows, 16] values of a K-major operand."""
+        smem, start, swz, lbo, sbo = self.wg_desc[name]
+        view = self.smem[smem].reshape(self.count, -1)
+        r = np.arange(rows)[:, None]
+        kk = np.arange(16)[None]
+        b0 = start[:, None, None] * 2
+        span = _TMA_SWIZZLE[swz]
+        if not span:
+            b = b0 + (r // 8) * sbo + (kk // 8) * lbo + (r % 8) * 16 + (kk % 8) * 2
+        else:
+            if np.any(b0 % span + 32 > span):
+                raise ValueError("wgmma K slice crosses a swizzled row")
+            b = b0 + (r // 8) * sbo + (r % 8) * span + kk * 2
+            b = b ^ (((b >> 7) & (span // 16 - 1)) << 4)
+        el = b // 2
+        if np.any((el < 0) | (el >= view.shape[1])):
+            raise IndexError(f"wgmma operand outside {smem!r}")
+        cta = self.local.reshape(-1, 128)[:, 0]
+        return view[cta[:, None, None], el].astype(np.float64)
+
+    def do_wgmma(self, st: ir.WgmmaMma) -> None:
+        """c = a . b (+ c when ``scale_d``) for each warpgroup: M = 64 rows of
+        A and N rows of B (B [N][K]) over K = 16, exact products summed with
+        the accumulator and rounded once to f32."""
+        n = wgmma_n(st.shape)
+        if not n or st.a_frag is not None or st.a_desc is None or st.trans_a or st.trans_b:
+            raise NotImplementedError("WgmmaMma: m64nNk16, A and B K-major from descriptors")
+        g = self._warpgroups()
+        name, cell = self._frag_ref(st.c_frags)
+        if wgmma_n(self.frag_shape[name]) != n:
+            raise ValueError("WgmmaMma shape and its c fragment differ")
+        A = self._wgmma_operand(st.a_desc, 64)
+        B = self._wgmma_operand(st.b_desc, n)
+        cr, ccl = wgmma_c_layout(n)
+        cf = self.frags[name][cell].reshape(g, 128, -1)
+        C = np.zeros((g, 64, n))
+        C[:, cr, ccl] = cf
+        sd = np.broadcast_to(truthy(self.ev(st.scale_d)) if hasattr(st.scale_d, "free_vars")
+                             else bool(st.scale_d), (self.n,)).reshape(g, 128)
+        if np.any(sd != sd[:, :1]):
+            raise ValueError("wgmma scale_d differs within a warpgroup")
+        D = np.einsum("gmk,gnk->gmn", A, B) + np.where(sd[:, :1, None], C, 0.0)
+        self.frags[name][cell] = D.astype(np.float32)[:, cr, ccl].reshape(self.n, -1)
+
+    def do_wgmma_wait(self, st: ir.WgmmaWait) -> None:
+        if int(st.group or 0) != 0:
+            raise NotImplementedError("WgmmaWait with groups left in flight")
+
     def do_reg_store(self, st: ir.RegStore) -> None:
         """Each active lane stores its C elements: element (m, n) of the cell
         to (r0 + m) * ldm + c0 + n of the buffer (``ldm`` defaults to its
@@ -1067,8 +1174,13 @@ class Machine:
         ldm = int(st.ldm) if st.ldm is not None else int(arr.shape[-1])
         r0 = np.broadcast_to(as_int64(self.ev(st.dst_index[0])), (self.n,))
         c0 = np.broadcast_to(as_int64(self.ev(st.dst_index[1])), (self.n,))
-        cr, ccl = mma_layout("c")
-        lane = (self.tid & 31).astype(np.int64)
+        wg_n = wgmma_n(self.frag_shape[name])
+        if wg_n:
+            cr, ccl = wgmma_c_layout(wg_n)
+            lane = (self.tid & 127).astype(np.int64)
+        else:
+            cr, ccl = mma_layout("c")
+            lane = (self.tid & 31).astype(np.int64)
         rows = r0[:, None] + cr[lane]
         cols = c0[:, None] + ccl[lane]
         ok = np.broadcast_to(self.live()[:, None], rows.shape).copy()

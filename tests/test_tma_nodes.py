@@ -211,3 +211,80 @@ def test_fragment_kernels_assemble(tmp_path):
         r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
                            capture_output=True, text=True)
         assert r.returncode == 0, r.stderr[-2000:]
+
+
+# -- warpgroup products ------------------------------------------------------------
+
+def _wgmma_inputs(m, n, k, dt, seed=0):
+    from oracle.interp import storage_dtype
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((m, k)).astype(storage_dtype(dt)),
+            rng.standard_normal((n, k)).astype(storage_dtype(dt)))
+
+
+def _wgmma_reference(a, bt):
+    """One rounding to f32 per k16 product, in K order."""
+    a64, b64 = a.astype(np.float64), bt.astype(np.float64)
+    c = np.zeros((a.shape[0], bt.shape[0]), np.float32)
+    for k0 in range(0, a.shape[1], 16):
+        c = (a64[:, k0:k0 + 16] @ b64[:, k0:k0 + 16].T + c).astype(np.float32)
+    return c
+
+
+def test_wgmma_c_layout_covers_the_tile_once():
+    from oracle.interp import wgmma_c_layout
+    for n in (8, 64, 256):
+        r, c = wgmma_c_layout(n)
+        cells = set(zip(r.ravel().tolist(), c.ravel().tolist()))
+        assert len(cells) == r.size == 64 * n
+
+
+@pytest.mark.parametrize("args", [(128, 64, 128, "bf16", 64, 1), (128, 128, 64, "f16", 128, 2),
+                                  (64, 256, 192, "bf16", 256, 1)])
+def test_oracle_matmul_wgmma(args):
+    m, n, k, dt, bn, g = args
+    spec = load_kernel_data(*irgen.matmul_wgmma(m, n, k, dt, bn, g), "wg")
+    a, bt = _wgmma_inputs(m, n, k, dt)
+    got = interpret(spec, {"x0": a, "x1": bt})["matmul"]
+    assert np.array_equal(got, _wgmma_reference(a, bt))
+
+
+def test_wgmma_nodes_round_trip():
+    nodes = [ir.WgmmaDescriptor(name="da", smem="s", smem_index=irgen.L(16), swizzle="B128",
+                                lbo_bytes=16, sbo_bytes=1024),
+             ir.WgmmaMma(c_frags="fc", b_desc="db", shape="m64n64k16", ab_dtype="bf16",
+                         a_desc="da", scale_d=irgen.L(1)),
+             ir.WgmmaFence(), ir.WgmmaCommit(), ir.WgmmaWait(group=0)]
+    for n in nodes:
+        assert ir.parse_stmt(repr(n)) == n
+
+
+def test_wgmma_lowering_refuses_uncommitted_loops():
+    """Products issued in a loop iteration must be committed and waited for
+    in it: the accumulators move between registers and TMEM there."""
+    gm = irgen.matmul_wgmma(64, 64, 128)
+    spec = load_kernel_data(gm[0], gm[1], "wgbad")
+    tl = spec.op.body[0]
+    body = list(tl.body)
+    loop_i = next(i for i, s_ in enumerate(body) if isinstance(s_, ir.StridedLoop))
+    lp = body[loop_i]
+    lp.body = tuple(s_ for s_ in lp.body if not isinstance(s_, (ir.WgmmaCommit, ir.WgmmaWait)))
+    with pytest.raises(LowerError, match="loop iteration"):
+        emit_generic(spec)
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+def test_wgmma_kernels_assemble(tmp_path):
+    for i, gm in enumerate((irgen.matmul_wgmma(128, 64, 128, "bf16", 64, 1),
+                            irgen.matmul_wgmma(128, 128, 64, "f16", 128, 2),
+                            irgen.matmul_wgmma(64, 256, 64, "bf16", 256, 1))):
+        ptx = compile_kernel(load_kernel_data(gm[0], gm[1], f"w{i}"))
+        for op in ("tcgen05.alloc", "tcgen05.mma.cta_group::1.kind::f16", "tcgen05.commit",
+                   "tcgen05.st.sync.aligned.16x256b", "tcgen05.ld.sync.aligned.16x256b",
+                   "tcgen05.dealloc"):
+            assert op in ptx
+        f = tmp_path / f"w{i}.ptx"
+        f.write_text(ptx)
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-2000:]
