@@ -58,7 +58,7 @@ under meta.json's launch, with the semantics of the golden model
 
 from __future__ import annotations
 
-from . import ir
+from . import ir, ops
 from .analysis import NoMatch, numel
 from .lower import Lowerer, LowerError, Val, storage_kind, value_kind
 from .model import KernelSpec, dtype_info
@@ -78,6 +78,7 @@ ERR_MBAR_WAIT = 0x304    # an mbarrier wait ran past its limit
 ERR_TMA = 0x305          # a TMA box copy that breaks its alignment or bounds (skipped)
 ERR_FRAG = 0x306         # a fragment load or store outside its buffer (skipped)
 ERR_WGMMA = 0x307        # a wgmma operand outside its buffer or misaligned (skipped)
+ERR_SMEM = 0x308         # launched with less dynamic shared memory than the layout needs
 _WG_LAYOUT = {"NONE": 0, "B32": 6, "B64": 4, "B128": 2}   # tcgen05 descriptor bits 61-63
 
 
@@ -153,6 +154,8 @@ class Generic:
             ir.RegStore: self.do_reg_store, ir.WgmmaDescriptor: self.do_wgmma_desc,
             ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: lambda st: None,
             ir.WgmmaCommit: self.do_wgmma_commit, ir.WgmmaWait: self.do_wgmma_wait,
+            ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
+            ir.FragmentRepack: self.do_frag_repack,
         }
         self.frags: dict[str, tuple] = {}    # name -> (role, dtype, [[regs] per cell])
         self.wg = None                       # warpgroup tensor-core state (setup_wgmma)
@@ -195,6 +198,17 @@ class Generic:
         if self.spec.smem_bytes > 0 or off > 48 * 1024:
             self.mod.add_global(f".extern .shared .align {al} .b8 emmy_dyn_smem[];")
             self.dyn = True
+            # a launch with less dynamic shared memory than the layout uses
+            # (meta.json's smem_bytes may be smaller) reports and returns at
+            # once, before any shared access or barrier
+            dsz, ok = k.reg("u32"), k.reg("pred")
+            fine = k.label("smem_ok")
+            k(f"mov.u32 {dsz}, %dynamic_smem_size")
+            k(f"setp.ge.u32 {ok}, {dsz}, {off}")
+            k(f"@{ok} bra {fine}")
+            k(f"st.global.u32 [emmy_err], {ERR_SMEM}")
+            k("ret")
+            k.place(fine)
             r = k.reg("u32")
             k(f"mov.u32 {r}, emmy_dyn_smem")
         else:
@@ -230,7 +244,8 @@ class Generic:
         self.mod.plan = {"entry": spec.entry, "kind": "generic", "block": int(spec.block[0]),
                          "grid_max": int(spec.grid[0] * spec.grid[1] * spec.grid[2]),
                          "grid_per_sm": 0,
-                         "smem": int(spec.smem_bytes if self.smem and self.dyn else 0),
+                         "smem": int(max(spec.smem_bytes, self.smem_bytes)
+                                     if self.smem and self.dyn else 0),
                          "geometry": "meta"}
         if self.checked:
             self.mod.plan["checked"] = True
@@ -1096,6 +1111,76 @@ class Generic:
             self.store_elem(a, sh, dt, Val(v, "f32"), atomic=bool(st.atomic))
             lo.mask = saved
 
+
+    def c_cell(self, ref) -> list:
+        name, regs = self.frag_cell(ref)
+        if self.frags[name][0] != "c" or self.frag_shape[name] != "m16n8k16":
+            raise LowerError(f"{ref!r} is not an m16n8 c fragment")
+        return regs
+
+    def do_frag_apply(self, st: ir.FragmentApply) -> None:
+        """op per element of an m16n8 c cell with the IR's op lowering;
+        "row" arguments give top to elements 0-1 (row g), bot to 2-3."""
+        k, lo = self.k, self.lo
+        if st.layout is not None or st.post is not None:
+            raise LowerError("FragmentApply layout / post")
+        out = self.c_cell(st.out)
+        if len(st.args) != len(st.kinds):
+            raise LowerError("FragmentApply args and kinds differ in length")
+        cols = []
+        if st.in_place:
+            cols.append(lambda e: Val(out[e], "f32"))
+        for a, kd in zip(st.args, st.kinds):
+            if kd == "frag":
+                src = self.c_cell(a)
+                cols.append(lambda e, src=src: Val(src[e], "f32"))
+            elif kd == "row":
+                top, bot = (lo.env[x] for x in a)
+                cols.append(lambda e, top=top, bot=bot: bot if e >= 2 else top)
+            elif kd == "scalar":
+                v = lo.env[a] if isinstance(a, str) else lo.ev(a)
+                cols.append(lambda e, v=v: v)
+            else:
+                raise LowerError(f"FragmentApply argument kind {kd!r}")
+        opname = getattr(st.op, "name", st.op)
+        res = [lo.coerce(lo.apply(opname, [f(e) for f in cols]), "f32") for e in range(4)]
+        g = self.guard()
+        for e in range(4):
+            k(f"{g}mov.f32 {out[e]}, {res[e].reg}")
+
+    def do_frag_rowreduce(self, st: ir.FragmentRowReduce) -> None:
+        k, lo = self.k, self.lo
+        refs = [st.frags] if isinstance(st.frags, str) else list(st.frags)
+        cells = [self.c_cell(r) for r in refs]
+        opname = ops.canon(getattr(st.op, "name", st.op))
+        if opname not in ("add", "maximum", "minimum"):
+            raise LowerError(f"FragmentRowReduce op {st.op!r}")
+        for half, name in ((0, st.top), (1, st.bot)):
+            v = None
+            for c in cells:
+                for e in (2 * half, 2 * half + 1):
+                    x = Val(c[e], "f32")
+                    v = x if v is None else lo.coerce(lo.apply(opname, [v, x]), "f32")
+            for x in (1, 2):
+                t = k.reg("f32")
+                k(f"shfl.sync.bfly.b32 {t}, {v.reg}, {x}, 31, -1")
+                v = lo.coerce(lo.apply(opname, [v, Val(t, "f32")]), "f32")
+            lo.bind(name, v)
+
+    def do_frag_repack(self, st: ir.FragmentRepack) -> None:
+        k = self.k
+        if st.fragment_layout is not None or st.part is not None:
+            raise LowerError("FragmentRepack layout / part")
+        name, regs = self.frag_cell(st.frag)
+        role, dt = self.frags[name][0], self.frags[name][1]
+        if role != "a" or dtype_info(st.ab_dtype)[0] != dt:
+            raise LowerError("FragmentRepack fills an a fragment of its own type")
+        if len(st.srcs) != 2:
+            raise LowerError("FragmentRepack takes two c cells")
+        src = self.c_cell(st.srcs[0]) + self.c_cell(st.srcs[1])
+        for j in range(4):
+            # element 2j in the low half, 2j + 1 in the high half
+            k(f"cvt.rn.{dt}x2.f32 {regs[j]}, {src[2 * j + 1]}, {src[2 * j]}")
 
     # -- warpgroup products on tcgen05 ----------------------------------------
 

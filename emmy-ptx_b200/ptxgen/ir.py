@@ -573,6 +573,38 @@ class RegStore(Node):
     col_dim: Any = None
 
 
+@dataclass(repr=False, eq=True)
+class FragmentApply(Node):
+    out: str
+    op: Any
+    args: tuple = ()
+    kinds: tuple = ()
+    in_place: bool = True
+    layout: Any = None
+    post: Any = None
+    row_base: Any = None
+    col_base: Any = None
+
+
+@dataclass(repr=False, eq=True)
+class FragmentRowReduce(Node):
+    top: str
+    bot: str
+    frags: Any = ()
+    op: Any = "add"
+    layout: Any = None
+    dtype: Any = "f32"
+
+
+@dataclass(repr=False, eq=True)
+class FragmentRepack(Node):
+    frag: str
+    srcs: tuple = ()
+    ab_dtype: Any = "bf16"
+    fragment_layout: Any = None
+    part: Any = None
+
+
 # -- warpgroup tensor-core products (``wgmma``), starred in the same table
 #    (``TASK.md:162-172``)
 
@@ -711,7 +743,7 @@ _CTORS: dict[str, Any] = {
         CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue, TmaDescriptor,
         TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
         RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore, WgmmaDescriptor, WgmmaMma, WgmmaFence,
-        WgmmaCommit, WgmmaWait,
+        WgmmaCommit, WgmmaWait, FragmentApply, FragmentRowReduce, FragmentRepack,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

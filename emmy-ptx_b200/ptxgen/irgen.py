@@ -29,6 +29,11 @@ re-derives the shape-dependent literals:
 * ``matmul_mma``  -- a 16-bit matmul on warp-level tensor-core fragments
                      (``RegFragment``, ``LdmatrixLoad``, ``MmaSyncPtx``,
                      ``RegStore``) fed by box copies;
+* ``attention_mma`` -- softmax(Q K^T / sqrt(D)) V in fragments: S cells
+                     by ``mma.sync``, row max and sum by
+                     ``FragmentRowReduce``, scaling and exp by
+                     ``FragmentApply``, P turned into A cells by
+                     ``FragmentRepack`` for the P V products;
 * ``matmul_wgmma`` -- C = A.B^T (B given K-major, [N][K]) on warpgroup
                      products (``WgmmaDescriptor``, ``WgmmaMma``,
                      ``WgmmaFence/Commit/Wait``) over 128-byte-swizzled box
@@ -49,7 +54,8 @@ from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCo
                  LdmatrixLoad, MbarrierArriveExpectTx, MbarrierInit, MbarrierWait, MmaSyncPtx,
                  RegFragment, RegStore, SetMaxNReg, Smem, StridedLoop, Sync, TernaryExpr, Tile,
                  TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, WgmmaCommit,
-                 WgmmaDescriptor, WgmmaFence, WgmmaMma, WgmmaWait, Window, Write, datatype)
+                 WgmmaDescriptor, WgmmaFence, WgmmaMma, WgmmaWait, Window, Write, datatype,
+                 FragmentApply, FragmentRepack, FragmentRowReduce)
 
 F32 = datatype("f32")
 
@@ -1047,6 +1053,94 @@ def matmul_wgmma(m: int, n: int, k: int, dtype="bf16", bn=64, groups=1, swizzle=
     return package(entry, "matmul", [tl], [("x0", (m, k), dtype, 0), ("x1", (n, k), dtype, 1)],
                    [], ("matmul", (m, n), "f32"), ["x0", "x1", "matmul"],
                    ((m // BM) * (n // bn), 1, 1), (TH, 1, 1), rtol=1e-3, atol=1e-3, pid=pid)
+
+
+def attention_mma(bh: int, s: int, d: int, dtype="bf16", entry="k_attention_mma",
+                  pid="attention_mma"):
+    """out = softmax(q k^T / sqrt(d)) v per batch*head (q, k, v [bh, s, d] in
+    bf16 or f16, out f32), flash style on m16n8k16 fragments: a CTA of four
+    warps owns 64 query rows (16 per warp, Q cells loaded once); per block
+    of 64 keys thread 0 brings K and V with two box copies, each warp forms
+    its 16 x 64 S in eight c cells, takes the row max (``FragmentRowReduce``),
+    rescales its running max, sum and O cells (``FragmentApply`` with row
+    pairs), exponentiates S in place, repacks it into four A cells
+    (``FragmentRepack``) and accumulates P V; O / l is stored at the end."""
+    BQ, BKV, TH = 64, 64, 128
+    if s % BQ or d % 16 or d > 128:
+        raise ValueError("attention_mma needs s a multiple of 64 and d a multiple of 16, <= 128")
+    t = V("t")
+    nk, no = d // 16, d // 8
+    row0 = ADD(MUL(V("bh"), L(s)), MUL(V("qb"), L(BQ)))
+    body = [TmaDescriptor(name=f"d{x}", src_buf=x, src_shape=(bh * s, d), box_extents=(BQ, d),
+                          swizzle="NONE", dtype=dtype) for x in ("q", "k", "v")]
+    body += [Smem(name=f"_{x}", extents=(BQ, d), dtype=_SMEM_C[dtype], align=128)
+             for x in ("q", "k", "v")]
+    body += [Smem(name="bar", extents=(1,), dtype=_MBAR, align=8),
+             RegFragment(name="fq", role="a", shape="m16n8k16", dtype=dtype, count=nk, nregs=4),
+             RegFragment(name="fk", role="b", shape="m16n8k16", dtype=dtype, count=1, nregs=2),
+             RegFragment(name="fv", role="b", shape="m16n8k16", dtype=dtype, count=1, nregs=2),
+             RegFragment(name="fp", role="a", shape="m16n8k16", dtype=dtype, count=4, nregs=4),
+             RegFragment(name="fo", role="c", shape="m16n8k16", dtype="f32", count=no, nregs=4),
+             Let(name="sc", value=Lf(1.0 / math.sqrt(d)), dtype=F32)]
+    for nm, v0 in (("m_t", -1e30), ("m_b", -1e30), ("l_t", 0.0), ("l_b", 0.0)):
+        body.append(Init(name=nm, identity=v0, dtype=F32))
+    body += [Cond(cond=EQ(t, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
+                  else_body=()),
+             Sync(barrier_id=0, count=None, warp=False),
+             _tma_issue(t, [TmaLoad(smem="_q", smem_index=L(0), desc="dq", coords=(row0, L(0)),
+                                    mbar="bar", mbar_slot=L(0))], BQ * d * 2),
+             MbarrierWait(mbar="bar", phase=L(0), slot=L(0))]
+    body += [LdmatrixLoad(frag="fq", src_buffer="_q", src_index=(MUL(V("warp"), L(16)), L(16 * i)),
+                          role="a", fragment_index=L(i)) for i in range(nk)]
+    krow = ADD(MUL(V("bh"), L(s)), V("_j"))
+    blk = [_tma_issue(t, [TmaLoad(smem=f"_{x}", smem_index=L(0), desc=f"d{x}",
+                                  coords=(krow, L(0)), mbar="bar", mbar_slot=L(0))
+                          for x in ("k", "v")], 2 * BKV * d * 2),
+           MbarrierWait(mbar="bar", phase=ADD(L(1), DIV(V("_j"), L(BKV))), slot=L(0)),
+           RegFragment(name="fs", role="c", shape="m16n8k16", dtype="f32", count=8, nregs=4)]
+    for n in range(BKV // 8):
+        for i in range(nk):
+            blk += [LdmatrixLoad(frag="fk", src_buffer="_k", src_index=(L(8 * n), L(16 * i)),
+                                 role="b", b_trans=False),
+                    MmaSyncPtx(c_frag=f"fs[{n}]", a_frag=f"fq[{i}]", b_frag="fk",
+                               shape="m16n8k16", ab_dtype=dtype, c_dtype="f32")]
+    cells = tuple(f"fs[{n}]" for n in range(BKV // 8))
+    blk += [FragmentApply(out=c, op="multiply", args=("sc",), kinds=("scalar",)) for c in cells]
+    blk.append(FragmentRowReduce(top="bm_t", bot="bm_b", frags=cells, op="maximum"))
+    for h in ("t", "b"):
+        blk += [assign(f"mn_{h}", "maximum", f"m_{h}", f"bm_{h}"),
+                assign(f"dm_{h}", "subtract", f"m_{h}", f"mn_{h}"),
+                assign(f"al_{h}", "exp", f"dm_{h}")]
+    blk += [FragmentApply(out=c, op="subtract", args=(("mn_t", "mn_b"),), kinds=("row",))
+            for c in cells]
+    blk += [FragmentApply(out=c, op="exp", args=(), kinds=()) for c in cells]
+    blk.append(FragmentRowReduce(top="rs_t", bot="rs_b", frags=cells, op="add"))
+    for h in ("t", "b"):
+        blk += [assign(f"ls_{h}", "multiply", f"l_{h}", f"al_{h}"),
+                assign(f"l_{h}", "add", f"ls_{h}", f"rs_{h}"),
+                assign(f"m_{h}", "copy", f"mn_{h}")]
+    blk += [FragmentApply(out=f"fo[{c}]", op="multiply", args=(("al_t", "al_b"),),
+                          kinds=("row",)) for c in range(no)]
+    blk += [FragmentRepack(frag=f"fp[{i}]", srcs=(f"fs[{2 * i}]", f"fs[{2 * i + 1}]"),
+                           ab_dtype=dtype) for i in range(BKV // 16)]
+    for c in range(no):
+        for i in range(BKV // 16):
+            blk += [LdmatrixLoad(frag="fv", src_buffer="_v", src_index=(L(16 * i), L(8 * c)),
+                                 role="b", b_trans=True),
+                    MmaSyncPtx(c_frag=f"fo[{c}]", a_frag=f"fp[{i}]", b_frag="fv",
+                               shape="m16n8k16", ab_dtype=dtype, c_dtype="f32")]
+    blk.append(Sync(barrier_id=0, count=None, warp=False))
+    body.append(strided("_j", s, L(0), L(BKV), blk))
+    body += [FragmentApply(out=f"fo[{c}]", op="divide", args=(("l_t", "l_b"),), kinds=("row",))
+             for c in range(no)]
+    body += [RegStore(dst_buffer="out", dst_index=(ADD(row0, MUL(V("warp"), L(16))), L(8 * c)),
+                      frag="fo", fragment_index=L(c), ldm=d) for c in range(no)]
+    tl = tile([ax("bh", bh), ax("qb", s // BQ), ax("t", TH)], body, block_threads=TH)
+    return package(entry, "attention", [tl],
+                   [("q", (bh, s, d), dtype, 0), ("k", (bh, s, d), dtype, 1),
+                    ("v", (bh, s, d), dtype, 2)], [], ("out", (bh, s, d), "f32"),
+                   ["q", "k", "v", "out"], (bh * (s // BQ), 1, 1), (TH, 1, 1),
+                   rtol=1e-2, atol=1e-3, pid=pid)
 
 
 def bench_kernels():

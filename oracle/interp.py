@@ -433,6 +433,8 @@ class Machine:
             ir.RegStore: self.do_reg_store, ir.WgmmaDescriptor: self.do_wgmma_desc,
             ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: self.do_nothing,
             ir.WgmmaCommit: self.do_nothing, ir.WgmmaWait: self.do_wgmma_wait,
+            ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
+            ir.FragmentRepack: self.do_frag_repack,
         }
         self.wg_desc: dict[str, tuple] = {}
         self.frags: dict[str, np.ndarray] = {}
@@ -1076,6 +1078,91 @@ class Machine:
         Cm[:, cr, ccl] = cf
         D = (np.einsum("wmk,wkn->wmn", A, B) + Cm).astype(np.float32)
         self.frags[cn][cc] = D[:, cr, ccl].reshape(self.n, -1)
+
+    def _c_cell(self, ref):
+        name, cell = self._frag_ref(ref)
+        if self.frag_role[name][0] != "c" or self.frag_shape[name] != "m16n8k16":
+            raise ValueError(f"{ref!r} is not an m16n8 c fragment")
+        return name, cell
+
+    def do_frag_apply(self, st: ir.FragmentApply) -> None:
+        """out = op(out, *args) (``in_place``) or op(*args), element by
+        element of an m16n8 c cell, with the IR's op semantics.  Argument
+        kinds: "frag" (a c cell), "row" (a (top, bot) pair of per-lane names:
+        top for the lane's row g elements, bot for row g + 8), "scalar" (a
+        name or literal).  Lanes outside the mask keep their elements."""
+        if st.layout is not None or st.post is not None:
+            raise NotImplementedError("FragmentApply layout / post")
+        name, cell = self._c_cell(st.out)
+        args = list(st.args)
+        kinds = list(st.kinds)
+        if len(args) != len(kinds):
+            raise ValueError("FragmentApply args and kinds differ in length")
+        cur = self.frags[name][cell]
+        cols = []
+        if st.in_place:
+            cols.append(lambda e: Val("f32", cur[:, e]))
+        for a, kd in zip(args, kinds):
+            if kd == "frag":
+                an, ac = self._c_cell(a)
+                src = self.frags[an][ac]
+                cols.append(lambda e, src=src: Val("f32", src[:, e]))
+            elif kd == "row":
+                top, bot = (self.env[x] for x in a)
+                cols.append(lambda e, top=top, bot=bot: bot if e >= 2 else top)
+            elif kd == "scalar":
+                v = self.env[a] if isinstance(a, str) else self.ev(a)
+                cols.append(lambda e, v=v: v)
+            else:
+                raise NotImplementedError(f"FragmentApply argument kind {kd!r}")
+        opname = getattr(st.op, "name", st.op)
+        out = cur.copy()
+        for e in range(4):
+            r = coerce(apply_op(opname, [f(e) for f in cols]), "f32")
+            out[:, e] = np.broadcast_to(r.a, (self.n,))
+        m = self.live()
+        self.frags[name][cell] = np.where(m[:, None], out, cur)
+
+    def do_frag_rowreduce(self, st: ir.FragmentRowReduce) -> None:
+        """top / bot = op over the lane's row-g / row-(g + 8) elements of the
+        cells in ``frags`` (in order, two elements per cell), then over the
+        four lanes of the row (exchanges with lane ^ 1, then lane ^ 2): every
+        lane of the quad gets the same row value."""
+        refs = [st.frags] if isinstance(st.frags, str) else list(st.frags)
+        cells = [self.frags[n][c] for n, c in (self._c_cell(r) for r in refs)]
+        opname = ops.canon(getattr(st.op, "name", st.op))
+        if opname not in ("add", "maximum", "minimum"):
+            raise NotImplementedError(f"FragmentRowReduce op {st.op!r}")
+        self._warps()
+        res = []
+        for half in (0, 1):
+            v = None
+            for c in cells:
+                for e in (2 * half, 2 * half + 1):
+                    x = Val("f32", c[:, e])
+                    v = x if v is None else coerce(apply_op(opname, [v, x]), "f32")
+            for x in (1, 2):
+                partner = np.arange(self.n) ^ x
+                v = coerce(apply_op(opname, [v, Val("f32", v.a[partner])]), "f32")
+            res.append(v)
+        self.bind(st.top, res[0])
+        self.bind(st.bot, res[1])
+
+    def do_frag_repack(self, st: ir.FragmentRepack) -> None:
+        """An A cell (m16 x k16) from two c cells (m16 x n8, keys 0-7 and
+        8-15), each value rounded to the 16-bit type: in the PTX layouts the
+        c cells' elements are exactly the A cell's, in order."""
+        if st.fragment_layout is not None or st.part is not None:
+            raise NotImplementedError("FragmentRepack layout / part")
+        name, cell = self._frag_ref(st.frag)
+        role, dt = self.frag_role[name]
+        if role != "a" or dtype_info(st.ab_dtype)[0] != dt:
+            raise ValueError("FragmentRepack fills an a fragment of its own type")
+        if len(st.srcs) != 2:
+            raise ValueError("FragmentRepack takes two c cells")
+        vals = np.concatenate([self.frags[n][c] for n, c in (self._c_cell(r) for r in st.srcs)],
+                              axis=1)
+        self.frags[name][cell] = vals.astype(storage_dtype(dt)).astype(np.float32)
 
     # -- warpgroup products (wgmma) ------------------------------------------
     # Starred (``TASK.md:162-172``), no behaviour in the reference; defined

@@ -174,3 +174,45 @@ def test_matmul_wgmma_on_tcgen05(args):
     got = _run(spec, {"x0": a, "x1": bt})["matmul"]
     scale = np.abs(a.astype(np.float64)) @ np.abs(bt.astype(np.float64)).T
     assert np.all(np.abs(got - want) <= 2.0 ** -17 * scale + 1e-30)
+
+
+@pytest.mark.parametrize("args", [(2, 128, 64, "bf16"), (1, 192, 32, "f16"),
+                                  (4, 256, 128, "bf16")])
+def test_attention_in_fragments(args):
+    """Flash attention written with FragmentRowReduce / FragmentApply /
+    FragmentRepack over mma.sync cells: against the oracle within 2e-3 of
+    the output scale (exp and the tensor core's sums round their own way,
+    which can move a P value by one 16-bit step), and against float64."""
+    from oracle.interp import storage_dtype
+    bh, s, d, dt = args
+    spec = load_kernel_data(*irgen.attention_mma(bh, s, d, dt), f"am{bh}{s}{d}{dt}")
+    rng = np.random.default_rng(bh + s + d)
+    x = {n: rng.standard_normal((bh, s, d)).astype(storage_dtype(dt)) for n in "qkv"}
+    want = interpret(spec, {n: a.copy() for n, a in x.items()})["out"]
+    got = _run(spec, x)["out"]
+    scale = np.abs(want).max()
+    assert np.abs(got - want).max() <= 2e-3 * scale
+    q, k, v = (x[n].astype(np.float64) for n in "qkv")
+    sc = q @ k.transpose(0, 2, 1) / np.sqrt(d)
+    p = np.exp(sc - sc.max(-1, keepdims=True))
+    ref = (p / p.sum(-1, keepdims=True)) @ v
+    assert np.abs(got - ref).max() <= 8e-3 * np.abs(ref).max()
+
+
+def test_short_dynamic_smem_is_reported_not_faulted():
+    """The d = 128 fragment attention lays out 49,160 bytes of shared memory
+    (a dynamic pool); meta.json's launch asks for none.  The plan launch
+    requests the whole pool, and a launch with less makes every thread
+    report 0x308 and return before touching shared memory."""
+    from ptxgen.runtime import EmmyError, parse_plan, run_kernel
+    from ptxgen.emit import compile_kernel
+    from oracle.interp import storage_dtype
+    spec = load_kernel_data(*irgen.attention_mma(1, 64, 128, "bf16"), "amsm")
+    assert parse_plan(compile_kernel(spec))["smem"] >= 49160
+    rng = np.random.default_rng(0)
+    x = {n: rng.standard_normal((1, 64, 128)).astype(storage_dtype("bf16")) for n in "qkv"}
+    with pytest.raises(EmmyError, match="0x308"):
+        run_kernel(spec, {n: a.copy() for n, a in x.items()}, geometry="meta")
+    want = interpret(spec, {n: a.copy() for n, a in x.items()})["out"]
+    got = _run(spec, x)["out"]
+    assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()

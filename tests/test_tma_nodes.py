@@ -288,3 +288,63 @@ def test_wgmma_kernels_assemble(tmp_path):
         r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
                            capture_output=True, text=True)
         assert r.returncode == 0, r.stderr[-2000:]
+
+
+# -- fragment arithmetic: apply, row reduce, repack ---------------------------------
+
+def _attn_inputs(bh, s, d, dt, seed=0):
+    from oracle.interp import storage_dtype
+    rng = np.random.default_rng(seed)
+    return {x: rng.standard_normal((bh, s, d)).astype(storage_dtype(dt)) for x in "qkv"}
+
+
+def _attn_f64(x):
+    q, k, v = (x[n].astype(np.float64) for n in "qkv")
+    sc = q @ k.transpose(0, 2, 1) / np.sqrt(q.shape[-1])
+    p = np.exp(sc - sc.max(-1, keepdims=True))
+    return (p / p.sum(-1, keepdims=True)) @ v
+
+
+@pytest.mark.parametrize("args", [(2, 128, 64, "bf16"), (1, 192, 32, "f16"),
+                                  (1, 64, 128, "bf16")])
+def test_oracle_attention_mma(args):
+    """The fragment attention in the oracle against float64 softmax
+    attention: P is rounded to the 16-bit type before P V, so the bound is a
+    few 16-bit ulps of the output scale."""
+    bh, s, d, dt = args
+    spec = load_kernel_data(*irgen.attention_mma(bh, s, d, dt), "am")
+    x = _attn_inputs(bh, s, d, dt)
+    got = interpret(spec, {n: a.copy() for n, a in x.items()})["out"]
+    ref = _attn_f64(x)
+    assert np.abs(got - ref).max() <= 8e-3 * np.abs(ref).max()
+
+
+def test_fragment_arith_round_trip():
+    nodes = [ir.FragmentApply(out="fs[2]", op="subtract", args=(("a", "b"),), kinds=("row",)),
+             ir.FragmentRowReduce(top="t", bot="b", frags=("fs[0]", "fs[1]"), op="maximum"),
+             ir.FragmentRepack(frag="fp[1]", srcs=("fs[2]", "fs[3]"), ab_dtype="bf16")]
+    for n in nodes:
+        assert ir.parse_stmt(repr(n)) == n
+
+
+@pytest.mark.skipif(shutil.which("ptxas") is None, reason="needs ptxas")
+def test_attention_mma_assembles(tmp_path):
+    for i, args in enumerate(((2, 128, 64, "bf16"), (1, 64, 128, "f16"))):
+        ptx = compile_kernel(load_kernel_data(*irgen.attention_mma(*args), f"am{i}"))
+        assert "shfl.sync.bfly.b32" in ptx and "cvt.rn." in ptx
+        f = tmp_path / f"a{i}.ptx"
+        f.write_text(ptx)
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_generic_plan_requests_the_whole_dynamic_pool():
+    """Shared memory above 48 KB goes to a dynamic pool; the plan asks for
+    all of it even when meta.json's smem_bytes is 0, and the kernel checks
+    the size it was given before any shared access."""
+    spec = load_kernel_data(*irgen.attention_mma(1, 64, 128, "bf16"), "amsm")
+    assert spec.smem_bytes == 0
+    ptx = compile_kernel(spec)
+    assert parse_plan(ptx)["smem"] >= 3 * 64 * 128 * 2
+    assert ptx.index("%dynamic_smem_size") < ptx.index("emmy_dyn_smem;")
