@@ -62,7 +62,7 @@ from . import ir, ops
 from .analysis import NoMatch, numel
 from .lower import Lowerer, LowerError, Val, storage_kind, value_kind
 from .model import KernelSpec, dtype_info
-from .ptx import Kernel, Module
+from .ptx import Kernel, Module, f32_hex, f64_hex
 
 _PTX_T = {"f32": "f32", "f64": "f64", "s32": "s32", "s64": "s64", "f16": "b16", "bf16": "b16",
           "pred": "u8"}
@@ -80,6 +80,49 @@ ERR_FRAG = 0x306         # a fragment load or store outside its buffer (skipped)
 ERR_WGMMA = 0x307        # a wgmma operand outside its buffer or misaligned (skipped)
 ERR_SMEM = 0x308         # launched with less dynamic shared memory than the layout needs
 _WG_LAYOUT = {"NONE": 0, "B32": 6, "B64": 4, "B128": 2}   # tcgen05 descriptor bits 61-63
+
+
+def plan_carries(body):
+    """(carrier -> (seed, dtype), id(loop body) -> carriers whose carrying
+    loop it is, id(loop body) -> carriers with a Carry inside it, carriers
+    set outside every loop): a carrier's carrying loop is the innermost loop
+    holding all its Carry statements."""
+    stacks: dict[str, list] = {}
+    info: dict[str, tuple] = {}
+
+    def walk(stmts, stack):
+        for st in stmts:
+            if isinstance(st, ir.Carry):
+                stacks.setdefault(st.name, []).append(stack)
+                seed = st.seed.value if isinstance(st.seed, ir.Literal) else st.seed
+                got = (float(seed), st.dtype if st.dtype is not None else "f32")
+                if info.setdefault(st.name, got) != got:
+                    raise LowerError(f"carrier {st.name!r}: Carry seeds or dtypes differ")
+            if isinstance(st, (ir.Loop, ir.StridedLoop)):
+                walk(st.body, stack + (id(st.body),))
+            else:
+                for child in st.nested():
+                    walk(child, stack)
+
+    walk(body, ())
+    home: dict[int, list] = {}
+    inside: dict[int, set] = {}
+    top = set()
+    for c, sts in stacks.items():
+        common = sts[0]
+        for s_ in sts[1:]:
+            n = 0
+            while n < min(len(common), len(s_)) and common[n] == s_[n]:
+                n += 1
+            common = common[:n]
+        if common:
+            home.setdefault(common[-1], []).append(c)
+        else:
+            top.add(c)
+        for s_ in sts:
+            for b in s_:
+                inside.setdefault(b, set()).add(c)
+    return info, home, inside, top
 
 
 def wgmma_n(shape) -> int:
@@ -155,8 +198,11 @@ class Generic:
             ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: lambda st: None,
             ir.WgmmaCommit: self.do_wgmma_commit, ir.WgmmaWait: self.do_wgmma_wait,
             ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
-            ir.FragmentRepack: self.do_frag_repack,
+            ir.FragmentRepack: self.do_frag_repack, ir.Pre: self.do_pre, ir.Carry: self.do_carry,
         }
+        (self.carriers, self.carry_home, self.carry_inside,
+         self.carry_top) = plan_carries(spec.op.body)
+        self.carry_regs: dict[tuple, tuple] = {}     # (carrier, cell) -> (cur, nxt)
         self.frags: dict[str, tuple] = {}    # name -> (role, dtype, [[regs] per cell])
         self.wg = None                       # warpgroup tensor-core state (setup_wgmma)
         self.wgdesc: dict[str, tuple] = {}
@@ -237,6 +283,9 @@ class Generic:
         lo.bind("lane", Val(lane, "s32"))
         lo.bind("warp", Val(warp, "s32"))
         self.tid = tid
+        # carried-state registers are seeded here (lines inserted at this
+        # point as cells are first met)
+        self.carry_at = len(k.lines)
         self.setup_wgmma()
         lo.run(spec.op.body)
         self.finish_wgmma()
@@ -505,6 +554,9 @@ class Generic:
         k(f"mov.b32 {var}, {start.reg}")
         saved_env = lo.env.get(axis)
         head, done = k.label("lp"), k.label("lpend")
+        # carried cells are seeded once as their carrying loop starts
+        for c in self.carry_home.get(id(body), ()):
+            self.carry_reset(c, body)
         k.place(head)
         p = k.reg("pred")
         k(f"setp.ge.s32 {p}, {var}, {bound.reg}")
@@ -520,6 +572,8 @@ class Generic:
         if self.wg_state() != before:
             raise LowerError("wgmma products must be committed and waited for inside each "
                              "loop iteration")
+        for c in sorted(self.carry_inside.get(id(body), ())):
+            self.carry_commit(c)
         k(f"add.s32 {var}, {var}, {step.reg}")
         k(f"bra {head}")
         k.place(done)
@@ -1181,6 +1235,79 @@ class Generic:
         for j in range(4):
             # element 2j in the low half, 2j + 1 in the high half
             k(f"cvt.rn.{dt}x2.f32 {regs[j]}, {src[2 * j + 1]}, {src[2 * j]}")
+
+    # -- carried state (Pre / Carry) ----------------------------------------
+
+    def carry_cell(self, index) -> tuple:
+        idx = index if isinstance(index, tuple) else (() if index is None else (index,))
+        out = []
+        for e in idx:
+            v = e.value if isinstance(e, ir.Literal) else e
+            if not isinstance(v, int) or isinstance(v, bool):
+                raise LowerError("carried-state cells take literal indices")
+            out.append(int(v))
+        return tuple(out)
+
+    def carry_pair(self, c: str, cell: tuple) -> tuple:
+        """(state, next state) registers of one cell, seeded where first used
+        (the prologue runs before any loop, so a cell read before its
+        carrying loop holds the seed)."""
+        if (c, cell) not in self.carry_regs:
+            seed, dt = self.carriers[c]
+            kind = value_kind(dt)
+            if kind == "f32":
+                imm = f32_hex(float(seed))
+            elif kind == "f64":
+                imm = f64_hex(float(seed))
+            elif kind in ("s32", "s64"):
+                imm = str(int(seed))
+            else:
+                raise LowerError(f"carrier {c!r} of dtype {dt!r}")
+            cur, nxt = self.k.reg(kind), self.k.reg(kind)
+            # registers set in the kernel's first lines, ahead of every loop
+            t = {"f32": "f32", "f64": "f64", "s32": "b32", "s64": "b64"}[kind]
+            self.k.lines.insert(self.carry_at, f"\tmov.{t} {cur}, {imm};")
+            self.k.lines.insert(self.carry_at, f"\tmov.{t} {nxt}, {imm};")
+            self.carry_regs[(c, cell)] = (cur, nxt, kind, imm)
+        return self.carry_regs[(c, cell)]
+
+    def carry_reset(self, c: str, body) -> None:
+        """Seed every cell of ``c`` as its carrying loop starts (cells first
+        met inside the loop included)."""
+        for st in ir.walk(body):
+            if isinstance(st, ir.Carry) and st.name == c:
+                self.carry_pair(c, self.carry_cell(st.index))
+            elif isinstance(st, ir.Pre) and st.carrier == c:
+                self.carry_pair(c, self.carry_cell(st.index))
+        g = self.guard()
+        for (cc, cell), (cur, nxt, kind, imm) in list(self.carry_regs.items()):
+            if cc == c:
+                t = {"f32": "f32", "f64": "f64", "s32": "b32", "s64": "b64"}[kind]
+                self.k(f"{g}mov.{t} {cur}, {imm}")
+                self.k(f"{g}mov.{t} {nxt}, {imm}")
+
+    def carry_commit(self, c: str) -> None:
+        for (cc, cell), (cur, nxt, kind, _) in list(self.carry_regs.items()):
+            if cc == c:
+                t = {"f32": "f32", "f64": "f64", "s32": "b32", "s64": "b64"}[kind]
+                self.k(f"mov.{t} {cur}, {nxt}")
+
+    def do_pre(self, st: ir.Pre) -> None:
+        if st.carrier not in self.carriers:
+            raise LowerError(f"carrier {st.carrier!r} has no Carry")
+        cur, _, kind, _ = self.carry_pair(st.carrier, self.carry_cell(st.index))
+        self.lo.bind(st.name, Val(cur, kind))
+
+    def do_carry(self, st: ir.Carry) -> None:
+        cur, nxt, kind, _ = self.carry_pair(st.name, self.carry_cell(st.index))
+        if st.value not in self.lo.env:
+            raise LowerError(f"undefined name {st.value!r}")
+        v = self.lo.coerce(self.lo.env[st.value], kind)
+        t = {"f32": "f32", "f64": "f64", "s32": "b32", "s64": "b64"}[kind]
+        g = self.guard()
+        self.k(f"{g}mov.{t} {nxt}, {v.reg}")
+        if st.name in self.carry_top:
+            self.k(f"{g}mov.{t} {cur}, {v.reg}")
 
     # -- warpgroup products on tcgen05 ----------------------------------------
 

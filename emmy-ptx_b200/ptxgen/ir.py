@@ -318,6 +318,22 @@ class Let(Node):
 
 
 @dataclass(repr=False, eq=True)
+class Pre(Node):
+    name: str
+    carrier: str
+    index: Any = ()
+
+
+@dataclass(repr=False, eq=True)
+class Carry(Node):
+    name: str
+    value: str
+    index: Any = ()
+    seed: Any = 0.0
+    dtype: Any = None
+
+
+@dataclass(repr=False, eq=True)
 class Init(Node):
     name: str
     identity: Any
@@ -743,7 +759,7 @@ _CTORS: dict[str, Any] = {
         CpAsyncCommit, CpAsyncWait, Select, SelectBranch, ZeroPrologue, TmaDescriptor,
         TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
         RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore, WgmmaDescriptor, WgmmaMma, WgmmaFence,
-        WgmmaCommit, WgmmaWait, FragmentApply, FragmentRowReduce, FragmentRepack,
+        WgmmaCommit, WgmmaWait, FragmentApply, FragmentRowReduce, FragmentRepack, Pre, Carry,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

@@ -34,6 +34,10 @@ re-derives the shape-dependent literals:
                      ``FragmentRowReduce``, scaling and exp by
                      ``FragmentApply``, P turned into A cells by
                      ``FragmentRepack`` for the P V products;
+* ``carry_scan``  -- a per-row recurrence on carried state (``Pre`` /
+                     ``Carry``): two cells updated from each other's previous
+                     values, a counter set only under a condition, the
+                     carrying loop run twice inside an outer loop;
 * ``matmul_wgmma`` -- C = A.B^T (B given K-major, [N][K]) on warpgroup
                      products (``WgmmaDescriptor``, ``WgmmaMma``,
                      ``WgmmaFence/Commit/Wait``) over 128-byte-swizzled box
@@ -55,7 +59,7 @@ from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCo
                  RegFragment, RegStore, SetMaxNReg, Smem, StridedLoop, Sync, TernaryExpr, Tile,
                  TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, WgmmaCommit,
                  WgmmaDescriptor, WgmmaFence, WgmmaMma, WgmmaWait, Window, Write, datatype,
-                 FragmentApply, FragmentRepack, FragmentRowReduce)
+                 FragmentApply, FragmentRepack, FragmentRowReduce, Pre, Carry)
 
 F32 = datatype("f32")
 
@@ -1141,6 +1145,48 @@ def attention_mma(bh: int, s: int, d: int, dtype="bf16", entry="k_attention_mma"
                     ("v", (bh, s, d), dtype, 2)], [], ("out", (bh, s, d), "f32"),
                    ["q", "k", "v", "out"], (bh * (s // BQ), 1, 1), (TH, 1, 1),
                    rtol=1e-2, atol=1e-3, pid=pid)
+
+
+def carry_scan(rows: int, cols: int, threads: int = 128, entry="k_carry_scan",
+               pid="carry_scan"):
+    """One thread per row of x [rows, cols], carried cells st[0], st[1]
+    (seed 1) and cnt (seed 0).  Per column: y[r, c] = st[1] as the previous
+    step left it; st[0] <- st[1], st[1] <- st[0] * 0.5 + st[1] * x[r, c]
+    (both from the previous state); cnt <- cnt + 1 where x[r, c] > 0.  The
+    column loop runs twice inside an outer loop (the cells are seeded again
+    each time); y[r, cols + 3 + rep] = st[1] after run rep, and after both
+    y[r, cols .. cols + 2] = st[0], st[1], cnt."""
+    r = V("r")
+    zero = L(0)
+    inner = [load("xv", "x", (r, V("c"))),
+             Pre(name="p0", carrier="st", index=(zero,)),
+             Pre(name="p1", carrier="st", index=(L(1),)),
+             Pre(name="q", carrier="cnt", index=()),
+             assign("a", "multiply", "p0", "half"),
+             assign("b", "multiply", "p1", "xv"),
+             assign("n1", "add", "a", "b"),
+             assign("q1", "add", "q", "one"),
+             write("y", (r, V("c")), "p1"),
+             Carry(name="st", value="p1", index=(zero,), seed=1.0, dtype=F32),
+             Carry(name="st", value="n1", index=(L(1),), seed=1.0, dtype=F32),
+             Cond(cond=BinaryExpr(op=">", left=V("xv"), right=Lf(0.0)),
+                  body=(Carry(name="cnt", value="q1", index=(), seed=0.0, dtype=F32),),
+                  else_body=())]
+    outer = [loop("c", cols, inner, seed=False),
+             Pre(name="g1", carrier="st", index=(L(1),)),
+             write("y", (r, ADD(L(cols + 3), V("rep"))), "g1")]
+    body = [Let(name="half", value=Lf(0.5), dtype=F32), Let(name="one", value=Lf(1.0), dtype=F32),
+            loop("rep", 2, outer, seed=False),
+            Pre(name="f0", carrier="st", index=(zero,)),
+            Pre(name="f1", carrier="st", index=(L(1),)),
+            Pre(name="fc", carrier="cnt", index=()),
+            write("y", (r, L(cols)), "f0"), write("y", (r, L(cols + 1)), "f1"),
+            write("y", (r, L(cols + 2)), "fc")]
+    tl = tile([ax("r", rows)], body, block_threads=threads)
+    return package(entry, "scan", [tl], [("x", (rows, cols), "f32", 0)], [],
+                   ("y", (rows, cols + 5), "f32"), ["x", "y"],
+                   ((rows + threads - 1) // threads, 1, 1), (threads, 1, 1), rtol=0.0, atol=0.0,
+                   pid=pid)
 
 
 def bench_kernels():

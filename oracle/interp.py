@@ -307,6 +307,49 @@ def swizzle_index(flat: np.ndarray, mode) -> np.ndarray:
     return flat ^ (((flat >> shift) & mask) << 3)
 
 
+def plan_carries(body):
+    """(carrier -> (seed, dtype), id(loop body) -> carriers it carries,
+    id(loop body) -> carriers with a Carry inside it, carriers set outside
+    every loop).  A carrier's carrying loop is the innermost loop that holds
+    all its Carry statements."""
+    stacks: dict[str, list] = {}
+    info: dict[str, tuple] = {}
+
+    def walk(stmts, stack):
+        for st in stmts:
+            if isinstance(st, ir.Carry):
+                stacks.setdefault(st.name, []).append(stack)
+                got = (float(st.seed) if not isinstance(st.seed, ir.Literal) else
+                       float(st.seed.value), st.dtype if st.dtype is not None else "f32")
+                if info.setdefault(st.name, got) != got:
+                    raise ValueError(f"carrier {st.name!r}: Carry seeds or dtypes differ")
+            if isinstance(st, (ir.Loop, ir.StridedLoop)):
+                walk(st.body, stack + (id(st.body),))
+            else:
+                for child in st.nested():
+                    walk(child, stack)
+
+    walk(body, ())
+    home: dict[int, list] = {}
+    inside: dict[int, set] = {}
+    top = set()
+    for c, sts in stacks.items():
+        common = sts[0]
+        for s_ in sts[1:]:
+            n = 0
+            while n < min(len(common), len(s_)) and common[n] == s_[n]:
+                n += 1
+            common = common[:n]
+        if common:
+            home.setdefault(common[-1], []).append(c)
+        else:
+            top.add(c)
+        for s_ in sts:
+            for b in s_:
+                inside.setdefault(b, set()).add(c)
+    return info, home, inside, top
+
+
 _TMA_SWIZZLE = {"NONE": 0, "B32": 32, "B64": 64, "B128": 128}
 
 
@@ -434,8 +477,10 @@ class Machine:
             ir.WgmmaMma: self.do_wgmma, ir.WgmmaFence: self.do_nothing,
             ir.WgmmaCommit: self.do_nothing, ir.WgmmaWait: self.do_wgmma_wait,
             ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
-            ir.FragmentRepack: self.do_frag_repack,
+            ir.FragmentRepack: self.do_frag_repack, ir.Pre: self.do_pre, ir.Carry: self.do_carry,
         }
+        (self.carriers, self.carry_home, self.carry_inside,
+         self.carry_top) = plan_carries(spec.op.body)
         self.wg_desc: dict[str, tuple] = {}
         self.frags: dict[str, np.ndarray] = {}
         self.frag_role: dict[str, tuple[str, str]] = {}
@@ -444,6 +489,62 @@ class Machine:
                           if isinstance(st, ir.TmaDescriptor)}
 
     # -- lane state -------------------------------------------------------
+
+    # -- carried state (Pre / Carry) ---------------------------------------
+    # Starred in the reference's table (``TASK.md:105-106``), absent from its
+    # interpreter.  A carrier is a set of cells (literal indices) of one
+    # dtype, seeded with one literal.  Its carrying loop is the innermost
+    # loop that holds all its Carry statements: the cells are seeded when
+    # that loop starts, a step's Pre reads see the state the previous step
+    # left (the seed on the first step), a Carry sets a cell's next value
+    # (active lanes only; cells not set keep theirs), and the next state
+    # becomes the state at the end of each step.  Pre after the loop reads
+    # the final state.  A carrier set outside every loop is updated at once.
+
+    def _cell(self, index) -> tuple:
+        idx = index if isinstance(index, tuple) else (() if index is None else (index,))
+        out = []
+        for e in idx:
+            v = e.value if isinstance(e, ir.Literal) else e
+            if not isinstance(v, int) or isinstance(v, bool):
+                raise NotImplementedError("carried-state cells take literal indices")
+            out.append(int(v))
+        return tuple(out)
+
+    def _carry_seed(self, c: str) -> Val:
+        seed, dt = self.carriers[c]
+        return coerce(Val("f32", np.float32(seed)) if _kind(dt) in ("f32", "f64", "f16") else
+                      Val("s32", int(seed)), _kind(dt))
+
+    def _carry_reset(self, c: str) -> None:
+        seed = self._carry_seed(c)
+        for state in (self.carry_cur, self.carry_nxt):
+            cells = state.setdefault(c, {})
+            for key in list(cells):
+                cells[key] = Val(seed.kind, np.where(self.live(), seed.a, cells[key].a))
+
+    def _carry_get(self, state, c: str, key: tuple) -> Val:
+        cells = state.setdefault(c, {})
+        if key not in cells:
+            seed = self._carry_seed(c)
+            cells[key] = Val(seed.kind, np.broadcast_to(seed.a, (self.n,)).copy())
+        return cells[key]
+
+    def do_pre(self, st: ir.Pre) -> None:
+        if st.carrier not in self.carriers:
+            raise KeyError(f"carrier {st.carrier!r} has no Carry")
+        self.bind(st.name, self._carry_get(self.carry_cur, st.carrier, self._cell(st.index)))
+
+    def do_carry(self, st: ir.Carry) -> None:
+        key = self._cell(st.index)
+        kind = _kind(self.carriers[st.name][1])
+        v = coerce(self.env[st.value], kind)
+        old = self._carry_get(self.carry_nxt, st.name, key)
+        new = Val(kind, np.where(self.live(), np.broadcast_to(v.a, (self.n,)), old.a))
+        self.carry_nxt[st.name][key] = new
+        if st.name in self.carry_top:
+            self._carry_get(self.carry_cur, st.name, key)
+            self.carry_cur[st.name][key] = new
 
     def _start_chunk(self, first: int, count: int) -> None:
         self.first = first
@@ -458,6 +559,8 @@ class Machine:
                                     "warp": Val("s32", self.tid >> 5)}
         self.smem = {nm: np.zeros((count,) + shp, dtype=dt)
                      for nm, (shp, dt) in self.smem_decl.items()}
+        self.carry_cur: dict[str, dict] = {}
+        self.carry_nxt: dict[str, dict] = {}
         for name in self.spec.arg_order:
             arg = self.spec.args[name]
             if arg.scalar:
@@ -766,6 +869,8 @@ class Machine:
             self.env[axis] = Val("s32", var)
             with self.under(alive):
                 self.run_body(body)
+            for c in self.carry_inside.get(id(body), ()):
+                self.carry_cur[c] = {key: v for key, v in self.carry_nxt.get(c, {}).items()}
             var = var + step
             steps += 1
             if steps > _STEP_LIMIT:
@@ -778,12 +883,16 @@ class Machine:
     def do_loop(self, st: ir.Loop) -> None:
         """``interp.py:803-826``: 0 .. extent-1."""
         self.seed_accums(st.body, bool(st.seed))
+        for c in self.carry_home.get(id(st.body), ()):
+            self._carry_reset(c)
         ext = int(st.axis.extent.as_static())
         self._counted(st.axis.name, np.zeros((), dtype=np.int64), np.int64(ext), 1, st.body)
 
     def do_strided(self, st: ir.StridedLoop) -> None:
         """``interp.py:828-856``: start, start+step, ... while < end (or extent)."""
         self.seed_accums(st.body, bool(st.seed))
+        for c in self.carry_home.get(id(st.body), ()):
+            self._carry_reset(c)
         ext = int(st.axis.extent.as_static())
         start = as_int64(self.ev(st.start))
         step = as_int64(self.ev(st.step)) if hasattr(st.step, "free_vars") else np.int64(int(st.step))

@@ -216,3 +216,15 @@ def test_short_dynamic_smem_is_reported_not_faulted():
     want = interpret(spec, {n: a.copy() for n, a in x.items()})["out"]
     got = _run(spec, x)["out"]
     assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("shape", [(200, 37), (1000, 130)])
+def test_carry_scan_bitexact(shape):
+    """Carried state (Pre / Carry) in registers: a two-cell recurrence, a
+    conditional counter and a carrying loop run twice, bit for bit against
+    the oracle."""
+    rows, cols = shape
+    spec = load_kernel_data(*irgen.carry_scan(rows, cols), f"cs{rows}")
+    x = np.random.default_rng(rows).standard_normal((rows, cols)).astype(np.float32)
+    want = interpret(spec, {"x": x.copy()})["y"]
+    assert np.array_equal(_run(spec, {"x": x})["y"], want)

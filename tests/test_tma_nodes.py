@@ -348,3 +348,58 @@ def test_generic_plan_requests_the_whole_dynamic_pool():
     ptx = compile_kernel(spec)
     assert parse_plan(ptx)["smem"] >= 3 * 64 * 128 * 2
     assert ptx.index("%dynamic_smem_size") < ptx.index("emmy_dyn_smem;")
+
+
+# -- carried state ------------------------------------------------------------------
+
+def carry_scan_reference(x):
+    rows, cols = x.shape
+    ref = np.zeros((rows, cols + 5), np.float32)
+    half = np.float32(0.5)
+    for r in range(rows):
+        for rep in range(2):
+            st0, st1, cnt = np.float32(1), np.float32(1), np.float32(0)
+            for c in range(cols):
+                ref[r, c] = st1
+                n1 = np.float32(np.float32(st0 * half) + np.float32(st1 * x[r, c]))
+                st0, st1 = st1, n1
+                if x[r, c] > 0:
+                    cnt = np.float32(cnt + 1)
+            ref[r, cols + 3 + rep] = st1
+        ref[r, cols:cols + 3] = [st0, st1, cnt]
+    return ref
+
+
+def test_oracle_carry_scan():
+    """Reads within a step see the previous state (st[0] <- st[1] and st[1]
+    <- f(st[0], st[1]) use the old values), a cell set under a condition
+    keeps its value elsewhere, the carrying loop seeds its cells each time
+    it starts, and Pre after the loop reads the final state; the block's
+    tail lanes (200 rows, 128 threads) change nothing."""
+    spec = load_kernel_data(*irgen.carry_scan(200, 37), "cs")
+    x = np.random.default_rng(0).standard_normal((200, 37)).astype(np.float32)
+    assert np.array_equal(interpret(spec, {"x": x})["y"], carry_scan_reference(x))
+
+
+def test_carry_nodes_round_trip_and_assemble(tmp_path):
+    for n in (ir.Pre(name="p", carrier="st", index=(irgen.L(1),)),
+              ir.Carry(name="st", value="v", index=(irgen.L(1),), seed=1.0, dtype="f32")):
+        assert ir.parse_stmt(repr(n)) == n
+    if shutil.which("ptxas") is None:
+        return
+    f = tmp_path / "cs.ptx"
+    f.write_text(compile_kernel(load_kernel_data(*irgen.carry_scan(200, 37), "cs")))
+    r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", str(f)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_carry_seeding_is_outside_the_step():
+    """The carrying loop's seeding comes before its head label, not inside
+    every step."""
+    ptx = compile_kernel(load_kernel_data(*irgen.carry_scan(64, 5), "cs"))
+    lines = [ln.strip() for ln in ptx.splitlines()]
+    heads = [i for i, ln in enumerate(lines) if ln.startswith("$L_lp_")]
+    inner = heads[1]
+    seeds = [i for i, ln in enumerate(lines) if ln.startswith("@") and "0f3F800000" in ln]
+    assert seeds and all(i < inner for i in seeds)
