@@ -199,6 +199,7 @@ class Generic:
             ir.WgmmaCommit: self.do_wgmma_commit, ir.WgmmaWait: self.do_wgmma_wait,
             ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
             ir.FragmentRepack: self.do_frag_repack, ir.Pre: self.do_pre, ir.Carry: self.do_carry,
+            ir.FragmentPromote: self.do_frag_promote,
         }
         (self.carriers, self.carry_home, self.carry_inside,
          self.carry_top) = plan_carries(spec.op.body)
@@ -1019,11 +1020,13 @@ class Generic:
         if str(st.shape) != "m16n8k16" and not (role == "c" and wg_n):
             raise LowerError(f"{role} fragment shape {st.shape!r}")
         dt = dtype_info(st.dtype)[0]
-        if (role in ("a", "b") and dt not in ("bf16", "f16")) or (role == "c" and dt != "f32"):
+        if (role in ("a", "b") and dt not in ("bf16", "f16")) or (
+                role == "c" and dt != "f32" and not (dt == "f16" and not wg_n)):
             raise LowerError(f"{role} fragment of {st.dtype!r}")
-        nregs = {"a": 4, "b": 2, "c": wg_n // 2 if wg_n else 4}[role]
+        # an f16 c cell is two packed f16 pairs
+        nregs = {"a": 4, "b": 2, "c": wg_n // 2 if wg_n else (2 if dt == "f16" else 4)}[role]
         if st.name not in self.frags:
-            cells = [k.regs("f32" if role == "c" else "b32", nregs)
+            cells = [k.regs("f32" if role == "c" and dt == "f32" else "b32", nregs)
                      for _ in range(int(st.count or 1))]
             self.frags[st.name] = (role, dt, cells)
             self.frag_shape[st.name] = str(st.shape)
@@ -1097,6 +1100,13 @@ class Generic:
         ab = self.frags[an][1]
         if self.frags[bn][1] != ab:
             raise LowerError("MmaSyncPtx: A and B of different types")
+        if self.frags[cn][1] == "f16":
+            if ab != "f16":
+                raise LowerError("an f16 accumulator takes f16 A and B")
+            self.k(f"mma.sync.aligned.m16n8k16.row.col.f16.f16.f16.f16 "
+                   f"{{{', '.join(c)}}}, {{{', '.join(a)}}}, {{{', '.join(b)}}}, "
+                   f"{{{', '.join(c)}}}")
+            return
         self.k(f"mma.sync.aligned.m16n8k16.row.col.f32.{ab}.{ab}.f32 "
                f"{{{', '.join(c)}}}, {{{', '.join(a)}}}, {{{', '.join(b)}}}, "
                f"{{{', '.join(c)}}}")
@@ -1112,6 +1122,8 @@ class Generic:
         name, regs = self.frag_cell(st.frag, st.fragment_index)
         if self.frags[name][0] != "c":
             raise LowerError("RegStore stores a c fragment")
+        if self.frags[name][1] == "f16":
+            regs = self.unpack_f16(regs)
         if st.dst_buffer not in self.base:
             raise LowerError(f"RegStore into {st.dst_buffer!r}")
         shape = self.spec.args[st.dst_buffer].shape
@@ -1166,11 +1178,37 @@ class Generic:
             lo.mask = saved
 
 
-    def c_cell(self, ref) -> list:
+    def c_cell(self, ref, dtype="f32") -> list:
         name, regs = self.frag_cell(ref)
-        if self.frags[name][0] != "c" or self.frag_shape[name] != "m16n8k16":
-            raise LowerError(f"{ref!r} is not an m16n8 c fragment")
+        if (self.frags[name][0], self.frags[name][1]) != ("c", dtype) or \
+                self.frag_shape[name] != "m16n8k16":
+            raise LowerError(f"{ref!r} is not an m16n8 {dtype} c fragment")
         return regs
+
+    def unpack_f16(self, regs) -> list:
+        """Four f32 values of a packed f16 c cell (element 2j in the low half)."""
+        k, out = self.k, []
+        for r in regs:
+            lo16, hi16 = k.reg("b16"), k.reg("b16")
+            k(f"mov.b32 {{{lo16}, {hi16}}}, {r}")
+            for h in (lo16, hi16):
+                f = k.reg("f32")
+                k(f"cvt.f32.f16 {f}, {h}")
+                out.append(f)
+        return out
+
+    def do_frag_promote(self, st: ir.FragmentPromote) -> None:
+        k = self.k
+        dst = self.c_cell(st.dst)
+        src = self.c_cell(st.src, "f16")
+        vals = self.unpack_f16(src)
+        g = self.guard()
+        for d, v in zip(dst, vals):
+            t = k.reg("f32")
+            k(f"add.rn.f32 {t}, {d}, {v}")
+            k(f"{g}mov.f32 {d}, {t}")
+        for r in src:
+            k(f"{g}mov.b32 {r}, 0")
 
     def do_frag_apply(self, st: ir.FragmentApply) -> None:
         """op per element of an m16n8 c cell with the IR's op lowering;

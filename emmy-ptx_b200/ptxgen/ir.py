@@ -590,6 +590,12 @@ class RegStore(Node):
 
 
 @dataclass(repr=False, eq=True)
+class FragmentPromote(Node):
+    dst: str
+    src: str
+
+
+@dataclass(repr=False, eq=True)
 class FragmentApply(Node):
     out: str
     op: Any
@@ -760,6 +766,7 @@ _CTORS: dict[str, Any] = {
         TmaLoad, MbarrierInit, MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg,
         RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore, WgmmaDescriptor, WgmmaMma, WgmmaFence,
         WgmmaCommit, WgmmaWait, FragmentApply, FragmentRowReduce, FragmentRepack, Pre, Carry,
+        FragmentPromote,
     )
 }
 _CTORS["dtype"] = _np_dtype_ctor

@@ -59,7 +59,7 @@ from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCo
                  RegFragment, RegStore, SetMaxNReg, Smem, StridedLoop, Sync, TernaryExpr, Tile,
                  TmaDescriptor, TmaLoad, TreeHalve, Var, WarpShuffle, WgmmaCommit,
                  WgmmaDescriptor, WgmmaFence, WgmmaMma, WgmmaWait, Window, Write, datatype,
-                 FragmentApply, FragmentRepack, FragmentRowReduce, Pre, Carry)
+                 FragmentApply, FragmentPromote, FragmentRepack, FragmentRowReduce, Pre, Carry)
 
 F32 = datatype("f32")
 
@@ -948,14 +948,19 @@ def matmul_tma(m: int, n: int, k: int, entry="k_matmul_tma", pid="matmul_tma"):
 
 
 def matmul_mma(m: int, n: int, k: int, dtype="bf16", m_valid=None, n_valid=None,
-               entry="k_matmul_mma", pid="matmul_mma"):
+               promote_every=0, entry="k_matmul_mma", pid="matmul_mma"):
     """C = A.B (A [m, k], B [k, n] in bf16 or f16, C in f32) on m16n8k16
     fragments: a 64 x 32 C tile per CTA of four warps, warp w owning rows
     16w..16w+15 as four 16 x 8 cells; per K step of 16 thread 0 brings the
     A (64 x 16) and B (16 x 32) boxes with two box copies on one mbarrier,
     each warp loads its A cell and the four B cells (``ldmatrix``, B [K][N]
     transposed) and accumulates four products.  ``m_valid`` / ``n_valid``:
-    rows and columns of C stored (the guards of ``RegStore``)."""
+    rows and columns of C stored (the guards of ``RegStore``).
+    ``promote_every`` (f16 only): the products accumulate in f16 cells that
+    ``FragmentPromote`` adds into the f32 cells every that many K steps and
+    once after the loop."""
+    if promote_every and dtype != "f16":
+        raise ValueError("f16 accumulators take f16 operands")
     BM, BN, BK, TH = 64, 32, 16, 128
     if m % BM or n % BN or k % BK:
         raise ValueError("matmul_mma shape must tile by 64x32 with K a multiple of 16")
@@ -974,6 +979,11 @@ def matmul_mma(m: int, n: int, k: int, dtype="bf16", m_valid=None, n_valid=None,
             Cond(cond=EQ(t, L(0)), body=(MbarrierInit(mbar="bar", count=L(1), slot=L(0)),),
                  else_body=()),
             Sync(barrier_id=0, count=None, warp=False)]
+    acc = "fc"
+    if promote_every:
+        body.insert(-2, RegFragment(name="fh", role="c", shape="m16n8k16", dtype="f16", count=4,
+                                    nregs=2))
+        acc = "fh"
     copies = [TmaLoad(smem="_a_smem", smem_index=L(0), desc="dA",
                       coords=(MUL(V("bm"), L(BM)), V("_ks")), mbar="bar", mbar_slot=L(0)),
               TmaLoad(smem="_b_smem", smem_index=L(0), desc="dB",
@@ -985,10 +995,18 @@ def matmul_mma(m: int, n: int, k: int, dtype="bf16", m_valid=None, n_valid=None,
     for j in range(BN // 8):
         ks += [LdmatrixLoad(frag="fb", src_buffer="_b_smem", src_index=(L(0), L(8 * j)),
                             role="b", b_trans=True, fragment_index=L(j)),
-               MmaSyncPtx(c_frag=f"fc[{j}]", a_frag="fa", b_frag=f"fb[{j}]", shape="m16n8k16",
-                          ab_dtype=dtype, c_dtype="f32")]
+               MmaSyncPtx(c_frag=f"{acc}[{j}]", a_frag="fa", b_frag=f"fb[{j}]",
+                          shape="m16n8k16", ab_dtype=dtype,
+                          c_dtype="f16" if promote_every else "f32")]
+    promote = [FragmentPromote(dst=f"fc[{j}]", src=f"fh[{j}]") for j in range(BN // 8)]
+    if promote_every:
+        step = DIV(V("_ks"), L(BK))
+        ks.append(Cond(cond=EQ(MOD(step, L(promote_every)), L(promote_every - 1)),
+                       body=tuple(promote), else_body=()))
     ks.append(Sync(barrier_id=0, count=None, warp=False))
     body.append(strided("_ks", k, L(0), L(BK), ks))
+    if promote_every:
+        body += promote
     for j in range(BN // 8):
         body.append(RegStore(dst_buffer="matmul",
                              dst_index=(ADD(MUL(V("bm"), L(BM)), MUL(V("warp"), L(16))),

@@ -478,6 +478,7 @@ class Machine:
             ir.WgmmaCommit: self.do_nothing, ir.WgmmaWait: self.do_wgmma_wait,
             ir.FragmentApply: self.do_frag_apply, ir.FragmentRowReduce: self.do_frag_rowreduce,
             ir.FragmentRepack: self.do_frag_repack, ir.Pre: self.do_pre, ir.Carry: self.do_carry,
+            ir.FragmentPromote: self.do_frag_promote,
         }
         (self.carriers, self.carry_home, self.carry_inside,
          self.carry_top) = plan_carries(spec.op.body)
@@ -1115,7 +1116,7 @@ class Machine:
         dt = dtype_info(st.dtype)[0]
         if role in ("a", "b") and dt not in ("bf16", "f16"):
             raise NotImplementedError(f"{role} fragment of {st.dtype!r}")
-        if role == "c" and dt != "f32":
+        if role == "c" and dt != "f32" and not (dt == "f16" and not wg_n):
             raise NotImplementedError(f"c fragment of {st.dtype!r}")
         elems = {"a": 8, "b": 4, "c": wg_n // 2 if wg_n else 4}[role]
         self.frags[st.name] = np.zeros((int(st.count or 1), self.n, elems), np.float32)
@@ -1186,13 +1187,29 @@ class Machine:
         B[:, br_, bcl] = bf
         Cm[:, cr, ccl] = cf
         D = (np.einsum("wmk,wkn->wmn", A, B) + Cm).astype(np.float32)
+        if self.frag_role[cn][1] == "f16":
+            # an f16 accumulator: A and B are f16 and each product's sum is
+            # rounded once to f16
+            if self.frag_role[an][1] != "f16" or self.frag_role[bn][1] != "f16":
+                raise ValueError("an f16 accumulator takes f16 A and B")
+            D = (np.einsum("wmk,wkn->wmn", A, B) + Cm).astype(np.float16).astype(np.float32)
         self.frags[cn][cc] = D[:, cr, ccl].reshape(self.n, -1)
 
-    def _c_cell(self, ref):
+    def _c_cell(self, ref, dtype="f32"):
         name, cell = self._frag_ref(ref)
-        if self.frag_role[name][0] != "c" or self.frag_shape[name] != "m16n8k16":
-            raise ValueError(f"{ref!r} is not an m16n8 c fragment")
+        if (self.frag_role[name] != ("c", dtype) or self.frag_shape[name] != "m16n8k16"):
+            raise ValueError(f"{ref!r} is not an m16n8 {dtype} c fragment")
         return name, cell
+
+    def do_frag_promote(self, st: ir.FragmentPromote) -> None:
+        """dst (f32) += src (f16), element by element with one f32 rounding,
+        then src = 0; lanes outside the mask keep both."""
+        dn, dc = self._c_cell(st.dst)
+        sn, sc = self._c_cell(st.src, "f16")
+        m = self.live()[:, None]
+        d, s_ = self.frags[dn][dc], self.frags[sn][sc]
+        self.frags[dn][dc] = np.where(m, (d + s_).astype(np.float32), d)
+        self.frags[sn][sc] = np.where(m, np.float32(0), s_)
 
     def do_frag_apply(self, st: ir.FragmentApply) -> None:
         """out = op(out, *args) (``in_place``) or op(*args), element by

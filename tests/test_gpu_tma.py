@@ -228,3 +228,21 @@ def test_carry_scan_bitexact(shape):
     x = np.random.default_rng(rows).standard_normal((rows, cols)).astype(np.float32)
     want = interpret(spec, {"x": x.copy()})["y"]
     assert np.array_equal(_run(spec, {"x": x})["y"], want)
+
+
+@pytest.mark.parametrize("every", [1, 3])
+def test_matmul_mma_f16_accumulators(every):
+    """mma.sync with f16 accumulators, promoted into f32 cells every
+    ``every`` K steps (FragmentPromote): against the oracle within 2^-9 of
+    sum |a||b| per element (the tensor core rounds its f16 sums its own
+    way; a layout slip would be off by whole products)."""
+    m, n, k = 128, 64, 160
+    spec = load_kernel_data(*irgen.matmul_mma(m, n, k, "f16", promote_every=every),
+                            f"mp{every}")
+    rng = np.random.default_rng(every)
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    b = rng.standard_normal((k, n)).astype(np.float16)
+    want = interpret(spec, {"x0": a.copy(), "x1": b.copy()})["matmul"]
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    assert np.all(np.abs(got - want) <= 2.0 ** -9 * scale)

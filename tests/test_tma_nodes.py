@@ -403,3 +403,21 @@ def test_carry_seeding_is_outside_the_step():
     inner = heads[1]
     seeds = [i for i, ln in enumerate(lines) if ln.startswith("@") and "0f3F800000" in ln]
     assert seeds and all(i < inner for i in seeds)
+
+
+def test_oracle_f16_accumulators_and_promote():
+    """f16 c cells take each k16 product rounded once to f16; every third K
+    step FragmentPromote adds them into the f32 cells and clears them."""
+    spec = load_kernel_data(*irgen.matmul_mma(128, 64, 160, "f16", promote_every=3), "mp")
+    a, b = _mma_inputs(128, 64, 160, "f16", 3)
+    got = interpret(spec, {"x0": a, "x1": b})["matmul"]
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    fc = np.zeros((128, 64), np.float32)
+    fh = np.zeros((128, 64), np.float32)
+    for i, k0 in enumerate(range(0, 160, 16)):
+        fh = (a64[:, k0:k0 + 16] @ b64[k0:k0 + 16] + fh).astype(np.float16).astype(np.float32)
+        if i % 3 == 2:
+            fc, fh = (fc + fh).astype(np.float32), np.zeros_like(fh)
+    assert np.array_equal(got, (fc + fh).astype(np.float32))
+    assert ir.parse_stmt(repr(ir.FragmentPromote(dst="fc[1]", src="fh[1]"))) == \
+        ir.FragmentPromote(dst="fc[1]", src="fh[1]")
