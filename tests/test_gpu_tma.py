@@ -246,3 +246,15 @@ def test_matmul_mma_f16_accumulators(every):
     got = _run(spec, {"x0": a, "x1": b})["matmul"]
     scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
     assert np.all(np.abs(got - want) <= 2.0 ** -9 * scale)
+
+
+def test_random_box_copies_bitexact():
+    """40 seeded box copies (every dtype and swizzle, view and box sizes,
+    origins off every edge, rank-3 views) bit for bit against the oracle."""
+    from tests.tma_cases import random_box_cases
+    for i, (case, view3) in enumerate(random_box_cases(40, seed=1)):
+        spec = box_case(case, view3=view3, name=f"rb{i}")
+        x = box_inputs(spec, seed=2)
+        want = interpret(spec, {"x0": x["x0"].copy()})["out"]
+        got = _run(spec, x)["out"]
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (i, case, view3)

@@ -421,3 +421,12 @@ def test_oracle_f16_accumulators_and_promote():
     assert np.array_equal(got, (fc + fh).astype(np.float32))
     assert ir.parse_stmt(repr(ir.FragmentPromote(dst="fc[1]", src="fh[1]"))) == \
         ir.FragmentPromote(dst="fc[1]", src="fh[1]")
+
+
+@pytest.mark.parametrize("case, view3", __import__("tests.tma_cases", fromlist=["x"])
+                         .random_box_cases(40, seed=1))
+def test_oracle_random_box_copies(case, view3):
+    spec = box_case(case, view3=view3, name="rb")
+    x = box_inputs(spec, seed=2)
+    got = interpret(spec, {"x0": x["x0"].copy()})["out"]
+    assert np.array_equal(got, box_reference(case, x["x0"]))

@@ -67,3 +67,29 @@ def unarrived_wait(n=64):
                        ("out", (n,), "f32"), ["x0", "out"], (1, 1, 1), (n, 1, 1),
                        pid="unarrived")
     return load_kernel_data(gm[0], gm[1], "unarrived")
+
+
+def random_box_cases(n, seed=0):
+    """Seeded box copies over the descriptor rules: dtype, swizzle (its box
+    row fixed by the span), view and box sizes, and box origins that run
+    off every edge of the view (zero fill), some through a rank-3 view."""
+    rng = np.random.default_rng(seed)
+    eb = {"f32": 4, "bf16": 2, "f16": 2, "f64": 8}
+    out = []
+    while len(out) < n:
+        dt = str(rng.choice(["f32", "bf16", "f16", "f64"]))
+        swz = str(rng.choice(["NONE", "NONE", "B32", "B64", "B128"]))
+        q = 16 // eb[dt]                                   # elements per 16 bytes
+        if swz == "NONE":
+            bc = q * int(rng.integers(1, 9))
+        else:
+            bc = {"B32": 32, "B64": 64, "B128": 128}[swz] // eb[dt]
+        cols = q * int(rng.integers(1, 12))
+        rows = int(rng.integers(2, 70))
+        br = int(rng.integers(1, 33))
+        nbr, nbc = int(rng.integers(1, 4)), int(rng.integers(1, 4))
+        off_r = int(rng.integers(-br, rows))
+        off_c = q * int(rng.integers(-(bc // q) - 1, cols // q + 1))
+        view3 = bool(rng.integers(0, 2)) and rows % 2 == 0 and br % 2 == 0 and off_r % 2 == 0
+        out.append(((dt, swz, rows, cols, br, bc, nbr, nbc, off_r, off_c), view3))
+    return out
