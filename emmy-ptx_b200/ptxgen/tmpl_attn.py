@@ -281,6 +281,7 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
               "grid_per_sm": 16, "grid_max": max(1, math.ceil(total / 128)),
               "flops": 4 * BH * S * S * D}
     if tc_ok:
+        plan.v_direct = two_q and tmpl_attn2q.v_direct()
         pre, ws_bytes, tm = _emit_pre(mod, spec, plan, lay)
         plan_d.update({
             "block": threads, "grid_per_sm": 1,
@@ -310,7 +311,8 @@ def _ws_layout(plan, lay):
         names = (["kh", "kl", "vh", "vl"] if lay["q_tmem"] else
                  ["qh", "ql", "kh", "kl", "vh", "vl"])
     else:
-        names = ["kh", "vh"]
+        # K only when given transposed; V^T unless P V reads V as stored
+        names = ["kh"] + ([] if getattr(plan, "v_direct", False) else ["vh"])
     for nm in names:
         off[nm] = cur
         cur += n
@@ -346,9 +348,11 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
                                                "_pre_k"))
             pre.append({"entry": f"{spec.entry}_pre_k", "block": 256, "grid_per_sm": 8,
                         "grid_max": BH * (D // 32) * (S // 32)})
-        mod.kernels.append(_emit_transpose(spec, plan, plan.v, S, D, off["vh"], None, "_pre_v"))
-        pre.append({"entry": f"{spec.entry}_pre_v", "block": 256, "grid_per_sm": 8,
-                    "grid_max": BH * (S // 32) * (D // 32)})
+        if not plan.v_direct:
+            mod.kernels.append(_emit_transpose(spec, plan, plan.v, S, D, off["vh"], None,
+                                               "_pre_v"))
+            pre.append({"entry": f"{spec.entry}_pre_v", "block": 256, "grid_per_sm": 8,
+                        "grid_max": BH * (S // 32) * (D // 32)})
     dt = "f32" if f32 else "bf16"
     e = plan.e
     atom = plan.atom
@@ -371,7 +375,8 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
         tm += [tmap("tmap_qh", plan.q, 0, D, S, BQ),
                (tmap("tmap_kh", "@ws", off["kh"], D, S, plan.bkv) if plan.k_trans else
                 tmap("tmap_kh", plan.k, 0, D, S, plan.bkv)),
-               tmap("tmap_vh", "@ws", off["vh"], S, D, D)]
+               (tmap("tmap_vh", plan.v, 0, D, S, plan.bkv) if plan.v_direct else
+                tmap("tmap_vh", "@ws", off["vh"], S, D, D))]
     return pre, max(total, 16), tm
 
 

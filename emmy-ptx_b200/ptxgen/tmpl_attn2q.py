@@ -65,6 +65,14 @@ S_COL = (0, BKV)                                       # S_A, S_B
 O_COL = (2 * BKV, 2 * BKV + D)                         # O_A, O_B
 
 
+def v_direct() -> bool:
+    """P V reads V as stored ([keys][D], D contiguous) as an MN-major B
+    operand (allowed for 16-bit types), so no pre-pass writes V^T;
+    ``EMMY_ATTN_V_DIRECT=0`` restores the transposing pre-pass.  Read when a
+    kernel is compiled."""
+    return os.environ.get("EMMY_ATTN_V_DIRECT", "1") not in ("0", "")
+
+
 def eligible(plan) -> bool:
     """bf16, D = 128, whole 256-row units: the two-tile kernel applies."""
     if os.environ.get("EMMY_ATTN_2Q", "1") in ("0", ""):
@@ -74,6 +82,7 @@ def eligible(plan) -> bool:
 
 
 def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
+    VD = v_direct()
     S, BH = plan.s, plan.bh
     nkv = S // BKV
     qblocks = S // (2 * BQ)
@@ -169,7 +178,8 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
     kmaj = _desc_const(16, 1024, 2)        # K-major, 128-byte swizzle, 8-row groups 1 KB apart
     id_s, id_o = k.reg("u32"), k.reg("u32")
     k(f"mov.u32 {id_s}, {_idesc('f16', BQ, BKV)}")
-    k(f"mov.u32 {id_o}, {_idesc('f16', BQ, D)}")
+    # V as stored is MN-major for P V: instruction-descriptor bit 16
+    k(f"mov.u32 {id_o}, {_idesc('f16', BQ, D) | ((1 << 16) if VD else 0)}")
     yes = k.reg("pred")
     k(f"setp.eq.u32 {yes}, 0, 0")
 
@@ -182,6 +192,15 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
         return r
 
     d_base = mkdesc(ring)
+    # MN-major, 128-byte swizzle: along D 64 elements per 128-byte row, the
+    # next 64 (the second D chunk) 16 KB on (leading offset); along the keys
+    # 8 rows of 128 bytes, the next 8 rows 1 KB on (stride offset)
+    mnmaj = _desc_const(CHUNK, 1024, 2)
+    ad0, d_base_mn = k.reg("u32"), k.reg("u64")
+    k(f"shr.u32 {ad0}, {ring}, 4")
+    k(f"and.b32 {ad0}, {ad0}, 16383")
+    k(f"cvt.u64.u32 {d_base_mn}, {ad0}")
+    k(f"or.b64 {d_base_mn}, {d_base_mn}, 0x{mnmaj:016X}")
 
     def dsc(base_d, off):
         assert off % 16 == 0
@@ -189,11 +208,11 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
         k(f"add.s64 {r}, {base_d}, {off >> 4}")
         return r
 
-    def stage_desc(st_, offs):
+    def stage_desc(st_, offs, base_d=None):
         # the stage's operand base: offs[0] for stage 0, offs[1] for stage 1
         r, t = k.reg("u64"), k.reg("u64")
         k(f"mul.wide.u32 {t}, {st_}, {(offs[1] - offs[0]) >> 4}")
-        k(f"add.s64 {r}, {d_base}, {t}")
+        k(f"add.s64 {r}, {base_d or d_base}, {t}")
         return dsc(r, offs[0]) if offs[0] else r
 
     def issue_qk(x, gg, commit_k, commit_q=None):
@@ -243,7 +262,7 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
         cx.wait(bar_at("p_full", x), pph, abort_l)
         cx.wait(bar_at("v_full", st_), phf, abort_l)
         k("tcgen05.fence::after_thread_sync")
-        vd = stage_desc(st_, OFF_V)
+        vd = stage_desc(st_, OFF_V, d_base_mn if VD else None)
         o_t = k.reg("u32")
         k(f"add.u32 {o_t}, {tmem}, {O_COL[x]}")
         firstb = k.reg("pred")
@@ -254,7 +273,9 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
                 a_ = k.reg("u32")
                 # keys c*64 + kk*16 .. +15: packed two per column from S_x's first
                 k(f"add.u32 {a_}, {tmem}, {S_COL[x] + c * 32 + kk * 8}")
-                b_ = dsc(vd, c * CHUNK + kk * 32)
+                # keys c*64 + kk*16 .. +15: V [keys][D] rows (MN-major) or
+                # V^T [D][keys] columns (K-major)
+                b_ = dsc(vd, (c * 4 + kk) * 2048 if VD else c * CHUNK + kk * 32)
                 acc = firstb if first else yes
                 first = False
                 k(f"@{pm} tcgen05.mma.cta_group::1.kind::f16 [{o_t}], [{a_}], {b_}, {id_o}, {acc}")
@@ -358,8 +379,8 @@ def emit_tc2q(k: Kernel, spec, plan, base, tid, cta, ncta):
         for c in range(2):
             dst, c0, c1 = k.reg("u32"), k.reg("u32"), k.reg("u32")
             k(f"add.u32 {dst}, {sbase}, {offs[0] + c * CHUNK}")
-            if nm == "k":
-                # K [keys, D]: D chunk c, key rows krow .. +127
+            if nm == "k" or VD:
+                # K or V [keys, D]: D chunk c, key rows krow .. +127
                 k(f"mov.u32 {c0}, {c * 64}")
                 k(f"mov.u32 {c1}, {krow}")
             else:
