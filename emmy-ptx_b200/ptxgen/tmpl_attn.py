@@ -52,8 +52,8 @@ from .tmpl_mma import ERR_WAIT_TIMEOUT, PLAN_MAGIC, _Ctx, _desc_const
 
 
 def _late_import():
-    from . import tmpl_attn2q
-    return tmpl_attn2q
+    from . import tmpl_attn2h, tmpl_attn2q
+    return tmpl_attn2q, tmpl_attn2h
 
 LOG2E = 1.4426950408889634
 SMEM_MAX = 232448            # shared memory per CTA, static + dynamic
@@ -249,10 +249,14 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
     p = k.reg("pred")
     simt = k.label("simt")
     # bf16 with D = 128: two query tiles per unit (tmpl_attn2q)
-    tmpl_attn2q = _late_import()
-    two_q = tmpl_attn2q.eligible(plan)
-    dyn = tmpl_attn2q.SMEM_DYN if two_q else lay["total"] + 1024
-    threads = tmpl_attn2q.THREADS if two_q else lay["threads"]
+    # bf16 with D = 128: two query tiles per unit on 64-key blocks with two
+    # S buffers per tile (tmpl_attn2h), else on 128-key blocks (tmpl_attn2q)
+    tmpl_attn2q, tmpl_attn2h = _late_import()
+    half = tmpl_attn2h.eligible(plan)
+    two_q = half or tmpl_attn2q.eligible(plan)
+    tq = tmpl_attn2h if half else tmpl_attn2q
+    dyn = tq.SMEM_DYN if two_q else lay["total"] + 1024
+    threads = tq.THREADS if two_q else lay["threads"]
     if plan.tc and dyn <= 232448 - 1024:
         mod.add_global(".extern .shared .align 1024 .b8 dsmem[];")
         flag, dsz = k.reg("u32"), k.reg("u32")
@@ -264,7 +268,9 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
         k(f"mov.u32 {dsz}, %dynamic_smem_size")
         k(f"setp.lt.u32 {p}, {dsz}, {dyn}")
         k(f"@{p} bra {simt}")
-        if two_q:
+        if half:
+            tmpl_attn2h.emit_tc2h(k, spec, plan, base, tid, cta, ncta)
+        elif two_q:
             tmpl_attn2q.emit_tc2q(k, spec, plan, base, tid, cta, ncta)
         else:
             _emit_tc(k, spec, plan, lay, base, tid, cta, ncta)
@@ -281,7 +287,8 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
               "grid_per_sm": 16, "grid_max": max(1, math.ceil(total / 128)),
               "flops": 4 * BH * S * S * D}
     if tc_ok:
-        plan.v_direct = two_q and tmpl_attn2q.v_direct()
+        plan.v_direct = half or (two_q and tmpl_attn2q.v_direct())
+        plan.kv_box = tmpl_attn2h.BKV if half else plan.bkv
         pre, ws_bytes, tm = _emit_pre(mod, spec, plan, lay)
         plan_d.update({
             "block": threads, "grid_per_sm": 1,
@@ -289,7 +296,8 @@ def emit_attention(spec: KernelSpec, plan: AttnPlan) -> Module:
             "workspace": {"sym": "emmy_ws", "bytes": ws_bytes}, "pre": pre, "tmaps": tm,
             "flags": [{"sym": "emmy_plan", "value": PLAN_MAGIC}],
             "tile": [2 * BQ if two_q else BQ, plan.bkv, D], "passes": plan.passes,
-            "schedule": "two query tiles" if two_q else "one query tile",
+            "schedule": ("two query tiles, 64-key blocks, two S buffers per tile" if half
+                         else "two query tiles" if two_q else "one query tile"),
         })
     mod.plan = plan_d
     return mod
@@ -312,7 +320,8 @@ def _ws_layout(plan, lay):
                  ["qh", "ql", "kh", "kl", "vh", "vl"])
     else:
         # K only when given transposed; V^T unless P V reads V as stored
-        names = ["kh"] + ([] if getattr(plan, "v_direct", False) else ["vh"])
+        names = (["kh"] if plan.k_trans else []) + (
+            [] if getattr(plan, "v_direct", False) else ["vh"])
     for nm in names:
         off[nm] = cur
         cur += n
@@ -373,9 +382,9 @@ def _emit_pre(mod: Module, spec: KernelSpec, plan, lay):
                tmap("tmap_vh", "@ws", off["vh"], S, D, D), tmap("tmap_vl", "@ws", off["vl"], S, D, D)]
     else:
         tm += [tmap("tmap_qh", plan.q, 0, D, S, BQ),
-               (tmap("tmap_kh", "@ws", off["kh"], D, S, plan.bkv) if plan.k_trans else
-                tmap("tmap_kh", plan.k, 0, D, S, plan.bkv)),
-               (tmap("tmap_vh", plan.v, 0, D, S, plan.bkv) if plan.v_direct else
+               (tmap("tmap_kh", "@ws", off["kh"], D, S, plan.kv_box) if plan.k_trans else
+                tmap("tmap_kh", plan.k, 0, D, S, plan.kv_box)),
+               (tmap("tmap_vh", plan.v, 0, D, S, plan.kv_box) if plan.v_direct else
                 tmap("tmap_vh", "@ws", off["vh"], S, D, D))]
     return pre, max(total, 16), tm
 

@@ -1,0 +1,140 @@
+"""A CPU model of the barrier protocol of the two-tile bf16 attention on
+64-key blocks (``ptxgen/tmpl_attn2h.py``), run with the random scheduler,
+TMA and commit rules of ``tests/test_attn2q_protocol.py``.
+
+Each query tile X keeps two S buffers in TMEM (S_X0, S_X1): block g uses
+buffer g % 2, so S_X = Q_X K_{g+2}^T can be issued as soon as P_X V_g has
+read buffer g % 2, while the softmax still works on block g + 1.  Per
+block g the MMA thread issues PV_A(g), PV_B(g), then QK_A(g+2), QK_B(g+2);
+a unit starts with QK_A, QK_B of its first two blocks.  Barriers per tile
+and buffer: s_full, p_full (128 arrivals), pv_done; per K/V stage full and
+empty; per unit q_full / q_empty.  Checked: no deadlock, no TMEM hazard and
+no wait that could pass on the wrong phase, for 2 to 4 stages; and that
+dropping the pv_done wait before a QK is caught.  P V of consecutive blocks
+may both be in flight on O_X: one thread's MMAs accumulate in issue
+order."""
+
+import pytest
+
+from tests.test_attn2q_protocol import run
+
+
+def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
+    W = lambda name, n: ("wait", name, n & 1, n)                  # noqa: E731
+    Wi = lambda name, n: ("wait", name, (n & 1) ^ 1, n - 1)       # noqa: E731
+
+    def prod():
+        g = 0
+        for u in range(units):
+            yield Wi("q_empty", u)
+            yield ("tma", "q_full")
+            for _ in range(nkv):
+                st, n = g % kvst, g // kvst
+                yield Wi(f"k_empty{st}", n)
+                yield ("tma", f"k_full{st}")
+                yield Wi(f"v_empty{st}", n)
+                yield ("tma", f"v_full{st}")
+                g += 1
+
+    def mma():
+        def qk(x, g, last_b):
+            st, h = g % kvst, g % 2
+            yield W(f"k_full{st}", g // kvst)
+            if g >= 2 and qk_waits_pv:
+                yield W(f"pv_done{x}{h}", (g - 2) >> 1)
+            yield ("write", f"S{x}{h}", g)
+            yield ("commit", f"s_full{x}{h}")
+            if x == "B":
+                yield ("commit", f"k_empty{st}")
+                if last_b:
+                    yield ("commit", "q_empty")
+
+        def pv(x, g, u):
+            st, h = g % kvst, g % 2
+            yield W(f"p_full{x}{h}", g >> 1)
+            yield W(f"v_full{st}", g // kvst)
+            yield ("read", f"S{x}{h}", g)
+            yield ("write", f"O{x}", u)
+            yield ("commit", f"pv_done{x}{h}")
+            if x == "B":
+                yield ("commit", f"v_empty{st}")
+
+        def one_thread():
+            g0 = 0
+            for u in range(units):
+                yield W("q_full", u)
+                for j in range(min(2, nkv)):
+                    yield from qk("A", g0 + j, False)
+                    yield from qk("B", g0 + j, j == nkv - 1)
+                for j in range(nkv):
+                    g = g0 + j
+                    yield from pv("A", g, u)
+                    yield from pv("B", g, u)
+                    if j + 2 < nkv:
+                        yield from qk("A", g + 2, False)
+                        yield from qk("B", g + 2, j + 2 == nkv - 1)
+                g0 += nkv
+
+        def qk_thread():
+            g = 0
+            for u in range(units):
+                yield W("q_full", u)
+                for j in range(nkv):
+                    yield from qk("A", g, False)
+                    yield from qk("B", g, j == nkv - 1)
+                    g += 1
+
+        def pv_thread():
+            g = 0
+            for u in range(units):
+                for _ in range(nkv):
+                    yield from pv("A", g, u)
+                    yield from pv("B", g, u)
+                    g += 1
+
+        return (qk_thread(), pv_thread()) if split else (one_thread(),)
+
+    def softmax(x):                        # one warp of four; 32 arrivals each
+        g = 0
+        for u in range(units):
+            for j in range(nkv):
+                h = g % 2
+                yield W(f"s_full{x}{h}", g >> 1)
+                yield ("read", f"S{x}{h}", g)
+                if j and rng.random() < 0.3:
+                    yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
+                    yield ("read", f"O{x}", u)
+                    yield ("write", f"O{x}", u)
+                yield ("write", f"S{x}{h}", g)      # P of block g over its scores
+                yield ("arrive", f"p_full{x}{h}", 32)
+                g += 1
+            yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
+            yield ("read", f"O{x}", u)           # the epilogue
+
+    issuers = mma()
+    return {"prod": prod(), **{f"mma{i}": t for i, t in enumerate(issuers)},
+            **{f"sm{x}{i}": softmax(x) for x in "AB" for i in range(4)}}
+
+
+SHAPES = [(1, 1), (1, 2), (2, 1), (1, 3), (3, 3), (2, 5), (4, 4), (3, 8)]
+
+
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("kvst", [2, 3, 4])
+def test_half_block_protocol_has_no_deadlock_or_aliasing(kvst, split):
+    """One issuing thread, or S = Q K^T and O += P V issued by two threads
+    (each thread's commits cover only its own MMAs)."""
+    for units, nkv in SHAPES:
+        for seed in range(150):
+            r = run(units, nkv, kvst, seed, roles=_roles, ordered_writes=True, split=split)
+            assert r == "ok", (units, nkv, seed, r)
+
+
+def test_model_finds_a_missing_pv_wait():
+    """Without the wait for P V of block g - 2, S = Q K^T of block g could
+    overwrite P of block g - 2 before it is read."""
+    for split in (False, True):
+        found = any(run(u, n, 4, seed, roles=_roles, ordered_writes=True,
+                        qk_waits_pv=False, split=split) != "ok"
+                    for u, n in SHAPES for seed in range(150))
+        assert found

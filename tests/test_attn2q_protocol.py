@@ -127,14 +127,17 @@ def _roles(units, nkv, kvst, rng, o_empty=False, qk_waits_pv=True):
             **{f"sm{x}{i}": softmax(x) for x in "AB" for i in range(4)}}
 
 
-def run(units, nkv, kvst, seed, **kw):
+def run(units, nkv, kvst, seed, roles=None, ordered_writes=False, **kw):
     """Random schedule; "ok", "deadlock" or the first hazard found.
 
     An MMA is in flight from its issue until a later commit of the issuing
     thread completes (a commit arrives once every earlier MMA of the thread
     is done); in-flight MMAs may execute in any order, so two in flight that
     touch the same TMEM region, one of them writing, are a hazard, and so is
-    a softmax or epilogue access to a region an in-flight MMA writes."""
+    a softmax or epilogue access to a region an in-flight MMA writes.
+    ``ordered_writes``: two in-flight MMAs that both accumulate into one
+    region are not a hazard (the tensor core applies one thread's MMAs to an
+    accumulator in issue order -- the way every K loop accumulates)."""
     rng = random.Random(seed)
     bars = {}
 
@@ -143,13 +146,13 @@ def run(units, nkv, kvst, seed, **kw):
             bars[name] = Bar(128 if name.startswith(("p_full", "o_empty")) else 1)
         return bars[name]
 
-    gens = _roles(units, nkv, kvst, rng, **kw)
+    gens = (roles or _roles)(units, nkv, kvst, rng, **kw)
     cur = {r: next(g) for r, g in gens.items()}
     tma = []
-    commits = []          # (barrier, number of MMAs issued before it)
-    flight = []           # (issue number, kind, region, value)
-    issued = 0
-    state = {"SA": None, "SB": None, "OA": None, "OB": None}
+    commits = []          # (issuer, barrier, number of its MMAs issued before it)
+    flight = []           # (issuer, issue number, kind, region, value)
+    issued: dict = {}     # MMAs issued so far, per issuing role ("mma...")
+    state: dict = {}              # TMEM region -> the value last written
     while cur or tma or commits:
         ready = [r for r, op in cur.items()
                  if op[0] != "wait" or bar(op[1]).passes(op[2])]
@@ -161,10 +164,13 @@ def run(units, nkv, kvst, seed, **kw):
             bar(tma.pop(rng.randrange(len(tma)))).arrive(1)
             continue
         if c == "COMMIT":
-            name, upto = commits.pop(0)
-            for f in [f for f in flight if f[0] < upto]:
-                if f[1] == "write":
-                    state[f[2]] = f[3]
+            # one issuer's commits complete in its order; issuers are independent
+            who = rng.choice(sorted({cm[0] for cm in commits}))
+            i = next(n for n, cm in enumerate(commits) if cm[0] == who)
+            _, name, upto = commits.pop(i)
+            for f in [f for f in flight if f[0] == who and f[1] < upto]:
+                if f[2] == "write":
+                    state[f[3]] = f[4]
                 flight.remove(f)
             bar(name).arrive(1)
             continue
@@ -176,21 +182,23 @@ def run(units, nkv, kvst, seed, **kw):
         elif op[0] == "tma":
             tma.append(op[1])
         elif op[0] == "commit":
-            commits.append((op[1], issued))
-        elif op[0] in ("read", "write") and c == "mma":
+            commits.append((c, op[1], issued.get(c, 0)))
+        elif op[0] in ("read", "write") and c.startswith("mma"):
             for f in flight:
-                if f[2] == op[1] and "write" in (f[1], op[0]):
-                    return f"hazard: MMA {op[0]} of {op[1]} while an MMA {f[1]} is in flight"
-            if op[0] == "read" and op[1].startswith("S") and state[op[1]] != op[2]:
-                if not any(f[1] == "write" and f[2] == op[1] for f in flight):
-                    return f"hazard: P.V read {op[1]} for block {op[2]}, it holds {state[op[1]]}"
-            flight.append((issued, op[0], op[1], op[2]))
-            issued += 1
+                if ordered_writes and f[0] == c and f[2] == op[0] == "write":
+                    continue
+                if f[3] == op[1] and "write" in (f[2], op[0]):
+                    return f"hazard: MMA {op[0]} of {op[1]} while an MMA {f[2]} is in flight"
+            if op[0] == "read" and op[1].startswith("S") and state.get(op[1]) != op[2]:
+                if not any(f[2] == "write" and f[3] == op[1] for f in flight):
+                    return f"hazard: P.V read {op[1]} for block {op[2]}, it holds {state.get(op[1])}"
+            flight.append((c, issued.get(c, 0), op[0], op[1], op[2]))
+            issued[c] = issued.get(c, 0) + 1
         elif op[0] in ("read", "write"):
-            if any(f[2] == op[1] for f in flight if f[1] == "write" or op[0] == "write"):
+            if any(f[3] == op[1] for f in flight if f[2] == "write" or op[0] == "write"):
                 return f"hazard: {c} {op[0]} of {op[1]} while an MMA touches it"
-            if op[0] == "read" and state[op[1]] != op[2]:
-                return f"hazard: {c} read {op[1]} wanting {op[2]}, it holds {state[op[1]]}"
+            if op[0] == "read" and state.get(op[1]) != op[2]:
+                return f"hazard: {c} read {op[1]} wanting {op[2]}, it holds {state.get(op[1])}"
             if op[0] == "write":
                 state[op[1]] = op[2]
         else:

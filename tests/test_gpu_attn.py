@@ -86,20 +86,30 @@ def test_generated(dtype, shape):
     assert ok, worst
 
 
-@pytest.mark.parametrize("two_q", ["1", "0"])
-@pytest.mark.parametrize("shape", [(1, 2, 256, 128), (2, 3, 512, 128), (1, 1, 1024, 128)])
-def test_bf16_d128_schedules(shape, two_q, monkeypatch):
-    """bf16 with D = 128 runs the two-query-tile kernel (``tmpl_attn2q``)
-    when S is a multiple of 256, else the one-tile kernel; both forms are
-    checked here at the same shapes (``EMMY_ATTN_2Q=0`` forces one tile)."""
-    monkeypatch.setenv("EMMY_ATTN_2Q", two_q)
+SCHEDULES = {"half": ({}, "two query tiles, 64-key blocks, two S buffers per tile"),
+             "two_q": ({"EMMY_ATTN_HALF": "0"}, "two query tiles"),
+             "one_q": ({"EMMY_ATTN_HALF": "0", "EMMY_ATTN_2Q": "0"}, "one query tile")}
+
+
+@pytest.mark.parametrize("sched", list(SCHEDULES))
+@pytest.mark.parametrize("shape", [(1, 2, 256, 128), (2, 3, 512, 128), (1, 1, 1024, 128),
+                                   (8, 16, 512, 128)])
+def test_bf16_d128_schedules(shape, sched, monkeypatch):
+    """bf16 with D = 128 and S a multiple of 256 runs the two-tile kernel on
+    64-key blocks (``tmpl_attn2h``); ``EMMY_ATTN_HALF=0`` selects the
+    two-tile kernel on 128-key blocks (``tmpl_attn2q``), and with
+    ``EMMY_ATTN_2Q=0`` too the one-tile kernel.  All three at the same
+    shapes, two launches each; the last shape has 256 units, so most CTAs
+    run two (the hand-over of Q and O between a CTA's units)."""
+    env, want = SCHEDULES[sched]
+    for key, val in env.items():
+        monkeypatch.setenv(key, val)
     b, h, s, d = shape
-    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), f"att2q{two_q}")
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), f"att{sched}")
     q, k, v = _bhsd(b, h, s, d, "bf16", seed=21)
     from ptxgen.runtime import PreparedKernel
     pk = PreparedKernel(spec)
     try:
-        want = "two query tiles" if two_q == "1" else "one query tile"
         assert pk.plan["schedule"] == want
         pk.upload({"q": q, "k": k, "v": v})
         for _ in range(2):
@@ -112,11 +122,14 @@ def test_bf16_d128_schedules(shape, two_q, monkeypatch):
     assert ok, worst
 
 
-def test_bf16_two_tile_rescale_path():
+@pytest.mark.parametrize("sched", ["half", "two_q"])
+def test_bf16_two_tile_rescale_path(sched, monkeypatch):
     """Keys scaled up along the sequence: every row's max keeps growing, so
-    the two-tile kernel rescales O in TMEM block after block."""
+    the two-tile kernels rescale O in TMEM block after block."""
+    for key, val in SCHEDULES[sched][0].items():
+        monkeypatch.setenv(key, val)
     b, h, s, d = 1, 2, 2048, 128
-    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "att2qr")
+    spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), f"att2r{sched}")
     q, k, v = _bhsd(b, h, s, d, "bf16", seed=23)
     grow = (1.0 + 8.0 * np.arange(s) / s)[None, None, :, None]
     k = (k.astype(np.float64) * grow).astype(k.dtype)
