@@ -638,11 +638,12 @@ EXP2_POLY = (0.9999280571937561, 0.6932609677314758, 0.2426111251115799,
 EXP_POLY_DEFAULT = 1
 
 
-def _exp_poly_share() -> int:
+def _exp_poly_share(default: int = EXP_POLY_DEFAULT) -> int:
     """Element pairs out of every four whose exp2 runs on the FMA pipe
-    (polynomial) instead of the MUFU (``ex2.approx``); bf16 P only."""
+    (polynomial) instead of the MUFU (``ex2.approx``); bf16 P only.
+    ``EMMY_ATTN_EXP_POLY`` overrides the kernel's default."""
     v = os.environ.get("EMMY_ATTN_EXP_POLY")
-    return max(0, min(4, int(v))) if v else EXP_POLY_DEFAULT
+    return max(0, min(4, int(v))) if v else default
 
 
 def _pair_const(v: float) -> str:

@@ -182,10 +182,11 @@ def test_bf16_shared_o(monkeypatch):
     assert np.abs(out - ref).max() <= 2e-2 * np.abs(ref).max()
 
 
-@pytest.mark.parametrize("share", [0, 4])
+@pytest.mark.parametrize("share", [0, 1, 4])
 def test_bf16_polynomial_exp2(share, monkeypatch):
-    """bf16 P with none or all of exp2 on the FMA-pipe polynomial (the
-    default, one pair of every four, runs in every other bf16 test)."""
+    """bf16 P with none, one pair in four, or all of exp2 on the FMA-pipe
+    polynomial (the kernels' defaults differ: the one-tile and 128-key
+    two-tile kernels use one pair in four, the 64-key kernel none)."""
     monkeypatch.setenv("EMMY_ATTN_EXP_POLY", str(share))
     b, h, s, d = 2, 2, 512, 128
     spec = load_kernel_data(*irgen.attention_bhsd(b, h, s, d, "bf16"), "attp")
