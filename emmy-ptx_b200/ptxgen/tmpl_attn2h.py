@@ -30,7 +30,8 @@ Barriers (modelled on the CPU in ``tests/test_attn2h_protocol.py``):
 ``v_full``/``v_empty`` per stage; per tile X and buffer b ``s_full``,
 ``p_full`` (128 arrivals), ``pv_done``.  Every wait is bounded by
 ``%globaltimer`` (``emmy_err`` 0x201 on expiry; the kernel then drains its
-MMAs, frees TMEM and returns).  No pre-pass: K and V are read as stored.
+MMAs, frees TMEM and returns).  K and V are read as stored (a K given
+transposed comes from ``tmpl_attn``'s pre-pass); no V^T pre-pass.
 """
 
 from __future__ import annotations

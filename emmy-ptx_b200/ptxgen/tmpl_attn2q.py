@@ -7,7 +7,7 @@ tile A (rows 0-127) and tile B (rows 128-255).  Per 128-key block g:
 
     S_A = Q_A K_g^T   S_B = Q_B K_g^T     (into S_A, S_B in TMEM)
     softmax A -> P_A over S_A             softmax B -> P_B over S_B
-    O_A += P_A V_g    O_B += P_B V_g      (P from TMEM, V^T from smem)
+    O_A += P_A V_g    O_B += P_B V_g      (P from TMEM, V from smem)
 
 TMEM holds S_A, S_B, O_A, O_B: 4 x 128 columns, all 512.  The MMA thread
 issues QK_A(g), QK_B(g), then per block PV_A(g), QK_A(g+1), PV_B(g),
@@ -20,7 +20,8 @@ CTA: 320 threads, one per SM (192 KB of shared memory):
 * warp 0 -- allocates TMEM; issues every MMA (converged loop, one elected
   lane), commits to the barriers;
 * warp 1 -- TMA: the unit's Q_A and Q_B (64 KB), then per key block K_g and
-  V^T_g (32 KB each) into two stages;
+  V_g (32 KB each; V as stored, an MN-major operand, or V^T from the
+  pre-pass with ``EMMY_ATTN_V_DIRECT=0``) into two stages;
 * warps 2-5 -- softmax and epilogue of tile A, one thread per query row
   (TMEM lane quarter warp % 4); warps 6-9 -- the same for tile B.  Per
   block: ``tcgen05.ld`` of the row's 128 scores, row max, ``p = exp2(s *
@@ -37,7 +38,8 @@ Barriers (the protocol is modelled on the CPU in
 Every wait is bounded by ``%globaltimer`` (``emmy_err`` 0x201 on expiry;
 the kernel then drains its MMAs, frees TMEM and returns).
 
-The pre-pass of ``tmpl_attn`` (V^T, and K from K^T) feeds it; any launch
+``tmpl_attn``'s pre-pass feeds it K from K^T when the IR gives K
+transposed (and V^T with ``EMMY_ATTN_V_DIRECT=0``); any launch
 that does not match the plan takes ``tmpl_attn``'s SIMT path.
 """
 
