@@ -19,7 +19,7 @@ import pytest
 from tests.test_attn2q_protocol import run
 
 
-def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
+def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False):
     W = lambda name, n: ("wait", name, n & 1, n)                  # noqa: E731
     Wi = lambda name, n: ("wait", name, (n & 1) ^ 1, n - 1)       # noqa: E731
 
@@ -41,7 +41,10 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
             st, h = g % kvst, g % 2
             yield W(f"k_full{st}", g // kvst)
             if g >= 2 and qk_waits_pv:
-                yield W(f"pv_done{x}{h}", (g - 2) >> 1)
+                if p_smem:      # S of block g - 2 read by the softmax
+                    yield W(f"s_free{x}{h}", (g - 2) >> 1)
+                else:           # P of block g - 2 (over S) read by P V
+                    yield W(f"pv_done{x}{h}", (g - 2) >> 1)
             yield ("write", f"S{x}{h}", g)
             yield ("commit", f"s_full{x}{h}")
             if x == "B":
@@ -53,7 +56,7 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
             st, h = g % kvst, g % 2
             yield W(f"p_full{x}{h}", g >> 1)
             yield W(f"v_full{st}", g // kvst)
-            yield ("read", f"S{x}{h}", g)
+            yield ("read", f"P{x}{h}" if p_smem else f"S{x}{h}", g)
             yield ("write", f"O{x}", u)
             yield ("commit", f"pv_done{x}{h}")
             if x == "B":
@@ -101,11 +104,19 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
                 h = g % 2
                 yield W(f"s_full{x}{h}", g >> 1)
                 yield ("read", f"S{x}{h}", g)
+                if p_smem:
+                    yield ("arrive", f"s_free{x}{h}", 32)
                 if j and rng.random() < 0.3:
                     yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
                     yield ("read", f"O{x}", u)
                     yield ("write", f"O{x}", u)
-                yield ("write", f"S{x}{h}", g)      # P of block g over its scores
+                if p_smem:
+                    # the P buffer of block g - 2 must have been read by its P V
+                    if g >= 2:
+                        yield W(f"pv_done{x}{h}", (g - 2) >> 1)
+                    yield ("write", f"P{x}{h}", g)
+                else:
+                    yield ("write", f"S{x}{h}", g)  # P of block g over its scores
                 yield ("arrive", f"p_full{x}{h}", 32)
                 g += 1
             yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
@@ -119,14 +130,22 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False):
 SHAPES = [(1, 1), (1, 2), (2, 1), (1, 3), (3, 3), (2, 5), (4, 4), (3, 8)]
 
 
-@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("form", ["one issuer", "two issuers", "P in shared memory"])
 @pytest.mark.parametrize("kvst", [2, 3, 4])
-def test_half_block_protocol_has_no_deadlock_or_aliasing(kvst, split):
-    """One issuing thread, or S = Q K^T and O += P V issued by two threads
-    (each thread's commits cover only its own MMAs)."""
+def test_half_block_protocol_has_no_deadlock_or_aliasing(kvst, form):
+    """One issuing thread; S = Q K^T and O += P V issued by two threads
+    (each thread's commits cover only its own MMAs); and the same with P in
+    shared memory, where an S buffer is free once the softmax has read it
+    (``s_free``) and the softmax waits for the P V two blocks back before
+    overwriting that block's P buffer.  The kernel ships the two-issuer
+    form; the P-in-shared-memory form is a measured alternative (correct,
+    slower: it adds shared-memory operand traffic) kept modelled so a
+    future variant starts from a checked protocol."""
+    kw = {"one issuer": {}, "two issuers": {"split": True},
+          "P in shared memory": {"split": True, "p_smem": True}}[form]
     for units, nkv in SHAPES:
         for seed in range(150):
-            r = run(units, nkv, kvst, seed, roles=_roles, ordered_writes=True, split=split)
+            r = run(units, nkv, kvst, seed, roles=_roles, ordered_writes=True, **kw)
             assert r == "ok", (units, nkv, seed, r)
 
 
@@ -138,3 +157,9 @@ def test_model_finds_a_missing_pv_wait():
                         qk_waits_pv=False, split=split) != "ok"
                     for u, n in SHAPES for seed in range(150))
         assert found
+    # with P in shared memory: S of block g overwritten before the softmax
+    # has read it, once QK stops waiting for s_free
+    found = any(run(u, n, 4, seed, roles=_roles, ordered_writes=True, qk_waits_pv=False,
+                    split=True, p_smem=True) != "ok"
+                for u, n in SHAPES for seed in range(150))
+    assert found
