@@ -19,7 +19,8 @@ import pytest
 from tests.test_attn2q_protocol import run
 
 
-def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False):
+def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False,
+           pingpong=False, tok_wait=True):
     W = lambda name, n: ("wait", name, n & 1, n)                  # noqa: E731
     Wi = lambda name, n: ("wait", name, (n & 1) ^ 1, n - 1)       # noqa: E731
 
@@ -110,6 +111,16 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False):
                     yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
                     yield ("read", f"O{x}", u)
                     yield ("write", f"O{x}", u)
+                if pingpong:
+                    # the exp2 loops take turns: A(g) after B(g - 1), B(g)
+                    # after A(g); "MUFU" holds whose loop runs, and a loop
+                    # that finds another tile's mark at its end overlapped it
+                    if tok_wait:
+                        if x == "B":
+                            yield W("tokA", g)
+                        elif g:
+                            yield W("tokB", g - 1)
+                    yield ("write", "MUFU", (x, g))
                 if p_smem:
                     # the P buffer of block g - 2 must have been read by its P V
                     if g >= 2:
@@ -117,6 +128,9 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False):
                     yield ("write", f"P{x}{h}", g)
                 else:
                     yield ("write", f"S{x}{h}", g)  # P of block g over its scores
+                if pingpong:
+                    yield ("read", "MUFU", (x, g))
+                    yield ("arrive", f"tok{x}", 32)
                 yield ("arrive", f"p_full{x}{h}", 32)
                 g += 1
             yield W(f"pv_done{x}{(g - 1) % 2}", (g - 1) >> 1)
@@ -130,19 +144,22 @@ def _roles(units, nkv, kvst, rng, qk_waits_pv=True, split=False, p_smem=False):
 SHAPES = [(1, 1), (1, 2), (2, 1), (1, 3), (3, 3), (2, 5), (4, 4), (3, 8)]
 
 
-@pytest.mark.parametrize("form", ["one issuer", "two issuers", "P in shared memory"])
+@pytest.mark.parametrize("form", ["one issuer", "two issuers", "P in shared memory",
+                                  "exp2 loops in turn"])
 @pytest.mark.parametrize("kvst", [2, 3, 4])
 def test_half_block_protocol_has_no_deadlock_or_aliasing(kvst, form):
     """One issuing thread; S = Q K^T and O += P V issued by two threads
     (each thread's commits cover only its own MMAs); and the same with P in
     shared memory, where an S buffer is free once the softmax has read it
     (``s_free``) and the softmax waits for the P V two blocks back before
-    overwriting that block's P buffer.  The kernel ships the two-issuer
-    form; the P-in-shared-memory form is a measured alternative (correct,
-    slower: it adds shared-memory operand traffic) kept modelled so a
-    future variant starts from a checked protocol."""
+    overwriting that block's P buffer; and the two-issuer form with the two
+    tiles' exp2 loops taking turns (``tok`` barriers).  The kernel ships the
+    two-issuer form; the other two are measured alternatives (correct and
+    slower) kept modelled so a future variant starts from a checked
+    protocol."""
     kw = {"one issuer": {}, "two issuers": {"split": True},
-          "P in shared memory": {"split": True, "p_smem": True}}[form]
+          "P in shared memory": {"split": True, "p_smem": True},
+          "exp2 loops in turn": {"split": True, "pingpong": True}}[form]
     for units, nkv in SHAPES:
         for seed in range(150):
             r = run(units, nkv, kvst, seed, roles=_roles, ordered_writes=True, **kw)
@@ -162,4 +179,12 @@ def test_model_finds_a_missing_pv_wait():
     found = any(run(u, n, 4, seed, roles=_roles, ordered_writes=True, qk_waits_pv=False,
                     split=True, p_smem=True) != "ok"
                 for u, n in SHAPES for seed in range(150))
+    assert found
+
+
+def test_model_finds_overlapping_exp2_loops():
+    """Without the token waits the two tiles' exp2 loops overlap."""
+    found = any(run(u, n, 4, seed, roles=_roles, ordered_writes=True, split=True,
+                    pingpong=True, tok_wait=False) != "ok"
+                for u, n in SHAPES for seed in range(50))
     assert found

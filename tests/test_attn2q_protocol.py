@@ -143,7 +143,7 @@ def run(units, nkv, kvst, seed, roles=None, ordered_writes=False, **kw):
 
     def bar(name):
         if name not in bars:
-            bars[name] = Bar(128 if name.startswith(("p_full", "o_empty", "s_free")) else 1)
+            bars[name] = Bar(128 if name.startswith(("p_full", "o_empty", "s_free", "tok")) else 1)
         return bars[name]
 
     gens = (roles or _roles)(units, nkv, kvst, rng, **kw)
