@@ -155,20 +155,48 @@ def match_matmul(spec: KernelSpec) -> MatmulPlan:
     plan = MatmulPlan()
     plan.a, plan.b, plan.c, plan.m, plan.n, plan.k = a_buf, b_buf, c_buf, m, n, k
     plan.atomic, plan.slices = atomic, max(1, slices)
-    plan.bn = next((bn for bn in (256, 128, 64, 32) if n % bn == 0), 0)
+    plan.bn = _choose_bn(m, n)
+    plan.partial_n = bool(plan.bn) and n % plan.bn != 0
     slice_k = k // plan.slices if plan.slices and k % plan.slices == 0 else k
     # slices shorter than a K block are merged (same sum, other association)
     while plan.slices > 1 and (slice_k % BK or slice_k < 4 * BK):
         plan.slices //= 2
         slice_k = k // plan.slices
     if plan.bn and m % BM == 0 and k % BK == 0:
-        plan.slices = _choose_slices(k, (m // BM) * (n // plan.bn), plan.slices,
+        plan.slices = _choose_slices(k, (m // BM) * -(-n // plan.bn), plan.slices,
                                      atomic=plan.atomic)
         slice_k = k // plan.slices
     plan.slice_k = slice_k
     plan.tc = (m % BM == 0 and plan.bn > 0 and k % 32 == 0 and slice_k % BK == 0
                and m * n < 2 ** 31 and m * k < 2 ** 31 and k * n < 2 ** 31)
     return plan
+
+
+BN_RAGGED = (256, 224, 192, 160)   # widths a ragged N edge may use
+
+
+def _choose_bn(m: int, n: int) -> int:
+    """The C tile width (the MMA's N): 256 or 128 where it divides N; for
+    other N that are multiples of 32 a full-rate width -- N itself up to
+    256, else 256 -- with the N edge tile sticking out past N: its B rows
+    load as zeros (the tensor map's bounds) and its C columns past N are
+    not stored (every 32-column store chunk is wholly in or out).  Other N
+    take the largest of 64, 32 that divides them.  Narrower widths chosen
+    to fill the last wave of a few-tile product (224 for the 8-GPU row shard
+    of 8192^3, 160 or 128 for the rect shards) measured no faster, or much
+    slower, than 256 on B200, so the width is not chosen by wave count.
+    ``EMMY_MATMUL_BN`` (read when the kernel is compiled) forces a width of
+    ``BN_RAGGED`` or 128 for measurements."""
+    import os
+    forced = os.environ.get("EMMY_MATMUL_BN", "").strip()
+    exact = next((bn for bn in (256, 128, 64, 32) if n % bn == 0), 0)
+    if forced and n % 32 == 0 and int(forced) in BN_RAGGED + (128,):
+        return int(forced)
+    if exact >= 128 or n % 32:
+        return exact
+    if n <= 256:
+        return n if n >= 128 else exact
+    return 256
 
 
 # K slices.  On B200 the kind::tf32 accumulation truncates each MMA's sum,
@@ -335,8 +363,11 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
     stage_bytes = 2 * (a_bytes + b_bytes)
     # the operand ring, then two staging buffers for the TMA stores of C
     dyn_smem = STAGES * stage_bytes + 2 * EPI_BUF + 1024
-    tcols = max(32, 1 << (2 * BN - 1).bit_length())
-    mt, nt = M // BM, (N // BN if plan.bn else 1)
+    # the two TMEM accumulators sit a power of two apart (BN rounded up), as
+    # every other accumulator in these kernels does
+    acc_stride = 1 << (BN - 1).bit_length()
+    tcols = max(32, 2 * acc_stride)
+    mt, nt = M // BM, (-(-N // BN) if plan.bn else 1)
     units = mt * nt * plan.slices
     kblocks = plan.slice_k // BK
 
@@ -357,7 +388,8 @@ def emit_matmul(spec: KernelSpec, plan: MatmulPlan) -> Module:
         k(f"mov.u32 {dsz}, %dynamic_smem_size")
         k(f"setp.lt.u32 {p}, {dsz}, {dyn_smem}")
         k(f"@{p} bra {simt}")
-        _emit_tc(k, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes, tcols,
+        _emit_tc(k, plan, A, B, C, tid, cta, ncta, BN, acc_stride, a_bytes, b_bytes, stage_bytes,
+                 tcols,
                  mt, nt, units, kblocks)
         k("ret")
     k.place(simt)
@@ -654,8 +686,8 @@ def _emit_nonfinite_fix(k: Kernel, plan, A, B, special, sbuf, rowq, r7, row0, co
     k.place(skip)
 
 
-def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, stage_bytes,
-             tcols, mt, nt, units, kblocks):
+def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, acc_stride, a_bytes, b_bytes,
+             stage_bytes, tcols, mt, nt, units, kblocks):
     M, N, K = plan.m, plan.n, plan.k
     wlim = k.reg("u64")
     k(f"ld.global.u64 {wlim}, [emmy_wait_ns]")
@@ -805,7 +837,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     cx.wait(bar("bar_tempty", a_i), aph, abort_l)
     k("tcgen05.fence::after_thread_sync")
     dt = k.reg("u32")
-    k(f"mad.lo.u32 {dt}, {a_i}, {BN}, {tmem}")
+    k(f"mad.lo.u32 {dt}, {a_i}, {acc_stride}, {tmem}")
     kb2 = k.reg("u32")
     k(f"mov.u32 {kb2}, 0")
     mkl = k.label("m_kb")
@@ -888,7 +920,7 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
     col0 = k.reg("u32")
     k(f"mul.lo.u32 {col0}, {tn4}, {BN}")
     tbase = k.reg("u32")
-    k(f"mad.lo.u32 {tbase}, {a4}, {BN}, {tmem}")
+    k(f"mad.lo.u32 {tbase}, {a4}, {acc_stride}, {tmem}")
     k(f"add.u32 {tbase}, {tbase}, {lane_off}")
     row0 = k.reg("u32")
     k(f"mul.lo.u32 {row0}, {tm4}, {BM}")
@@ -906,6 +938,14 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
         k(f"tcgen05.ld.sync.aligned.32x32b.x{EPI_COLS}.b32 {{{', '.join(regs)}}}, [{tad}]")
         k("tcgen05.wait::ld.sync.aligned")
         special = _any_nonfinite(k, regs)
+        inb = None
+        if plan.partial_n:
+            # a chunk past N (an edge tile's overhang) is neither fixed up
+            # nor stored
+            cc0, inb = k.reg("u32"), k.reg("pred")
+            k(f"add.u32 {cc0}, {col0}, {c * EPI_COLS}")
+            k(f"setp.lt.u32 {inb}, {cc0}, {N}")
+            k(f"and.pred {special}, {special}, {inb}")
         # the buffer is free once the store that used it two chunks ago read it
         k(f"@{is_iss} cp.async.bulk.wait_group.read 1")
         k(f"bar.sync 1, {EPI_THREADS}")
@@ -922,11 +962,15 @@ def _emit_tc(k: Kernel, plan, A, B, C, tid, cta, ncta, BN, a_bytes, b_bytes, sta
         k(f"bar.sync 1, {EPI_THREADS}")
         cc = k.reg("u32")
         k(f"add.u32 {cc}, {col0}, {c * EPI_COLS}")
+        st_p = is_iss
+        if inb is not None:
+            st_p = k.reg("pred")
+            k(f"and.pred {st_p}, {is_iss}, {inb}")
         if plan.slices > 1:
-            k(f"@{is_iss} cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group "
+            k(f"@{st_p} cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group "
               f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
         else:
-            k(f"@{is_iss} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group "
+            k(f"@{st_p} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group "
               f"[{tmaps['c']}, {{{cc}, {row0}}}], [{sbuf}]")
         k(f"@{is_iss} cp.async.bulk.commit_group")
         k(f"add.u32 {ec}, {ec}, 1")

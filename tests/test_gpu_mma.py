@@ -156,3 +156,76 @@ def test_baseline_shapes_sampled(shape):
     rows = np.random.default_rng(2).choice(m, 64, replace=False)
     ok, rel = _bound_ok(got, a, b, rows)
     assert ok, rel
+
+
+@pytest.mark.parametrize("m,n,k,bn,forced", [(1024, 4160, 256, 256, None),
+                                             (512, 2496, 512, 256, None),
+                                             (1024, 8192, 256, 224, "224"),
+                                             (2048, 4096, 256, 160, "160")])
+def test_ragged_n_edge(m, n, k, bn, forced, monkeypatch):
+    """Tile widths that leave a ragged N edge (4160 = 16 x 256 + 64, 2496 =
+    9 x 256 + 192; forced widths 224 and 160 at 8192 and 4096): the edge
+    tile's B rows past N load as zeros and its C columns past N are not
+    stored."""
+    from ptxgen.runtime import PreparedKernel
+    if forced:
+        monkeypatch.setenv("EMMY_MATMUL_BN", forced)
+    else:
+        monkeypatch.delenv("EMMY_MATMUL_BN", raising=False)
+    spec = load_kernel_data(*irgen.matmul(m, n, k), f"rag{n}{bn}")
+    rng = np.random.default_rng(m + n + bn)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    pk = PreparedKernel(spec)
+    try:
+        assert pk.plan["tile"][1] == bn and n % bn
+        pk.upload({"x0": a, "x1": b})
+        pk.launch()
+        pk.check_errors()
+        got = pk.download()["matmul"]
+    finally:
+        pk.close()
+    rows = np.random.default_rng(7).choice(m, 64, replace=False)
+    ok, rel = _bound_ok(got, a, b, rows)
+    assert ok, rel
+    # every column of the last (ragged) tile, all rows of one row block
+    ref = a[:128].astype(np.float64) @ b[:, (n // bn) * bn:].astype(np.float64)
+    assert np.abs(got[:128, (n // bn) * bn:] - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+def test_ragged_n_edge_sliced(monkeypatch):
+    """The same ragged edge with K slices reduce-added into a cleared C (the
+    opt-in slicing): the overhanging chunks are not reduce-added either."""
+    monkeypatch.delenv("EMMY_MATMUL_BN", raising=False)
+    monkeypatch.setenv("EMMY_MATMUL_MAX_SLICE_K", "256")
+    m, n, k = 1024, 4160, 512
+    spec = load_kernel_data(*irgen.matmul(m, n, k), "ragsl")
+    rng = np.random.default_rng(8)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    rows = np.random.default_rng(9).choice(m, 64, replace=False)
+    ok, rel = _bound_ok(got, a, b, rows)
+    assert ok, rel
+
+
+def test_ragged_n_edge_infinite_operand(monkeypatch):
+    """An infinite A element at a ragged shape: its row's outputs are
+    recomputed in f32 (+-inf by the sign of B's element, NaN where that is
+    0), and the overhanging chunks of the edge tile, whose zero-filled B
+    makes inf * 0 = NaN there, are skipped rather than recomputed from B
+    columns past N."""
+    monkeypatch.delenv("EMMY_MATMUL_BN", raising=False)
+    m, n, k = 1024, 4160, 256
+    spec = load_kernel_data(*irgen.matmul(m, n, k), "raginf")
+    rng = np.random.default_rng(10)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    b[17, 5] = 0.0
+    a[900, 17] = np.inf
+    got = _run(spec, {"x0": a, "x1": b})["matmul"]
+    want = np.where(b[17] > 0, np.inf, np.where(b[17] < 0, -np.inf, np.nan)).astype(np.float32)
+    assert np.array_equal(got[900], want, equal_nan=True)
+    others = np.delete(np.arange(m), 900)[:: 97]
+    ok, rel = _bound_ok(got, a, b, others)
+    assert ok, rel

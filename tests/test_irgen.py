@@ -75,3 +75,38 @@ def test_splitk_overwrites_only_when_slices_grouped():
         spec = load_kernel_data(*irgen.matmul_splitk(m, n, k, slice_k=128), "sk")
         plan = json.loads(re.search(r"// @emmy-plan (\{.*\})", compile_kernel(spec)).group(1))
         assert (plan.get("overwrites") == ["matmul"]) == grouped, (m, n, k, plan.get("split_k"))
+
+
+def test_matmul_tile_width(monkeypatch):
+    """The C tile width: 256 or 128 where it divides N (every BASELINE shape
+    and its row shards); N itself for 160, 192, 224; 256 with a ragged edge
+    for longer N that are multiples of 32 only (such N used to fall to 64-
+    or 32-column tiles); the divisor rule otherwise."""
+    from ptxgen import tmpl_mma
+    monkeypatch.delenv("EMMY_MATMUL_BN", raising=False)
+    want = {(8192, 8192): 256, (16384, 4096): 256, (1024, 8192): 256, (2048, 4096): 256,
+            (4096, 4096): 256, (512, 512): 256, (256, 128): 128, (384, 192): 192,
+            (1024, 4160): 256, (512, 2496): 256, (512, 2400): 256, (256, 96): 32, (128, 64): 64}
+    for (m, n), bn in want.items():
+        assert tmpl_mma._choose_bn(m, n) == bn, (m, n)
+    monkeypatch.setenv("EMMY_MATMUL_BN", "224")
+    assert tmpl_mma._choose_bn(1024, 8192) == 224
+    monkeypatch.setenv("EMMY_MATMUL_BN", "100")            # not a choice: the rule
+    assert tmpl_mma._choose_bn(1024, 8192) == 256
+
+
+def test_matmul_ragged_edge_guards_stores(monkeypatch):
+    """With a ragged N edge the C stores (and the non-finite recompute) are
+    predicated on the chunk's first column being inside N; without one the
+    store path is unchanged."""
+    from ptxgen.emit import compile_kernel
+    from ptxgen.loader import load_kernel_data
+    monkeypatch.delenv("EMMY_MATMUL_BN", raising=False)
+    rag = compile_kernel(load_kernel_data(*irgen.matmul(1024, 4160, 256), "rag"))
+    even = compile_kernel(load_kernel_data(*irgen.matmul(8192, 8192, 256), "even"))
+    store = "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group"
+    assert sum(1 for ln in rag.splitlines() if store in ln) == 256 // 32
+    # each guarded store names its own predicate; unguarded ones the issuer's
+    preds_rag = {ln.split()[0] for ln in rag.splitlines() if store in ln}
+    preds_even = {ln.split()[0] for ln in even.splitlines() if store in ln}
+    assert len(preds_even) == 1 and len(preds_rag) == 256 // 32
