@@ -336,6 +336,16 @@ def record_attention(dt, rank, world, strong=True):
              else "bf16: max|err| <= 2e-2 max|ref| of float64 on sampled rows"))
 
 
+def live_durations(step_ms: float, alone_ms: dict) -> dict:
+    """Each kernel's duration over the timed region: the timed step (max
+    over ranks) times the kernel's share of the back-to-back launch times
+    measured alone -- the step itself when a record has one kernel.  The
+    back-to-back loop runs after the timed region, at whatever clock the
+    power cap then allows, so it gives the shares and not the durations."""
+    total = sum(alone_ms.values())
+    return {k: step_ms * v / total for k, v in alone_ms.items()}
+
+
 _SMALL = False
 # The jobs of a record never read what another job (or the previous launch
 # of the same job) writes, so kernels whose plans allow it start while the
@@ -694,13 +704,7 @@ def measure(name: str, args, dist: Dist, strong: bool, dev) -> dict:
     flops_step = dist.rdv.sum(sum(j.algo_flops for j in jobs))
     pk = peaks()
     dom = max(jobs, key=lambda j: per_kernel[j.key])
-    # the dominant kernel's duration over the timed region: the timed step
-    # (max over ranks) times the kernel's share of the back-to-back launch
-    # times above -- the step itself when the record has one kernel; the
-    # back-to-back loop runs after the timed region, at whatever clock the
-    # power cap then allows, so it gives the shares and not the duration
-    alone_total = sum(per_kernel.values())
-    live_ms = {k: ms * v / alone_total for k, v in per_kernel.items()}
+    live_ms = live_durations(ms, per_kernel)
     dom_ms = live_ms[dom.key]
     traffic = None
     tpath = ROOT / "profiles" / "traffic.json"

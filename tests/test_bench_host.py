@@ -95,3 +95,13 @@ def test_record_table_names_every_baseline_config():
                                   "matmul_rect", "matmul_splitk8", "attention_f32",
                                   "attention_bf16"}
     assert bench.ALIASES["matmul"] == ["matmul_square", "matmul_rect", "matmul_splitk8"]
+
+
+def test_live_durations_apportion_the_timed_step():
+    """The roofline's kernel durations: one kernel takes the whole timed
+    step; several share it in proportion to their back-to-back times alone
+    (which the power cap may stretch uniformly after the timed region)."""
+    assert bench.live_durations(3.6, {"attention_bf16": 3.85}) == {"attention_bf16": 3.6}
+    live = bench.live_durations(4.35, {"m.pre": 0.27, "m": 4.33})
+    assert abs(sum(live.values()) - 4.35) < 1e-12
+    assert abs(live["m"] / live["m.pre"] - 4.33 / 0.27) < 1e-9
