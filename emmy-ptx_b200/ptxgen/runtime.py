@@ -392,6 +392,7 @@ class PreparedKernel:
         self.geometry = geometry
         self.ws = 0
         self.bufs: dict[str, int] = {}
+        self._own: dict[str, int] = {}      # what this kernel allocated (close frees it)
         self.scalars: dict[str, object] = {}
         for name in spec.arg_order:
             a = spec.args[name]
@@ -405,7 +406,7 @@ class PreparedKernel:
                 v = a.value if a.value is not None else 0
                 self.scalars[name] = ct(float(v) if ct in (C.c_float, C.c_double) else int(v))
                 continue
-            self.bufs[name] = self.dev.alloc(a.nbytes)
+            self.bufs[name] = self._own[name] = self.dev.alloc(a.nbytes)
         for name in spec.arg_order:
             a = spec.args[name]
             if a.scalar:
@@ -435,6 +436,27 @@ class PreparedKernel:
             ptr, size = self.mod.global_ptr(f["sym"])
             self.dev.htod(ptr, np.array([int(f["value"])], dtype=np.uint32))
         self.dev.sync()
+
+    def bind(self, name: str, ptr: int) -> int:
+        """Read argument ``name`` from the device buffer at ``ptr`` -- another
+        kernel's copy of the same array, say, so that one host-to-device copy
+        feeds both -- instead of the buffer it points at now; tensor maps over
+        that argument are refilled.  Returns the previous address.  The
+        caller keeps ``ptr`` alive while this kernel uses it; ``close`` frees
+        only the buffers this kernel allocated, whatever is bound."""
+        a = self.spec.args[name]
+        if a.scalar:
+            raise EmmyError(f"bind: {name} is a by-value argument")
+        old = self.bufs[name]
+        self.bufs[name] = int(ptr)
+        if self.geometry != "meta":
+            for t in self.plan.get("tmaps", []):
+                if t["buf"] == name:
+                    self.mod.fill_tmap(t["sym"], int(ptr) + int(t.get("offset", 0)),
+                                       t["dtype"], t["dims"], t["strides"], t["box"],
+                                       t["swizzle"])
+            self.dev.sync()
+        return old
 
     def attach_peers(self, inbox) -> None:
         """Join a multi-GPU full reduction: the kernel's cross-GPU exchange
@@ -568,9 +590,10 @@ class PreparedKernel:
 
     def close(self) -> None:
         self.detach_peers()
-        for p in self.bufs.values():
+        for p in self._own.values():
             self.dev.free(p)
         self.bufs = {}
+        self._own = {}
         if self.ws:
             self.dev.free(self.ws)
             self.ws = 0

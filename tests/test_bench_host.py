@@ -105,3 +105,35 @@ def test_live_durations_apportion_the_timed_step():
     live = bench.live_durations(4.35, {"m.pre": 0.27, "m": 4.33})
     assert abs(sum(live.values()) - 4.35) < 1e-12
     assert abs(live["m"] / live["m.pre"] - 4.33 / 0.27) < 1e-9
+
+
+def test_e2e_copies_each_shared_input_once():
+    """The end-to-end step copies every distinct host array once: a job
+    reading an array an earlier job takes is bound to that job's device
+    copy and bound back afterwards; an argument a kernel also writes is
+    never shared."""
+    from types import SimpleNamespace as NS
+
+    class PK:
+        def __init__(self, bufs):
+            self.bufs = dict(bufs)
+
+        def bind(self, name, ptr):
+            old, self.bufs[name] = self.bufs[name], ptr
+            return old
+
+    def job(key, bufs, inputs, outs=()):
+        args = {n: NS(output=n in outs) for n in bufs}
+        return NS(key=key, pk=PK(bufs), inputs=inputs, spec=NS(args=args))
+
+    x, xr = np.zeros(4), np.ones(4)
+    s = job("sum", {"x": 100}, {"x": x})
+    m = job("mean", {"x": 200}, {"x": x})
+    r = job("row_sum", {"x": 300}, {"x": xr})
+    w = job("inplace", {"x": 400}, {"x": x}, outs=("x",))
+    copies, rebound = bench.e2e_copy_plan([s, m, r, w])
+    assert [(c[0].key, c[1]) for c in copies] == [("sum", "x"), ("row_sum", "x"), ("inplace", "x")]
+    assert m.pk.bufs["x"] == 100 and [(j.key, n, own) for j, n, own in rebound] == [("mean", "x", 200)]
+    for j, n, own in rebound:
+        j.pk.bind(n, own)
+    assert m.pk.bufs["x"] == 200

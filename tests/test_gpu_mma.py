@@ -229,3 +229,32 @@ def test_ragged_n_edge_infinite_operand(monkeypatch):
     others = np.delete(np.arange(m), 900)[:: 97]
     ok, rel = _bound_ok(got, a, b, others)
     assert ok, rel
+
+
+def test_bind_reads_another_kernels_buffer():
+    """``PreparedKernel.bind``: a matmul whose A argument is bound to another
+    kernel's A buffer reads that buffer -- its tensor maps follow -- and
+    closing both kernels frees each buffer once."""
+    from ptxgen.runtime import PreparedKernel
+    m, n, k = 256, 512, 256
+    spec = load_kernel_data(*irgen.matmul(m, n, k), "bind")
+    rng = np.random.default_rng(11)
+    a1, a2 = ((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32) for _ in range(2))
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    p1, p2 = PreparedKernel(spec), PreparedKernel(spec)
+    try:
+        p1.upload({"x0": a1, "x1": b})
+        p2.upload({"x0": a2, "x1": b})
+        own = p2.bind("x0", p1.bufs["x0"])
+        p2.launch()
+        p2.check_errors()
+        ok, rel = _bound_ok(p2.download()["matmul"], a1, b)
+        assert ok, rel
+        p2.bind("x0", own)
+        p2.launch()
+        p2.check_errors()
+        ok, rel = _bound_ok(p2.download()["matmul"], a2, b)
+        assert ok, rel
+    finally:
+        p2.close()
+        p1.close()
