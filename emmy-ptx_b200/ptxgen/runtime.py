@@ -442,8 +442,9 @@ class PreparedKernel:
         kernel's copy of the same array, say, so that one host-to-device copy
         feeds both -- instead of the buffer it points at now; tensor maps over
         that argument are refilled.  Returns the previous address.  The
-        caller keeps ``ptr`` alive while this kernel uses it; ``close`` frees
-        only the buffers this kernel allocated, whatever is bound."""
+        caller keeps ``ptr`` alive while this kernel uses it; ``upload`` to
+        ``name`` writes into it; ``close`` frees only the buffers this kernel
+        allocated, whatever is bound."""
         a = self.spec.args[name]
         if a.scalar:
             raise EmmyError(f"bind: {name} is a by-value argument")
